@@ -1,0 +1,62 @@
+/*
+ * gguf_cuda.h - the fused dequant-matvec of the reference, on the device.
+ *
+ * GGUFWeight has the layout of the reference's include/gguf_model.h:36-45
+ * with one difference of meaning: `data` is a DEVICE pointer to the packed
+ * rows (bytes exactly as stored in the GGUF file). Row r starts at
+ * data + r * row_bytes.
+ *
+ * GGML type ids: 0 F32, 1 F16, 2 Q4_0, 8 Q8_0, 12 Q4_K, 13 Q5_K, 14 Q6_K.
+ * All calls are asynchronous on `stream` (a cudaStream_t, NULL for the
+ * default stream); x, out and data are device pointers. Return 1 on
+ * success, 0 on bad arguments or an unsupported type (nothing launched).
+ */
+#ifndef GGUF_CUDA_H
+#define GGUF_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+    const char *name;     /* optional label */
+    const void *data;     /* device pointer to row 0 */
+    uint32_t type;        /* GGML type id */
+    uint64_t cols;        /* ne0: input length */
+    uint64_t rows;        /* ne1: output length */
+    uint64_t row_bytes;   /* (cols / block_weights) * block_bytes */
+    uint64_t byte_size;   /* rows * row_bytes */
+} GGUFWeight;
+
+/*
+ * out[r] = sum_c W[r][c] * x[c] for r < rows, read from the packed blocks
+ * with no FP32 copy of W. Replaces gguf_matvec, reference
+ * include/gguf_model.h:141-145 / src/gguf_model.c:693-771 (same argument
+ * meaning; out must not alias x). Agrees with the reference's fast kernels
+ * to float32 rounding (relative L2 ~1e-7).
+ */
+int gguf_cuda_matvec(const GGUFWeight *weight, const float *x, float *out, void *stream);
+
+/*
+ * Decode rows [row0, row0 + nrows) to FP32 into out (nrows * cols floats),
+ * bit-identical to the reference's gguf_weight_dequantize_row
+ * (include/gguf_model.h:112-116, src/gguf_model.c:314-359) and block
+ * decoders (src/gguf_quant.c:92-407).
+ */
+int gguf_cuda_dequantize_rows(const GGUFWeight *weight, uint64_t row0, uint64_t nrows,
+                              float *out, void *stream);
+
+/*
+ * out[h] = FP32 value of half-precision bit pattern h for all 65536 h,
+ * bit-identical to gguf_fp16_to_fp32 (src/gguf_quant.c:6-59), NaN
+ * payloads included.
+ */
+int gguf_cuda_fp16_table(float *out65536, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,69 @@
+/*
+ * pk_dev.h - the internal C ABI between the C11 host engine (engine.c) and
+ * the CUDA side (pk_device.cu). Plain C types only.
+ */
+#ifndef PK_DEV_H
+#define PK_DEV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* One weight tensor inside the device weight arena. */
+typedef struct {
+    uint32_t type;      /* GGML type id */
+    uint64_t rows;      /* ne1 (1 for vectors) */
+    uint64_t cols;      /* ne0 */
+    uint64_t row_bytes;
+    uint64_t offset;    /* byte offset of row 0 inside the arena */
+} PkdTensor;
+
+typedef struct {
+    int dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, seq_len, rope_dim;
+    float rms_eps;
+    float att_scale;            /* 1/sqrtf(head_size), computed as the reference does */
+    PkdTensor embd, output;
+    const PkdTensor *wq, *wk, *wv, *wo, *gate, *up, *down; /* n_layers each */
+    const PkdTensor *attn_norm, *ffn_norm;                  /* n_layers each, decoded on the device */
+    PkdTensor output_norm;
+    const float *rope_cs;       /* host: seq_len * rope_dim floats, (cos, sin) pairs */
+} PkdModel;
+
+typedef struct PkdCtx PkdCtx;
+
+/* Device context for one handle on `device`. NULL + message on failure. */
+PkdCtx *pkd_create(int device, uint64_t arena_bytes, char *err, size_t cap);
+void pkd_destroy(PkdCtx *ctx);
+
+/* Copy `bytes` host bytes to arena offset `offset` (through pinned staging). */
+int pkd_upload(PkdCtx *ctx, uint64_t offset, const void *src, uint64_t bytes, char *err, size_t cap);
+
+/* Allocate run state (KV cache, activations), upload norms and the RoPE
+ * table, and capture the decode-step graph. */
+int pkd_build(PkdCtx *ctx, const PkdModel *m, char *err, size_t cap);
+
+/* One decode step. Returns host (pinned) logits owned by ctx, or NULL on a
+ * device error (ctx then stays failed). */
+float *pkd_forward(PkdCtx *ctx, int token, int pos);
+
+/* One decode step returning the greedy token (device argmax, lowest index
+ * on ties); -1 if a logit is not finite; -2 on a device error. */
+int pkd_forward_greedy(PkdCtx *ctx, int token, int pos);
+
+/* n greedy steps fed back on the device (token, pos), (argmax, pos+1), ...
+ * without host round trips; out receives the n generated tokens (-1 where
+ * a logit was not finite) and device_ms the CUDA-event time of the n graph
+ * replays. Returns 1 on success. */
+int pkd_generate_greedy(PkdCtx *ctx, int token, int pos, int n, int *out, float *device_ms);
+
+/* Last device error message ("" if none). */
+const char *pkd_error(const PkdCtx *ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

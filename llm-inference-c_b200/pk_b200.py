@@ -1,0 +1,218 @@
+"""ctypes binding of libpocketllm_b200.so (engine.h, engine_ext.h, gguf_cuda.h).
+
+This is how Python callers (the tests, bench.py) reach the C ABI, in the
+same style as the reference's ctypes package (python/pocketllm/__init__.py).
+The library is required: there is no CPU fallback, and loading fails loudly
+when the built .so is missing.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libpocketllm_b200.so")
+
+F32, F16, Q4_0, Q8_0, Q4_K, Q5_K, Q6_K = 0, 1, 2, 8, 12, 13, 14
+BLOCK = {F32: (1, 4), F16: (1, 2), Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144),
+         Q5_K: (256, 176), Q6_K: (256, 210)}
+
+_P = ctypes.c_void_p
+
+# Every symbol the public headers declare (include/engine.h, engine_ext.h,
+# gguf_cuda.h, tokenizer.h).
+EXPORTS = [
+    "engine_open", "engine_close", "engine_forward", "engine_config", "engine_file_context",
+    "engine_format", "engine_tokenizer", "engine_kv_cache_bytes", "engine_description",
+    "engine_is_stop_token", "engine_open_device", "engine_forward_greedy", "engine_last_error",
+    "engine_weight_bytes", "engine_generate_greedy", "gguf_cuda_matvec", "gguf_cuda_dequantize_rows", "gguf_cuda_fp16_table",
+    "tokenizer_free",
+]
+
+
+def row_bytes(qtype, cols):
+    bw, bb = BLOCK[qtype]
+    assert cols % bw == 0
+    return cols // bw * bb
+
+
+def build():
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+class Config(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("dim", "hidden_dim", "n_layers", "n_heads",
+                                             "n_kv_heads", "vocab_size", "seq_len", "rope_dim")] + \
+               [(n, ctypes.c_float) for n in ("rope_freq_base", "rms_norm_eps", "rope_scale")]
+
+
+class LLMOptions(ctypes.Structure):
+    _fields_ = [("model_path", ctypes.c_char_p), ("tokenizer_path", ctypes.c_char_p),
+                ("max_context", ctypes.c_int)]
+
+
+class TokenizerIndex(ctypes.Structure):
+    _fields_ = [("text", ctypes.c_char_p), ("id", ctypes.c_int)]
+
+
+class Tokenizer(ctypes.Structure):
+    _fields_ = [("vocab", ctypes.POINTER(ctypes.c_char_p)), ("scores", ctypes.POINTER(ctypes.c_float)),
+                ("sorted_vocab", ctypes.POINTER(TokenizerIndex)), ("vocab_size", ctypes.c_size_t),
+                ("max_token_length", ctypes.c_size_t), ("byte_pieces", ctypes.c_ubyte * 512),
+                ("bos_id", ctypes.c_int), ("eos_id", ctypes.c_int), ("byte_ids", ctypes.c_int * 256),
+                ("special_ids", ctypes.POINTER(ctypes.c_int)), ("n_special", ctypes.c_size_t),
+                ("scores_reconstructed", ctypes.c_int)]
+
+
+class GGUFWeight(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("data", _P), ("type", ctypes.c_uint32),
+                ("cols", ctypes.c_uint64), ("rows", ctypes.c_uint64),
+                ("row_bytes", ctypes.c_uint64), ("byte_size", ctypes.c_uint64)]
+
+
+_lib = None
+
+
+def lib(path=LIB_PATH):
+    """Load the engine library (RuntimeError if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise RuntimeError(f"{path} is missing: run `make -C {HERE}` (the CUDA path has no fallback)")
+    L = ctypes.CDLL(path)
+    L.engine_open.restype = _P
+    L.engine_open.argtypes = [ctypes.POINTER(LLMOptions), ctypes.c_char_p, ctypes.c_size_t]
+    L.engine_open_device.restype = _P
+    L.engine_open_device.argtypes = [ctypes.POINTER(LLMOptions), ctypes.c_int, ctypes.c_char_p,
+                                     ctypes.c_size_t]
+    L.engine_close.argtypes = [_P]
+    L.engine_forward.restype = ctypes.POINTER(ctypes.c_float)
+    L.engine_forward.argtypes = [_P, ctypes.c_int, ctypes.c_int]
+    L.engine_forward_greedy.restype = ctypes.c_int
+    L.engine_forward_greedy.argtypes = [_P, ctypes.c_int, ctypes.c_int]
+    L.engine_config.restype = ctypes.POINTER(Config)
+    L.engine_config.argtypes = [_P]
+    L.engine_file_context.restype = ctypes.c_int
+    L.engine_file_context.argtypes = [_P]
+    L.engine_format.restype = ctypes.c_int
+    L.engine_format.argtypes = [_P]
+    L.engine_tokenizer.restype = ctypes.POINTER(Tokenizer)
+    L.engine_tokenizer.argtypes = [_P]
+    L.engine_kv_cache_bytes.restype = ctypes.c_size_t
+    L.engine_kv_cache_bytes.argtypes = [_P]
+    L.engine_description.restype = ctypes.c_char_p
+    L.engine_description.argtypes = [_P]
+    L.engine_is_stop_token.restype = ctypes.c_int
+    L.engine_is_stop_token.argtypes = [_P, ctypes.c_int]
+    L.engine_last_error.restype = ctypes.c_char_p
+    L.engine_last_error.argtypes = [_P]
+    L.engine_weight_bytes.restype = ctypes.c_size_t
+    L.engine_weight_bytes.argtypes = [_P]
+    L.engine_generate_greedy.restype = ctypes.c_int
+    L.engine_generate_greedy.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P,
+                                         ctypes.POINTER(ctypes.c_float)]
+    L.gguf_cuda_matvec.restype = ctypes.c_int
+    L.gguf_cuda_matvec.argtypes = [ctypes.POINTER(GGUFWeight), _P, _P, _P]
+    L.gguf_cuda_dequantize_rows.restype = ctypes.c_int
+    L.gguf_cuda_dequantize_rows.argtypes = [ctypes.POINTER(GGUFWeight), ctypes.c_uint64,
+                                            ctypes.c_uint64, _P, _P]
+    L.gguf_cuda_fp16_table.restype = ctypes.c_int
+    L.gguf_cuda_fp16_table.argtypes = [_P, _P]
+    _lib = L
+    return L
+
+
+class Engine:
+    """One engine_open() handle."""
+
+    def __init__(self, path, max_context=0, device=None, tokenizer_path=None):
+        L = lib()
+        self._path = path.encode()
+        self._tok = tokenizer_path.encode() if tokenizer_path else None
+        opts = LLMOptions(self._path, self._tok, max_context)
+        err = ctypes.create_string_buffer(512)
+        if device is None:
+            self.h = L.engine_open(ctypes.byref(opts), err, 512)
+        else:
+            self.h = L.engine_open_device(ctypes.byref(opts), device, err, 512)
+        if not self.h:
+            raise RuntimeError("engine_open failed: " + err.value.decode())
+        c = L.engine_config(self.h).contents
+        self.config = {n: getattr(c, n) for n, _ in Config._fields_}
+        self.vocab_size = c.vocab_size
+        self.seq_len = c.seq_len
+
+    def forward(self, token, pos):
+        """Logits as a fresh numpy array, or None when engine_forward returns NULL."""
+        p = lib().engine_forward(self.h, token, pos)
+        if not p:
+            return None
+        return np.ctypeslib.as_array(p, shape=(self.vocab_size,)).copy()
+
+    def forward_raw(self, token, pos):
+        return lib().engine_forward(self.h, token, pos)
+
+    def forward_greedy(self, token, pos):
+        return lib().engine_forward_greedy(self.h, token, pos)
+
+    def generate_greedy(self, token, pos, n):
+        """n device-side greedy steps: (tokens, device milliseconds)."""
+        out = np.zeros(max(n, 1), dtype=np.int32)
+        ms = ctypes.c_float(0.0)
+        if lib().engine_generate_greedy(self.h, token, pos, n, out.ctypes.data, ctypes.byref(ms)) != 1:
+            raise RuntimeError("engine_generate_greedy failed: " + self.last_error())
+        return out[:n], ms.value
+
+    def description(self):
+        return lib().engine_description(self.h).decode()
+
+    def kv_cache_bytes(self):
+        return lib().engine_kv_cache_bytes(self.h)
+
+    def weight_bytes(self):
+        return lib().engine_weight_bytes(self.h)
+
+    def file_context(self):
+        return lib().engine_file_context(self.h)
+
+    def format(self):
+        return lib().engine_format(self.h)
+
+    def tokenizer(self):
+        return lib().engine_tokenizer(self.h).contents
+
+    def is_stop(self, token):
+        return lib().engine_is_stop_token(self.h, token)
+
+    def last_error(self):
+        return lib().engine_last_error(self.h).decode()
+
+    def close(self):
+        if self.h:
+            lib().engine_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def make_weight(dev_ptr, qtype, rows, cols):
+    rb = row_bytes(qtype, cols)
+    return GGUFWeight(b"w", dev_ptr, qtype, cols, rows, rb, rb * rows)
+
+
+def matvec(weight, x_ptr, y_ptr, stream=0):
+    return lib().gguf_cuda_matvec(ctypes.byref(weight), x_ptr, y_ptr, stream)
+
+
+def dequantize_rows(weight, row0, nrows, out_ptr, stream=0):
+    return lib().gguf_cuda_dequantize_rows(ctypes.byref(weight), row0, nrows, out_ptr, stream)
+
+
+def fp16_table(out_ptr, stream=0):
+    return lib().gguf_cuda_fp16_table(out_ptr, stream)
