@@ -189,8 +189,14 @@ def run_matvec_sweep(args):
     hbm, _ = peaks()
     shapes = [(2048, 2048), (256, 2048), (5632, 2048), (2048, 5632), (32000, 2048), (4096, 4096),
               (14336, 4096), (128256, 4096)]
+    only = None
+    if args.only:  # e.g. "Q4_K:128256x4096"
+        t, shp = args.only.split(":")
+        only = (t, tuple(int(v) for v in shp.split("x")))
     for name, qt in (("Q4_0", 2), ("Q8_0", 8), ("Q4_K", 12), ("Q5_K", 13), ("Q6_K", 14)):
         for rows, cols in shapes:
+            if only is not None and (name, (rows, cols)) != only:
+                continue
             rb = pk_b200.row_bytes(qt, cols)
             nbytes = rows * rb
             copies = max(1, min(8, (512 << 20) // nbytes))  # rotate > 2x L2 of weight copies
@@ -226,6 +232,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="tinyllama", choices=list(WORKLOADS) + ["matvec"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", default=None, help="matvec workload: one TYPE:ROWSxCOLS case")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

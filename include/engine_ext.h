@@ -34,6 +34,14 @@ int engine_forward_greedy(LLMModel *model, int token, int pos);
 int engine_generate_greedy(LLMModel *model, int token, int pos, int n,
                            int *out_tokens, float *device_ms);
 
+/* Tracing: when the handle was opened with POCKET_CUDA_TRACE=1, copies the
+ * device timestamps (ns, %globaltimer, taken by CTA 0) of the last decode
+ * step into out and returns how many were written (0 when tracing is off):
+ * the step's start, then for each of its 5 * n_layers + 1 phases the time
+ * after staging the input vector, after the phase's work and after the
+ * grid barrier that ends it. */
+int engine_trace(LLMModel *model, unsigned long long *out, int cap);
+
 /* Message of the last device error of this handle ("" if none). */
 const char *engine_last_error(const LLMModel *model);
 

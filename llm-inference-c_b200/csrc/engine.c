@@ -753,6 +753,11 @@ int engine_generate_greedy(LLMModel *m, int token, int pos, int n, int *out_toke
     return 1;
 }
 
+int engine_trace(LLMModel *m, unsigned long long *out, int cap)
+{
+    return m == NULL ? 0 : pkd_trace(m->dev, out, cap);
+}
+
 const char *engine_last_error(const LLMModel *m)
 {
     return m == NULL ? "" : m->last_error;

@@ -6,13 +6,14 @@
 //     uses the explicitly rounded intrinsics (__fmul_rn, __fsub_rn) so nvcc
 //     cannot contract them into FMAs; the reference is compiled with
 //     -std=c11, i.e. -ffp-contract=off.
-//   * unit_dot<T>(): the fused dequant-dot of one 64-column "unit" of a row
-//     with 64 activations held in registers. This is the hot loop of every
-//     matvec. It follows the reference's algebra (src/gguf_model.c:445-691):
-//     per 32- or 16-weight group, sum q*x first and apply the group scale
-//     (and, for Q4_K/Q5_K, subtract dmin*m*sum(x)) once per group. The sums
-//     use FMA accumulation instead of the reference's pairwise trees, so
-//     results agree to float32 rounding (~1e-7 relative), not bit for bit.
+//   * unit_*(): the fused dequant-dot of one 64-column "unit" of a row with
+//     the unit's activations held in registers in integer form (XUnit). This
+//     is the hot loop of every matvec. It follows the reference's algebra
+//     (src/gguf_model.c:445-691): per 32- or 16-weight group, sum q*x first
+//     and apply the group scale (and, for Q4_K/Q5_K, subtract
+//     dmin*m*sum(x)) once per group. The group sums are exact integer dp4a
+//     sums over a 23-bit fixed-point copy of x, so results agree with the
+//     reference's float32 kernels to ~1e-7 relative, not bit for bit.
 //
 // Units (64 consecutive columns each, so activation slices are shared by
 // every format):
@@ -22,6 +23,7 @@
 //   Q4_0 / Q8_0 : blocks 2u and 2u+1 (the second may be absent)
 //   F32 / F16   : columns 64u .. 64u+63 (guarded at the row end)
 #pragma once
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 namespace pk {
@@ -197,15 +199,111 @@ __device__ __forceinline__ float decode_col(int t, const uint8_t *row, int c)
 // Fused dequant-dot of one 64-column unit                            //
 // ------------------------------------------------------------------ //
 
-// 2^23 + n as a float for a small integer n, then minus 2^23: an exact
-// int->float conversion in two cheap ALU ops (avoids the slow I2F path).
-__device__ __forceinline__ float u2f_small(uint32_t n)
+// ------------------------------------------------------------------ //
+// Integer form of the activations                                    //
+// ------------------------------------------------------------------ //
+//
+// Before a matvec every 32-column group g of x is written as
+//     x_i = s_g * (d0_i + 2^8 d1_i + 2^16 d2_i),   s_g = 2^(E_g - 22)
+// with E_g the binary exponent of max|x_g| and d0..d2 signed bytes: a 23-bit
+// fixed-point copy of x (relative error <= 2^-23 of the group maximum). The
+// dot of a group with integer quants q is then three exact int32 dp4a sums,
+// one per digit plane, combined in float once per group:
+//     sum_i q_i x_i = s_g * (A0 + 2^8 A1 + 2^16 A2),  A_p = sum_i q_i dp_i.
+// One dp4a does four multiply-adds, so a weight costs ~3/4 dp4a plus its
+// share of the nibble unpack, instead of an int->float conversion and an FMA.
+// The group scales of the formats are applied afterwards exactly as the
+// reference's fast kernels do (src/gguf_model.c:445-691).
+
+// Shared-memory layout per 64-column unit u (two groups 2u, 2u+1):
+//   digits : 208 bytes at u*208: [group][plane][32 bytes] + 16 pad
+//   info   : 80 bytes at u*80:   per group {scale, sum(x), dsum[half][plane]}
+//            (8 words each) + 16 pad. dsum are the digit sums of each
+//            16-column half, used to apply q - 32 / q - 8 offsets.
+constexpr int XQ_UNIT_BYTES = 208;
+constexpr int XG_UNIT_WORDS = 20;
+
+struct XUnit {
+    uint32_t d[2][3][8];  // digit words: bytes of columns 4w..4w+3
+    float scale[2];
+    float sum[2];
+    int dsum[2][2][3];    // [group][half][plane]
+};
+
+__device__ __forceinline__ void load_xunit(const uint8_t *xq, const float *xg, int u, XUnit &x)
 {
-    return __uint_as_float(0x4B000000u | n) - 8388608.0f;
+    const uint4 *q = reinterpret_cast<const uint4 *>(xq + u * XQ_UNIT_BYTES);
+    uint32_t *dst = &x.d[0][0][0];
+#pragma unroll
+    for (int i = 0; i < 12; i++) {
+        const uint4 t = q[i];
+        dst[4 * i] = t.x;
+        dst[4 * i + 1] = t.y;
+        dst[4 * i + 2] = t.z;
+        dst[4 * i + 3] = t.w;
+    }
+    const float4 *gp = reinterpret_cast<const float4 *>(xg + u * XG_UNIT_WORDS);
+#pragma unroll
+    for (int g = 0; g < 2; g++) {
+        const float4 a = gp[2 * g], b = gp[2 * g + 1];
+        x.scale[g] = a.x;
+        x.sum[g] = a.y;
+        x.dsum[g][0][0] = __float_as_int(a.z);
+        x.dsum[g][0][1] = __float_as_int(a.w);
+        x.dsum[g][0][2] = __float_as_int(b.x);
+        x.dsum[g][1][0] = __float_as_int(b.y);
+        x.dsum[g][1][1] = __float_as_int(b.z);
+        x.dsum[g][1][2] = __float_as_int(b.w);
+    }
 }
 
-// Four consecutive 32-bit words starting at a 2-byte-aligned shared
-// address (rows of Q6_K / Q4_0 / Q8_0 are not 4-byte aligned in general).
+// Four unsigned bytes of a times four signed bytes of b, plus c.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c)
+{
+    int r;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+// Four signed bytes of a times four signed bytes of b, plus c.
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c)
+{
+    int r;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+__device__ __forceinline__ float planes(int a0, int a1, int a2)
+{
+    // a0 + 2^8 a1 is exact in int32 (|a1| < 2^23); two conversions, one FMA.
+    return fmaf((float)a2, 65536.0f, (float)(a0 + (a1 << 8)));
+}
+
+// fp16 -> fp32 by the hardware conversion: exact for every finite value,
+// which is all a matvec needs (a NaN scale gives a NaN either way).
+__device__ __forceinline__ float hf(uint32_t bits16)
+{
+    return __half2float(__ushort_as_half((unsigned short)bits16));
+}
+
+// The two 6-bit (scale, min) pairs of sub-blocks 2j and 2j+1 of a Q4_K /
+// Q5_K block, from the scale bytes held in three words s0 = bytes 0..3,
+// s1 = 4..7, s2 = 8..11 (src/gguf_quant.c:65-90): pairs come out packed as
+// two bytes (sub-block 2j in the low byte).
+__device__ __forceinline__ void scale_min_pair(uint32_t s0, uint32_t s1, uint32_t s2, int j, uint32_t &sc,
+                                               uint32_t &mn)
+{
+    const int sh = 16 * (j & 1);
+    const uint32_t a = (s0 >> sh) & 0xFFFFu, b = (s1 >> sh) & 0xFFFFu, c = (s2 >> sh) & 0xFFFFu;
+    const uint32_t sc_lo = a & 0x3F3Fu, mn_lo = b & 0x3F3Fu;
+    const uint32_t sc_hi = (c & 0x0F0Fu) | (((a >> 6) & 0x0303u) << 4);
+    const uint32_t mn_hi = ((c >> 4) & 0x0F0Fu) | (((b >> 6) & 0x0303u) << 4);
+    sc = j < 2 ? sc_lo : sc_hi;
+    mn = j < 2 ? mn_lo : mn_hi;
+}
+
+// NW consecutive 32-bit words starting at a 2-byte-aligned shared address
+// (rows of Q6_K / Q4_0 / Q8_0 are not 4-byte aligned in general).
 template <int NW>
 __device__ __forceinline__ void ld_words_a2(const uint8_t *p, uint32_t *w)
 {
@@ -221,10 +319,15 @@ __device__ __forceinline__ void ld_words_a2(const uint8_t *p, uint32_t *w)
     }
 }
 
-// Q4_K unit: d*sc*sum(q*x) - dmin*m*sum(x) for sub-blocks 2j and 2j+1.
-// `row` is 16-byte aligned (Q4_K rows are multiples of 144 = 9*16 bytes).
-__device__ __forceinline__ float unit_q4k(const uint8_t *row, int u, const float *xr, float xs_lo,
-                                          float xs_hi)
+// ------------------------------------------------------------------ //
+// Fused dequant-dot of one 64-column unit                            //
+// ------------------------------------------------------------------ //
+
+// Q4_K unit: d*sc*sum(q*x) - dmin*m*sum(x) for sub-blocks 2j and 2j+1
+// (src/gguf_model.c:457-507). `row` is 16-byte aligned (144 = 9*16). High
+// nibbles enter dp4a unshifted (16 q), and the 1/16 folds into the float
+// combine, exactly.
+__device__ __forceinline__ float unit_q4k(const uint8_t *row, int u, const XUnit &x)
 {
     const uint8_t *blk = row + (u >> 2) * 144;
     const int j = u & 3;
@@ -232,26 +335,28 @@ __device__ __forceinline__ float unit_q4k(const uint8_t *row, int u, const float
     const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * j);
     const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * j);
     const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    float slo = 0.0f, shi = 0.0f;
+    int A[2][3] = {{0, 0, 0}, {0, 0, 0}};
 #pragma unroll
     for (int k = 0; k < 8; k++) {
+        const uint32_t lo = w[k] & 0x0F0F0F0Fu, hi16 = w[k] & 0xF0F0F0F0u;
 #pragma unroll
-        for (int b = 0; b < 4; b++) {
-            slo = fmaf(u2f_small((w[k] >> (8 * b)) & 15u), xr[4 * k + b], slo);
-            shi = fmaf(u2f_small((w[k] >> (8 * b + 4)) & 15u), xr[32 + 4 * k + b], shi);
+        for (int p = 0; p < 3; p++) {
+            A[0][p] = dp4a_us(lo, x.d[0][p][k], A[0][p]);
+            A[1][p] = dp4a_us(hi16, x.d[1][p][k], A[1][p]);
         }
     }
-    const float d = h2f(hdr.x & 0xFFFFu), dmin = h2f(hdr.x >> 16);
-    uint32_t s0, m0, s1, m1;
-    scale_min_w(hdr.y, hdr.z, hdr.w, 2 * j, s0, m0);
-    scale_min_w(hdr.y, hdr.z, hdr.w, 2 * j + 1, s1, m1);
-    return (d * (float)s0) * slo - (dmin * (float)m0) * xs_lo + (d * (float)s1) * shi -
-           (dmin * (float)m1) * xs_hi;
+    uint32_t sc, mn;
+    scale_min_pair(hdr.y, hdr.z, hdr.w, j, sc, mn);
+    const float d = hf(hdr.x & 0xFFFFu), dmin = hf(hdr.x >> 16);
+    const float s0v = x.scale[0] * planes(A[0][0], A[0][1], A[0][2]);
+    const float s1v = (x.scale[1] * 0.0625f) * planes(A[1][0], A[1][1], A[1][2]);
+    return (d * (float)(sc & 255u)) * s0v - (dmin * (float)(mn & 255u)) * x.sum[0] +
+           (d * (float)(sc >> 8)) * s1v - (dmin * (float)(mn >> 8)) * x.sum[1];
 }
 
-// Q5_K unit: as Q4_K with the fifth bit from qh (bits 2j, 2j+1).
-__device__ __forceinline__ float unit_q5k(const uint8_t *row, int u, const float *xr, float xs_lo,
-                                          float xs_hi)
+// Q5_K unit: as Q4_K with the fifth bit from qh (bits 2j, 2j+1),
+// src/gguf_model.c:574-626.
+__device__ __forceinline__ float unit_q5k(const uint8_t *row, int u, const XUnit &x)
 {
     const uint8_t *blk = row + (u >> 2) * 176;
     const int j = u & 3;
@@ -261,127 +366,136 @@ __device__ __forceinline__ float unit_q5k(const uint8_t *row, int u, const float
     const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 48 + 32 * j);
     const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 64 + 32 * j);
     const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    // Move bit 2j of every qh byte to bit 4 and bit 2j+1 to bit 4 of a
-    // second word, so each lands where the fifth quant bit belongs.
     const uint32_t h[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
-    float slo = 0.0f, shi = 0.0f;
+    int A[2][3] = {{0, 0, 0}, {0, 0, 0}};
 #pragma unroll
     for (int k = 0; k < 8; k++) {
-        const uint32_t hlo = ((h[k] >> (2 * j)) & 0x01010101u) << 4;
-        const uint32_t hhi = ((h[k] >> (2 * j + 1)) & 0x01010101u) << 4;
-        const uint32_t qlo = (w[k] & 0x0F0F0F0Fu) | hlo;
-        const uint32_t qhi = ((w[k] >> 4) & 0x0F0F0F0Fu) | hhi;
+        const uint32_t lo = (w[k] & 0x0F0F0F0Fu) | (((h[k] >> (2 * j)) & 0x01010101u) << 4);
+        const uint32_t hi = ((w[k] >> 4) & 0x0F0F0F0Fu) | (((h[k] >> (2 * j + 1)) & 0x01010101u) << 4);
 #pragma unroll
-        for (int b = 0; b < 4; b++) {
-            slo = fmaf(u2f_small((qlo >> (8 * b)) & 31u), xr[4 * k + b], slo);
-            shi = fmaf(u2f_small((qhi >> (8 * b)) & 31u), xr[32 + 4 * k + b], shi);
+        for (int p = 0; p < 3; p++) {
+            A[0][p] = dp4a_us(lo, x.d[0][p][k], A[0][p]);
+            A[1][p] = dp4a_us(hi, x.d[1][p][k], A[1][p]);
         }
     }
-    const float d = h2f(hdr.x & 0xFFFFu), dmin = h2f(hdr.x >> 16);
-    uint32_t s0, m0, s1, m1;
-    scale_min_w(hdr.y, hdr.z, hdr.w, 2 * j, s0, m0);
-    scale_min_w(hdr.y, hdr.z, hdr.w, 2 * j + 1, s1, m1);
-    return (d * (float)s0) * slo - (dmin * (float)m0) * xs_lo + (d * (float)s1) * shi -
-           (dmin * (float)m1) * xs_hi;
+    uint32_t sc, mn;
+    scale_min_pair(hdr.y, hdr.z, hdr.w, j, sc, mn);
+    const float d = hf(hdr.x & 0xFFFFu), dmin = hf(hdr.x >> 16);
+    const float s0v = x.scale[0] * planes(A[0][0], A[0][1], A[0][2]);
+    const float s1v = x.scale[1] * planes(A[1][0], A[1][1], A[1][2]);
+    return (d * (float)(sc & 255u)) * s0v - (dmin * (float)(mn & 255u)) * x.sum[0] +
+           (d * (float)(sc >> 8)) * s1v - (dmin * (float)(mn >> 8)) * x.sum[1];
 }
 
 // Q6_K unit: columns 128h + 64mm + [0, 64) of block u/4. Weight
 // 128h + 64mm + 32k + l uses ql[64h + 32k + l] (low nibble if mm = 0, high
-// if mm = 1) and bits 2(2mm + k) of qh[32h + l]; q - 32 times the int8 scale
-// of its 16-weight group, times d.
-__device__ __forceinline__ float unit_q6k(const uint8_t *row, int u, const float *xr)
+// if mm = 1) and bits 2(2mm + k) of qh[32h + l]; (q - 32) times the int8
+// scale of its 16-weight group, times d (src/gguf_model.c:516-566).
+__device__ __forceinline__ float unit_q6k(const uint8_t *row, int u, const XUnit &x)
 {
     const uint8_t *blk = row + (u >> 2) * 210;
     const int h = (u >> 1) & 1, mm = u & 1;
     uint32_t ql[16], qh[8];
     ld_words_a2<16>(blk + 64 * h, ql);
     ld_words_a2<8>(blk + 128 + 32 * h, qh);
-    float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    int A[4][3];
+#pragma unroll
+    for (int i = 0; i < 4; i++) A[i][0] = A[i][1] = A[i][2] = 0;
 #pragma unroll
     for (int k = 0; k < 2; k++) {
-        const int hs = 2 * (2 * mm + k);
+        const int sh = 2 * (2 * mm + k);
 #pragma unroll
-        for (int wv = 0; wv < 8; wv++) {  // 8 words = 32 l values
+        for (int wv = 0; wv < 8; wv++) {
             const uint32_t nib = mm ? ((ql[8 * k + wv] >> 4) & 0x0F0F0F0Fu) : (ql[8 * k + wv] & 0x0F0F0F0Fu);
-            const uint32_t q6 = nib | (((qh[wv] >> hs) & 0x03030303u) << 4);
+            const uint32_t q6 = nib | (((qh[wv] >> sh) & 0x03030303u) << 4);
+            const int g16 = 2 * k + (wv >> 2);
 #pragma unroll
-            for (int b = 0; b < 4; b++) {
-                const int col = 32 * k + 4 * wv + b;  // within the unit
-                // q - 32 exactly: (2^23 + q) - (2^23 + 32)
-                const float qf = __uint_as_float(0x4B000000u | ((q6 >> (8 * b)) & 63u)) - 8388640.0f;
-                s[col >> 4] = fmaf(qf, xr[col], s[col >> 4]);
-            }
+            for (int p = 0; p < 3; p++) A[g16][p] = dp4a_us(q6, x.d[k][p][wv], A[g16][p]);
         }
     }
-    const float d = h2f(ld_u16(blk + 208));
+    const float d = hf(ld_u16(blk + 208));
     const int8_t *sc = reinterpret_cast<const int8_t *>(blk + 192 + 8 * h + 4 * mm);
-    return (d * (float)sc[0]) * s[0] + (d * (float)sc[1]) * s[1] + (d * (float)sc[2]) * s[2] +
-           (d * (float)sc[3]) * s[3];
+    float total = 0.0f;
+#pragma unroll
+    for (int g16 = 0; g16 < 4; g16++) {
+        const int g = g16 >> 1, half = g16 & 1;
+        const float v = x.scale[g] * planes(A[g16][0] - 32 * x.dsum[g][half][0], A[g16][1] - 32 * x.dsum[g][half][1],
+                                            A[g16][2] - 32 * x.dsum[g][half][2]);
+        total = fmaf(d * (float)sc[g16], v, total);
+    }
+    return total;
 }
 
-// Q4_0 unit: blocks 2u and (if present) 2u+1.
-__device__ __forceinline__ float unit_q4_0(const uint8_t *row, int u, int nblocks, const float *xr)
+// Q4_0 unit: blocks 2u and (if present) 2u+1, w = d*(q-8),
+// src/gguf_model.c:633-661.
+__device__ __forceinline__ float unit_q4_0(const uint8_t *row, int u, int nblocks, const XUnit &x)
 {
     float total = 0.0f;
 #pragma unroll
-    for (int k = 0; k < 2; k++) {
-        if (2 * u + k < nblocks) {
-            const uint8_t *blk = row + (2 * u + k) * 18;
+    for (int kb = 0; kb < 2; kb++) {
+        if (2 * u + kb < nblocks) {
+            const uint8_t *blk = row + (2 * u + kb) * 18;
             uint32_t w[4];
             ld_words_a2<4>(blk + 2, w);
-            float s = 0.0f;
+            int A[3] = {0, 0, 0};
 #pragma unroll
             for (int wv = 0; wv < 4; wv++) {
+                const uint32_t lo = w[wv] & 0x0F0F0F0Fu, hi = (w[wv] >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
-                for (int b = 0; b < 4; b++) {
-                    const uint32_t byte = (w[wv] >> (8 * b)) & 255u;
-                    s = fmaf(__uint_as_float(0x4B000000u | (byte & 15u)) - 8388616.0f,
-                             xr[32 * k + 4 * wv + b], s);
-                    s = fmaf(__uint_as_float(0x4B000000u | (byte >> 4)) - 8388616.0f,
-                             xr[32 * k + 16 + 4 * wv + b], s);
+                for (int p = 0; p < 3; p++) {
+                    A[p] = dp4a_us(lo, x.d[kb][p][wv], A[p]);
+                    A[p] = dp4a_us(hi, x.d[kb][p][4 + wv], A[p]);
                 }
             }
-            total = fmaf(h2f(ld_u16(blk)), s, total);
+            const float v = x.scale[kb] * planes(A[0] - 8 * (x.dsum[kb][0][0] + x.dsum[kb][1][0]),
+                                                 A[1] - 8 * (x.dsum[kb][0][1] + x.dsum[kb][1][1]),
+                                                 A[2] - 8 * (x.dsum[kb][0][2] + x.dsum[kb][1][2]));
+            total = fmaf(hf(ld_u16(blk)), v, total);
         }
     }
     return total;
 }
 
-// Q8_0 unit: blocks 2u and (if present) 2u+1.
-__device__ __forceinline__ float unit_q8_0(const uint8_t *row, int u, int nblocks, const float *xr)
+// Q8_0 unit: blocks 2u and (if present) 2u+1, w = q*d,
+// src/gguf_model.c:664-691.
+__device__ __forceinline__ float unit_q8_0(const uint8_t *row, int u, int nblocks, const XUnit &x)
 {
     float total = 0.0f;
 #pragma unroll
-    for (int k = 0; k < 2; k++) {
-        if (2 * u + k < nblocks) {
-            const uint8_t *blk = row + (2 * u + k) * 34;
+    for (int kb = 0; kb < 2; kb++) {
+        if (2 * u + kb < nblocks) {
+            const uint8_t *blk = row + (2 * u + kb) * 34;
             uint32_t w[8];
             ld_words_a2<8>(blk + 2, w);
-            float s = 0.0f;
+            int A[3] = {0, 0, 0};
 #pragma unroll
             for (int wv = 0; wv < 8; wv++) {
 #pragma unroll
-                for (int b = 0; b < 4; b++) {
-                    // signed byte -> (2^23 + 128 + q) - (2^23 + 128)
-                    const uint32_t byte = ((w[wv] >> (8 * b)) & 255u) ^ 128u;
-                    s = fmaf(__uint_as_float(0x4B000000u | byte) - 8388736.0f, xr[32 * k + 4 * wv + b], s);
-                }
+                for (int p = 0; p < 3; p++) A[p] = dp4a_ss(w[wv], x.d[kb][p][wv], A[p]);
             }
-            total = fmaf(h2f(ld_u16(blk)), s, total);
+            total = fmaf(hf(ld_u16(blk)), x.scale[kb] * planes(A[0], A[1], A[2]), total);
         }
     }
     return total;
 }
 
-// F32 / F16 unit: columns 64u .. min(64u+64, cols).
-__device__ __forceinline__ float unit_float(int t, const uint8_t *row, int u, int cols, const float *xr)
+// F32 / F16 unit: columns 64u .. min(64u+64, cols). The activations are
+// rebuilt from the digits in shared memory (these formats are rare in the
+// quantized path, so they do not get a register copy).
+__device__ __forceinline__ float unit_float(int t, const uint8_t *row, int u, int cols, const uint8_t *xq,
+                                            const float *xg)
 {
     float s = 0.0f;
-#pragma unroll
+    const int8_t *dq = reinterpret_cast<const int8_t *>(xq + u * XQ_UNIT_BYTES);
+#pragma unroll 4
     for (int i = 0; i < 64; i++) {
         const int c = 64 * u + i;
         if (c < cols) {
-            s = fmaf(t == T_F32 ? decode_elem<T_F32>(row, c) : decode_elem<T_F16>(row, c), xr[i], s);
+            const int g = i >> 5, l = i & 31;
+            const float xv = xg[u * XG_UNIT_WORDS + 8 * g] *
+                             planes(dq[96 * g + l], dq[96 * g + 32 + l], dq[96 * g + 64 + l]);
+            const float wv = t == T_F32 ? decode_elem<T_F32>(row, c) : decode_elem<T_F16>(row, c);
+            s = fmaf(wv, xv, s);
         }
     }
     return s;

@@ -1,0 +1,734 @@
+// pk_stream.cuh - the phase executor shared by every kernel of the decode
+// path: one "phase" is a fused dequant-matvec over up to three matrices
+// (with its prologue and epilogue) or the attention of one layer.
+//
+// Data movement. Every warp owns a ring of shared-memory stages and an
+// mbarrier per stage. Lane 0 issues 1-D bulk copies (cp.async.bulk, the
+// TMA engine) of whole packed rows into the ring; the tiles a warp will
+// consume are known in advance for every phase, so in the persistent decode
+// kernel the ring keeps streaming the NEXT phases' weights while the warp
+// waits at a grid barrier. Weights never depend on activations.
+//
+// Compute. x is staged once per phase and CTA in integer form (pk_quant.cuh);
+// each lane owns 64-column units; a row's units are summed over the warp.
+#pragma once
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "pk_quant.cuh"
+
+namespace pk {
+
+constexpr long long WAIT_LIMIT_CYCLES = 4000000000LL;  // ~2 s at 2 GHz
+
+enum { PH_MV = 0, PH_ATTN = 1 };
+enum { PRO_PLAIN = 0, PRO_NORM = 1, PRO_EMBED_NORM = 2 };
+enum { EPI_STORE = 0, EPI_ADD = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
+enum { KIND_PLAIN = 0, KIND_Q = 1, KIND_K = 2, KIND_V = 3 };
+enum { ERR_TIMEOUT_MV = 1, ERR_TIMEOUT_BARRIER = 2, ERR_NONFINITE = 4 };
+
+// ------------------------------------------------------------------ //
+// PTX helpers                                                        //
+// ------------------------------------------------------------------ //
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init()
+{
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for phase `parity` of `bar`, giving up after WAIT_LIMIT_CYCLES.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
+    }
+    return true;
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p)
+{
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+    return v;
+}
+
+// Float -> uint32 whose unsigned order is the float order.
+__device__ __forceinline__ uint32_t order_key(float f)
+{
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// ------------------------------------------------------------------ //
+// Phase description                                                  //
+// ------------------------------------------------------------------ //
+
+struct MvSeg {
+    const uint8_t *w;   // row 0 of the (first) matrix
+    const uint8_t *w2;  // row 0 of the paired matrix (EPI_SWIGLU) or null
+    uint64_t rb, rb2;   // bytes per row of each
+    int rows, type, type2, R, tile0, kind;
+};
+
+struct Phase {
+    int kind, pro, epi;
+    // fused matvec
+    MvSeg seg[3];
+    int nseg, ntiles, cols, nunits;
+    const float *xin;     // input vector (PRO_PLAIN / PRO_NORM)
+    const float *norm;    // RMSNorm weights (PRO_NORM / PRO_EMBED_NORM)
+    float eps;
+    float *y;             // output / residual / SwiGLU result / logits
+    const uint8_t *embd;  // PRO_EMBED_NORM: embedding table, row bytes, type
+    uint64_t embd_rb;
+    int embd_type;
+    float *xout;          // PRO_EMBED_NORM: CTA 0 stores the raw embedding row here
+    float *q, *kc, *vc;   // EPI_QKV
+    const float *rope_cs;
+    int hs, rope_dim, kv_dim, seq_len, layer;
+    unsigned long long *amax;  // EPI_LOGITS: [0] packed argmax, [1] non-finite flag
+    // attention
+    const float *aq;
+    float *aout, *part;
+    unsigned *count;
+    int kv_mul, n_kv, nsplit_max;
+    float scale;
+};
+
+// ------------------------------------------------------------------ //
+// Bulk-copy ring                                                     //
+// ------------------------------------------------------------------ //
+
+struct Span {
+    uintptr_t a0;
+    uint32_t bulk, tail;
+};
+
+// Bytes [st, st + n) land at buf + (st & 15): the 16-byte aligned body via
+// the bulk-copy engine, the sub-16-byte tail (only a matrix's last row can
+// end unaligned) via plain loads, so nothing past the matrix is read.
+__device__ __forceinline__ Span make_span(uintptr_t st, uint64_t n)
+{
+    Span sp;
+    sp.a0 = st & ~(uintptr_t)15;
+    const uintptr_t a1 = (st + n) & ~(uintptr_t)15;
+    sp.bulk = a1 > sp.a0 ? (uint32_t)(a1 - sp.a0) : 0u;
+    sp.tail = (uint32_t)(st + n - (sp.a0 + sp.bulk));
+    return sp;
+}
+
+__device__ __forceinline__ void fill_span(const Span &sp, uint8_t *buf, uint64_t *bar)
+{
+    if (sp.bulk) bulk_g2s(buf, reinterpret_cast<const void *>(sp.a0), sp.bulk, bar);
+    const uint8_t *t = reinterpret_cast<const uint8_t *>(sp.a0 + sp.bulk);
+    for (uint32_t i = 0; i < sp.tail; i++) buf[sp.bulk + i] = t[i];
+}
+
+__device__ __forceinline__ const MvSeg &find_seg(const Phase &p, int t)
+{
+    if (p.nseg > 2 && t >= p.seg[2].tile0) return p.seg[2];
+    if (p.nseg > 1 && t >= p.seg[1].tile0) return p.seg[1];
+    return p.seg[0];
+}
+
+// Lane 0: issue the copies of tile t of phase p into buf; completes on bar.
+__device__ __forceinline__ void issue_tile(const Phase &p, int t, uint8_t *buf, int stage_bytes, uint64_t *bar)
+{
+    const MvSeg &s = find_seg(p, t);
+    const int r0 = (t - s.tile0) * s.R;
+    const int nr = min(s.R, s.rows - r0);
+    const Span sa = make_span(reinterpret_cast<uintptr_t>(s.w) + (uintptr_t)r0 * s.rb, (uint64_t)nr * s.rb);
+    if (s.w2 != nullptr) {
+        const Span sb = make_span(reinterpret_cast<uintptr_t>(s.w2) + (uintptr_t)r0 * s.rb2, (uint64_t)nr * s.rb2);
+        mbar_expect_tx(bar, sa.bulk + sb.bulk);
+        fill_span(sa, buf, bar);
+        fill_span(sb, buf + stage_bytes / 2, bar);
+    } else {
+        mbar_expect_tx(bar, sa.bulk);
+        fill_span(sa, buf, bar);
+    }
+}
+
+// A warp's ring and its producer cursor (phase index, tile ordinal).
+struct Ring {
+    uint64_t *bars;
+    uint8_t *buf;
+    int stages, stage_bytes;
+    uint32_t issued, consumed;
+    int cp, ck;
+};
+
+// Lane 0: top the ring up with this warp's next tiles, in consumption order,
+// across phase boundaries.
+__device__ __forceinline__ void ring_fill(Ring &r, const Phase *ph, int nph, int gw, int nw_total)
+{
+    while (r.issued - r.consumed < (uint32_t)r.stages && r.cp < nph) {
+        const Phase &p = ph[r.cp];
+        const int t = gw + r.ck * nw_total;
+        if (p.kind != PH_MV || t >= p.ntiles) {
+            r.cp++;
+            r.ck = 0;
+            continue;
+        }
+        const uint32_t slot = r.issued % (uint32_t)r.stages;
+        issue_tile(p, t, r.buf + slot * r.stage_bytes, r.stage_bytes, r.bars + slot);
+        r.issued++;
+        r.ck++;
+    }
+}
+
+// Wait (bounded) for every copy still in flight, e.g. before leaving early.
+__device__ __forceinline__ void ring_drain(Ring &r)
+{
+    for (uint32_t i = r.consumed; i < r.issued; i++) {
+        mbar_wait_bounded(r.bars + i % (uint32_t)r.stages, (i / (uint32_t)r.stages) & 1u);
+    }
+    r.consumed = r.issued;
+}
+
+// ------------------------------------------------------------------ //
+// x staging                                                          //
+// ------------------------------------------------------------------ //
+
+// 2^k as a float, for -126 <= k <= 127.
+__device__ __forceinline__ float pow2f(int k)
+{
+    return __uint_as_float((uint32_t)(k + 127) << 23);
+}
+
+// Stage the phase's input vector in integer form (pk_quant.cuh): RMSNorm'ed
+// as src/gguf_forward.c:24-40 (o = w * (ss * x), ss = 1 / sqrtf(mean(x^2) +
+// eps)) for PRO_NORM, and taken from the embedding row (bit-exact decode,
+// src/gguf_model.c:314-359) for PRO_EMBED_NORM. All threads of the CTA.
+//
+// Four threads own a 32-column group (eight columns each, kept in
+// registers from one load to the digits), so there are no per-element
+// round trips and only two-step shuffles within the quad.
+__device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t *xq, float *xg)
+{
+    constexpr int MAXP = 4;  // groups per quad per pass
+    __shared__ float red[32];
+    const int pro = p.pro, n = p.cols, ng = 2 * p.nunits;
+    const float *xin = p.xin, *norm = p.norm;
+    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
+    const int quad = tid >> 2, t = tid & 3, nquads = nt >> 2;
+    const bool one_pass = ng <= MAXP * nquads;  // values stay in registers from load to digits
+    const uint8_t *erow = nullptr;
+    int etype = 0;
+    if (pro == PRO_EMBED_NORM) {
+        erow = p.embd + (size_t)step[0] * p.embd_rb;
+        etype = p.embd_type;
+    }
+    auto load8 = [&](int c0, float *v) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[e] = 0.0f;
+        if (pro == PRO_EMBED_NORM) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                if (c0 + e < n) v[e] = decode_col(etype, erow, c0 + e);
+            }
+        } else if (c0 + 8 <= n) {
+            // x was written by other CTAs (possibly in this launch): read L2
+            const float4 a = __ldcg(reinterpret_cast<const float4 *>(xin + c0));
+            const float4 b = __ldcg(reinterpret_cast<const float4 *>(xin + c0 + 4));
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+            v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                if (c0 + e < n) v[e] = __ldcg(xin + c0 + e);
+            }
+        }
+    };
+    // RMSNorm scale from the block-wide sum of squares.
+    auto norm_scale = [&](float ss) -> float {
+        ss = warp_sum(ss);
+        __syncthreads();  // `red` may still be read by a previous phase's staging
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float tot = 0.0f;
+        for (int w = 0; w < (nt >> 5); w++) tot += red[w];
+        float m = __fdiv_rn(tot, (float)n);
+        m = __fadd_rn(m, p.eps);
+        return __fdiv_rn(1.0f, __fsqrt_rn(m));
+    };
+    float sc = 1.0f;
+    if (pro != PRO_PLAIN && !one_pass) {
+        float ss = 0.0f;
+        for (int g = quad; g < ng; g += nquads) {
+            float v[8];
+            load8(32 * g + 8 * t, v);
+#pragma unroll
+            for (int e = 0; e < 8; e++) ss = fmaf(v[e], v[e], ss);
+        }
+        sc = norm_scale(ss);
+    }
+    for (int base = 0; base < ng; base += MAXP * nquads) {
+        float v[MAXP][8];
+        float ss = 0.0f;
+#pragma unroll
+        for (int k = 0; k < MAXP; k++) {
+            const int g = base + quad + k * nquads;
+            load8(32 * g + 8 * t, v[k]);  // beyond ng: zeros (c0 >= n)
+            if (pro == PRO_EMBED_NORM && blockIdx.x == 0 && g < ng) {
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    if (32 * g + 8 * t + e < n) p.xout[32 * g + 8 * t + e] = v[k][e];
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < 8; e++) ss = fmaf(v[k][e], v[k][e], ss);
+        }
+        if (pro != PRO_PLAIN && one_pass) sc = norm_scale(ss);
+#pragma unroll
+        for (int k = 0; k < MAXP; k++) {
+            // The shuffles below name all 32 lanes, so the loop may only be
+            // left by whole warps: quads past ng run on zeros, store nothing.
+            if (base + 8 * warp + k * nquads >= ng) break;
+            const int g = base + quad + k * nquads;
+            const bool act = g < ng;
+            const int c0 = 32 * g + 8 * t;
+            if (pro != PRO_PLAIN) {
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    if (c0 + e < n) v[k][e] = __fmul_rn(norm[c0 + e], __fmul_rn(sc, v[k][e]));
+                }
+            }
+            float amax = 0.0f, sum = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                amax = fmaxf(amax, fabsf(v[k][e]));
+                sum += v[k][e];
+            }
+            amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
+            sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+            sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+            // amax = m * 2^E with m in [0.5, 1): E from the exponent bits.
+            // Groups below 2^-105 (or subnormal) are stored as zero.
+            const int E = (int)((__float_as_uint(amax) >> 23) & 255u) - 126;
+            const bool live = E >= -104;
+            const float f = live ? pow2f(22 - E) : 0.0f;
+            uint32_t w0[2] = {0u, 0u}, w1[2] = {0u, 0u}, w2[2] = {0u, 0u};
+            int ds0 = 0, ds1 = 0, ds2 = 0;
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                // exact: |v * f| < 2^22 and f is a power of two
+                const int X = __float2int_rn(v[k][e] * f);
+                // signed base-256 digits: X = d0 + 2^8 d1 + 2^16 d2, |dk| <= 128
+                const int d0 = ((X + 128) & 255) - 128;
+                const int r1 = (X - d0) >> 8;
+                const int d1 = ((r1 + 128) & 255) - 128;
+                const int d2 = (r1 - d1) >> 8;
+                w0[e >> 2] |= (uint32_t)(d0 & 255) << (8 * (e & 3));
+                w1[e >> 2] |= (uint32_t)(d1 & 255) << (8 * (e & 3));
+                w2[e >> 2] |= (uint32_t)(d2 & 255) << (8 * (e & 3));
+                ds0 += d0;
+                ds1 += d1;
+                ds2 += d2;
+            }
+            // digit sums per 16-column half: threads (0,1) and (2,3)
+            ds0 += __shfl_xor_sync(0xFFFFFFFFu, ds0, 1);
+            ds1 += __shfl_xor_sync(0xFFFFFFFFu, ds1, 1);
+            ds2 += __shfl_xor_sync(0xFFFFFFFFu, ds2, 1);
+            if (!act) continue;
+            uint8_t *q = xq + (g >> 1) * XQ_UNIT_BYTES + (g & 1) * 96 + 8 * t;
+            *reinterpret_cast<uint2 *>(q) = make_uint2(w0[0], w0[1]);
+            *reinterpret_cast<uint2 *>(q + 32) = make_uint2(w1[0], w1[1]);
+            *reinterpret_cast<uint2 *>(q + 64) = make_uint2(w2[0], w2[1]);
+            float *gi = xg + (g >> 1) * XG_UNIT_WORDS + (g & 1) * 8;
+            if (t == 0) {
+                gi[0] = live ? pow2f(E - 22) : 0.0f;
+                gi[1] = sum;
+                gi[2] = __int_as_float(ds0);
+                gi[3] = __int_as_float(ds1);
+                gi[4] = __int_as_float(ds2);
+            } else if (t == 2) {
+                gi[5] = __int_as_float(ds0);
+                gi[6] = __int_as_float(ds1);
+                gi[7] = __int_as_float(ds2);
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// ------------------------------------------------------------------ //
+// Tile compute                                                       //
+// ------------------------------------------------------------------ //
+
+template <int T>
+__device__ __forceinline__ float unit_dot(const uint8_t *row, int u, int nblk, int cols, const XUnit &x,
+                                          const uint8_t *xq, const float *xg)
+{
+    if (T == T_Q4_K) return unit_q4k(row, u, x);
+    if (T == T_Q5_K) return unit_q5k(row, u, x);
+    if (T == T_Q6_K) return unit_q6k(row, u, x);
+    if (T == T_Q4_0) return unit_q4_0(row, u, nblk, x);
+    if (T == T_Q8_0) return unit_q8_0(row, u, nblk, x);
+    return unit_float(T, row, u, cols, xq, xg);
+}
+
+// Row sums of a tile: lane i (< nr) returns row i's dot in .x (and the
+// paired row's in .y). Rows go in unrolled chunks of RU (independent dp4a
+// chains for ILP, accumulated in registers); units are taken 32 at a time,
+// one per lane, and each row is reduced over the warp once.
+template <int T, bool PAIR>
+__device__ __forceinline__ float2 tile_rows(const uint8_t *ra, uint64_t rba, const uint8_t *rb, uint64_t rbb, int nr,
+                                           int nunits, int cols, const uint8_t *xq, const float *xg, int lane)
+{
+    constexpr int RU = PAIR ? 2 : 4;
+    const int nblk = cols / block_weights(T);
+    float a = 0.0f, b = 0.0f;
+    for (int i0 = 0; i0 < nr; i0 += RU) {
+        float va[RU], vb[RU];
+#pragma unroll
+        for (int j = 0; j < RU; j++) va[j] = vb[j] = 0.0f;
+        for (int u0 = 0; u0 < nunits; u0 += 32) {
+            const int u = u0 + lane;
+            if (u < nunits) {
+                XUnit x;
+                if (T != T_F32 && T != T_F16) load_xunit(xq, xg, u, x);
+#pragma unroll
+                for (int j = 0; j < RU; j++) {
+                    if (i0 + j < nr) {
+                        va[j] += unit_dot<T>(ra + (size_t)(i0 + j) * rba, u, nblk, cols, x, xq, xg);
+                        if (PAIR) vb[j] += unit_dot<T>(rb + (size_t)(i0 + j) * rbb, u, nblk, cols, x, xq, xg);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < RU; j++) {
+            const float sa = warp_sum(va[j]);
+            if (lane == i0 + j) a = sa;
+            if (PAIR) {
+                const float sb = warp_sum(vb[j]);
+                if (lane == i0 + j) b = sb;
+            }
+        }
+    }
+    return make_float2(a, b);
+}
+
+template <bool PAIR>
+__device__ __forceinline__ float2 tile_dispatch(int type, const uint8_t *ra, uint64_t rba, const uint8_t *rb,
+                                                uint64_t rbb, int nr, int nunits, int cols, const uint8_t *xq,
+                                                const float *xg, int lane)
+{
+    switch (type) {
+    case T_Q4_K: return tile_rows<T_Q4_K, PAIR>(ra, rba, rb, rbb, nr, nunits, cols, xq, xg, lane);
+    case T_Q5_K: return tile_rows<T_Q5_K, PAIR>(ra, rba, rb, rbb, nr, nunits, cols, xq, xg, lane);
+    case T_Q6_K: return tile_rows<T_Q6_K, PAIR>(ra, rba, rb, rbb, nr, nunits, cols, xq, xg, lane);
+    case T_Q4_0: return tile_rows<T_Q4_0, PAIR>(ra, rba, rb, rbb, nr, nunits, cols, xq, xg, lane);
+    case T_Q8_0: return tile_rows<T_Q8_0, PAIR>(ra, rba, rb, rbb, nr, nunits, cols, xq, xg, lane);
+    case T_F32: return tile_rows<T_F32, PAIR>(ra, rba, rb, rbb, nr, nunits, cols, xq, xg, lane);
+    case T_F16: return tile_rows<T_F16, PAIR>(ra, rba, rb, rbb, nr, nunits, cols, xq, xg, lane);
+    default: return make_float2(0.0f, 0.0f);
+    }
+}
+
+// Compute tile t of phase p from its ring slot and apply the epilogue.
+__device__ __forceinline__ void run_tile(const Phase &p, int t, const uint8_t *buf, int stage_bytes,
+                                         const uint8_t *xq, const float *xg, const int *step, int lane,
+                                         unsigned long long *cta_amax)
+{
+    const MvSeg &s = find_seg(p, t);
+    const int r0 = (t - s.tile0) * s.R;
+    const int nr = min(s.R, s.rows - r0);
+    const uint8_t *ra = buf + ((reinterpret_cast<uintptr_t>(s.w) + (uintptr_t)r0 * s.rb) & 15);
+    float va, vb = 0.0f;
+    if (p.epi == EPI_SWIGLU && s.type == s.type2) {
+        const uint8_t *rb =
+            buf + stage_bytes / 2 + ((reinterpret_cast<uintptr_t>(s.w2) + (uintptr_t)r0 * s.rb2) & 15);
+        const float2 v = tile_dispatch<true>(s.type, ra, s.rb, rb, s.rb2, nr, p.nunits, p.cols, xq, xg, lane);
+        va = v.x;
+        vb = v.y;
+    } else {
+        va = tile_dispatch<false>(s.type, ra, s.rb, nullptr, 0, nr, p.nunits, p.cols, xq, xg, lane).x;
+        if (p.epi == EPI_SWIGLU) {  // gate and up stored in different formats
+            const uint8_t *rb =
+                buf + stage_bytes / 2 + ((reinterpret_cast<uintptr_t>(s.w2) + (uintptr_t)r0 * s.rb2) & 15);
+            vb = tile_dispatch<false>(s.type2, rb, s.rb2, nullptr, 0, nr, p.nunits, p.cols, xq, xg, lane).x;
+        }
+    }
+    // Epilogue: lane i owns row r0 + i.
+    const int r = r0 + lane;
+    if (p.epi == EPI_QKV) {
+        // RoPE pairs (2i, 2i+1) sit in neighbouring lanes (R and r0 are even).
+        const float other = __shfl_xor_sync(0xFFFFFFFFu, va, 1);
+        if (lane < nr) {
+            const int pos = step[1];
+            float v = va;
+            const int d = r % p.hs;
+            if (s.kind != KIND_V && (d & ~1) < p.rope_dim) {
+                // rope_head, src/gguf_forward.c:50-66 (cos/sin from the host table)
+                const int i0 = d & ~1;
+                const float c = p.rope_cs[(size_t)pos * p.rope_dim + i0];
+                const float sn = p.rope_cs[(size_t)pos * p.rope_dim + i0 + 1];
+                const float v0 = (d & 1) ? other : va, v1 = (d & 1) ? va : other;
+                v = (d & 1) ? __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, c))
+                            : __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, sn));
+            }
+            const size_t cache_row = ((size_t)p.layer * p.seq_len + pos) * p.kv_dim;
+            float *dst = s.kind == KIND_Q ? p.q + r : (s.kind == KIND_K ? p.kc : p.vc) + cache_row + r;
+            *dst = v;
+        }
+    } else if (p.epi == EPI_LOGITS) {
+        // logits + greedy argmax: the warp's best (value, lowest row) goes to
+        // the CTA's slot; the CTA's to the global one at the end of the phase
+        unsigned long long key = 0ull;
+        bool bad = false;
+        if (lane < nr) {
+            p.y[r] = va;
+            if (isfinite(va)) {
+                key = ((unsigned long long)order_key(va) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)r);
+            } else {
+                bad = true;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, key, o);
+            key = other > key ? other : key;
+        }
+        if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) cta_amax[1] = 1ull;
+        if (lane == 0 && key != 0ull) atomicMax(cta_amax, key);
+    } else if (lane < nr) {
+        if (p.epi == EPI_STORE) {
+            p.y[r] = va;
+        } else if (p.epi == EPI_ADD) {
+            p.y[r] = __fadd_rn(__ldcg(p.y + r), va);
+        } else if (p.epi == EPI_SWIGLU) {
+            p.y[r] = __fmul_rn(__fdiv_rn(va, __fadd_rn(1.0f, expf(-va))), vb);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ //
+// Attention item                                                     //
+// ------------------------------------------------------------------ //
+
+// Positions per attention sub-chunk (one K/V tile in shared memory).
+constexpr int ATT_SUB = 32;
+
+// Scratch floats an attention item needs: queries, two K tiles (rows padded
+// to hs + 1 floats: conflict-free per-position dot products), two V tiles,
+// probabilities, the running output and softmax state, merge weights.
+__host__ __device__ inline int attn_scratch_floats(int kv_mul, int hs, int nsplit_max)
+{
+    return kv_mul * hs + 2 * ATT_SUB * (hs + 1) + 2 * ATT_SUB * hs + kv_mul * ATT_SUB + kv_mul * hs + 3 * kv_mul +
+           kv_mul * nsplit_max;
+}
+
+// Positions one attention item covers at context length n: enough items to
+// cover the GPU (n_kv * splits ~ grid), in whole sub-chunks.
+__device__ __forceinline__ int attn_span(int n, int n_kv, int grid)
+{
+    const int splits = max(1, grid / n_kv);
+    const int per = (n + splits - 1) / splits;
+    return max(ATT_SUB, (per + ATT_SUB - 1) / ATT_SUB * ATT_SUB);
+}
+
+__device__ __forceinline__ void cp_async4(float *dst, const float *src)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+// Item (g, s): positions [s * span, s * span + span) of the kv_mul query heads
+// sharing KV head g, so each K/V row is read once per group. K/V tiles of 32
+// positions are double-buffered with cp.async; the softmax runs online over
+// the tiles (running max and sum). With one split the item writes the head
+// outputs directly; otherwise the last item of the group to finish merges the
+// splits' (max, sum, weighted V) partials in split order.
+// src/gguf_forward.c:228-267 with the softmax of src/transformer.c:85-109.
+// All threads of the CTA.
+__device__ __forceinline__ void attn_item(const Phase &p, int g, int s, int n, int span, float *sm)
+{
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int hs = p.hs, km = p.kv_mul, kvd = p.kv_dim;
+    const int nsplit = (n + span - 1) / span;
+    const int t0 = s * span, cnt = min(span, n - t0);
+    const int nsub = (cnt + ATT_SUB - 1) / ATT_SUB;
+    const int ks = hs + 1;
+    float *qs = sm;                                  // km * hs
+    float *sK = qs + km * hs;                        // 2 * ATT_SUB * ks
+    float *sV = sK + 2 * ATT_SUB * ks;               // 2 * ATT_SUB * hs
+    float *pr = sV + 2 * ATT_SUB * hs;               // km * ATT_SUB
+    float *orun = pr + km * ATT_SUB;                 // km * hs
+    float *mrun = orun + km * hs, *lrun = mrun + km, *alpha = lrun + km;
+    float *wts = alpha + km;                         // km * nsplit_max
+    __shared__ int last_sh;
+
+    const size_t lbase = (size_t)p.layer * p.seq_len * kvd + (size_t)g * hs;
+    auto load_tile = [&](int sub, int buf) {
+        const int tb = t0 + sub * ATT_SUB, tc = min(ATT_SUB, t0 + cnt - tb);
+        float *K = sK + buf * ATT_SUB * ks, *V = sV + buf * ATT_SUB * hs;
+        for (int i = tid; i < tc * hs; i += blockDim.x) {
+            const int t = i / hs, d = i % hs;
+            const size_t off = lbase + (size_t)(tb + t) * kvd + d;
+            cp_async4(K + t * ks + d, p.kc + off);
+            cp_async4(V + t * hs + d, p.vc + off);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    load_tile(0, 0);
+    for (int i = tid; i < km * hs; i += blockDim.x) {
+        qs[i] = __ldcg(p.aq + (size_t)g * km * hs + i);
+        orun[i] = 0.0f;
+    }
+    if (tid < km) {
+        mrun[tid] = -INFINITY;
+        lrun[tid] = 0.0f;
+    }
+    for (int sub = 0; sub < nsub; sub++) {
+        const int buf = sub & 1;
+        if (sub + 1 < nsub) {
+            load_tile(sub + 1, buf ^ 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        const int tc = min(ATT_SUB, cnt - sub * ATT_SUB);
+        const float *K = sK + buf * ATT_SUB * ks, *V = sV + buf * ATT_SUB * hs;
+        // scores: thread (head h, position t)
+        for (int i = tid; i < km * ATT_SUB; i += blockDim.x) {
+            const int h = i / ATT_SUB, t = i % ATT_SUB;
+            float sc = -INFINITY;
+            if (t < tc) {
+                float acc = 0.0f;
+                for (int d = 0; d < hs; d++) acc = fmaf(qs[h * hs + d], K[t * ks + d], acc);
+                sc = acc * p.scale;
+            }
+            pr[i] = sc;
+        }
+        __syncthreads();
+        // online softmax per head (one warp per head, one lane per position)
+        for (int h = warp; h < km; h += nw) {
+            const float sc = pr[h * ATT_SUB + lane];
+            const float mnew = fmaxf(mrun[h], warp_max(sc));
+            const float e = lane < tc ? expf(sc - mnew) : 0.0f;
+            pr[h * ATT_SUB + lane] = e;
+            const float lsum = warp_sum(e);
+            if (lane == 0) {
+                const float a = expf(mrun[h] - mnew);  // 0 on the first tile (mrun = -inf)
+                alpha[h] = a;
+                lrun[h] = fmaf(lrun[h], a, lsum);
+                mrun[h] = mnew;
+            }
+        }
+        __syncthreads();
+        for (int i = tid; i < km * hs; i += blockDim.x) {
+            const int h = i / hs, d = i % hs;
+            float o = orun[i] * alpha[h];
+            for (int t = 0; t < tc; t++) o = fmaf(pr[h * ATT_SUB + t], V[t * hs + d], o);
+            orun[i] = o;
+        }
+        __syncthreads();
+    }
+    if (nsplit == 1) {
+        for (int i = tid; i < km * hs; i += blockDim.x) p.aout[(size_t)g * km * hs + i] = orun[i] / lrun[i / hs];
+        return;
+    }
+    const int stride = hs + 2;
+    for (int i = tid; i < km * hs; i += blockDim.x) {
+        const int h = i / hs, d = i % hs;
+        float *P = p.part + ((size_t)(g * km + h) * p.nsplit_max + s) * stride;
+        P[2 + d] = orun[i];
+        if (d == 0) {
+            P[0] = mrun[h];
+            P[1] = lrun[h];
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last_sh = (atomicAdd(p.count + g, 1u) == (unsigned)(nsplit - 1));
+    __syncthreads();
+    if (last_sh) {
+        __threadfence();
+        for (int h = warp; h < km; h += nw) {
+            const float *P = p.part + (size_t)(g * km + h) * p.nsplit_max * stride;
+            float M = -INFINITY;
+            for (int j = lane; j < nsplit; j += 32) M = fmaxf(M, __ldcg(P + (size_t)j * stride));
+            M = warp_max(M);
+            float L = 0.0f;
+            for (int j = lane; j < nsplit; j += 32) {
+                const float w = expf(__ldcg(P + (size_t)j * stride) - M);
+                wts[h * p.nsplit_max + j] = w;
+                L = fmaf(__ldcg(P + (size_t)j * stride + 1), w, L);
+            }
+            L = warp_sum(L);
+            for (int j = lane; j < nsplit; j += 32) wts[h * p.nsplit_max + j] /= L;
+        }
+        __syncthreads();
+        for (int i = tid; i < km * hs; i += blockDim.x) {
+            const int h = i / hs, d = i % hs;
+            const float *P = p.part + (size_t)(g * km + h) * p.nsplit_max * stride + 2 + d;
+            const float *w = wts + h * p.nsplit_max;
+            float O = 0.0f;
+#pragma unroll 4
+            for (int j = 0; j < nsplit; j++) O = fmaf(__ldcg(P + (size_t)j * stride), w[j], O);
+            p.aout[(size_t)(g * km + h) * hs + d] = O;
+        }
+        if (tid == 0) p.count[g] = 0;
+    }
+    __syncthreads();
+}
+
+}  // namespace pk

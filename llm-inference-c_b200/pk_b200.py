@@ -26,7 +26,7 @@ EXPORTS = [
     "engine_open", "engine_close", "engine_forward", "engine_config", "engine_file_context",
     "engine_format", "engine_tokenizer", "engine_kv_cache_bytes", "engine_description",
     "engine_is_stop_token", "engine_open_device", "engine_forward_greedy", "engine_last_error",
-    "engine_weight_bytes", "engine_generate_greedy", "gguf_cuda_matvec", "gguf_cuda_dequantize_rows", "gguf_cuda_fp16_table",
+    "engine_weight_bytes", "engine_generate_greedy", "engine_trace", "gguf_cuda_matvec", "gguf_cuda_dequantize_rows", "gguf_cuda_fp16_table",
     "tokenizer_free",
 ]
 
@@ -113,6 +113,8 @@ def lib(path=LIB_PATH):
     L.engine_generate_greedy.restype = ctypes.c_int
     L.engine_generate_greedy.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P,
                                          ctypes.POINTER(ctypes.c_float)]
+    L.engine_trace.restype = ctypes.c_int
+    L.engine_trace.argtypes = [_P, _P, ctypes.c_int]
     L.gguf_cuda_matvec.restype = ctypes.c_int
     L.gguf_cuda_matvec.argtypes = [ctypes.POINTER(GGUFWeight), _P, _P, _P]
     L.gguf_cuda_dequantize_rows.restype = ctypes.c_int
@@ -164,6 +166,16 @@ class Engine:
         if lib().engine_generate_greedy(self.h, token, pos, n, out.ctypes.data, ctypes.byref(ms)) != 1:
             raise RuntimeError("engine_generate_greedy failed: " + self.last_error())
         return out[:n], ms.value
+
+    def trace(self):
+        """Per-phase device times (us) of the last step as an array of rows
+        (stage x, work, barrier), or None when tracing is off."""
+        out = np.zeros(4096, dtype=np.uint64)
+        n = lib().engine_trace(self.h, out.ctypes.data, out.size)
+        if n <= 1:
+            return None
+        d = np.diff(out[:n].astype(np.float64)) / 1000.0
+        return d[: (len(d) // 3) * 3].reshape(-1, 3)
 
     def description(self):
         return lib().engine_description(self.h).decode()
