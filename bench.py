@@ -44,6 +44,11 @@ WORKLOADS = {
                       prompt=32, context=8192),
 }
 PUBLISHED_TOKS = 8.03  # reference, TinyLlama-1.1B-Chat Q4_K_M, 8 threads (documentation/PERFORMANCE.md:60)
+
+# DRAM bytes (read + write) of one decode-step launch of phase_kernel, from
+# the ncu capture summarised in profiles/phase_kernel_tinyllama_decode.md;
+# None until a capture exists for the workload.
+NCU_TRAFFIC = {}
 FALLBACK_HBM_GBS = 6650.0
 MODEL_SEED = 1234
 
@@ -311,7 +316,12 @@ def main():
     kvb = kv_bytes_per_step(cfg, positions)
     step_s = ms_max / 1000.0 / args.steps
     achieved = (wbytes + kvb) / step_s / 1e9
-    launches_per_step = 1 + 5 * cfg["n_layers"] + 2
+    launches_per_step = e.launches_per_step()
+    if launches_per_step == 2:
+        kernel = (f"phase_kernel (one cooperative launch per step: {5 * cfg['n_layers'] + 1} phases "
+                  f"with grid barriers) + finish_kernel (1 thread)")
+    else:
+        kernel = f"phase_kernel x{launches_per_step - 1} (one per phase) + finish_kernel"
 
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -337,11 +347,12 @@ def main():
                     "path": "engine_forward (host logits) + host argmax",
                     "same_tokens_as_device_loop": bool(e2e_tokens_match)},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": None,
-                         "kernel": f"decode step graph ({launches_per_step} launches: mv_kernel x"
-                                   f"{4 * cfg['n_layers'] + 1}, attn_kernel x{cfg['n_layers']}, embed, finish)",
+                         "frac": achieved / hbm, "traffic": NCU_TRAFFIC.get(wl["name"]),
+                         "kernel": kernel,
+                         "duration": "CUDA events around the graph replays of the timed steps, per step",
                          "algorithmic_bytes_per_step": wbytes + kvb,
                          "weight_bytes_per_step": wbytes,
+                         "weight_stream_frac": wbytes / step_s / 1e9 / hbm,
                          "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs" if peak_kind == "measured"
                          else "fallback 6.65 TB/s"},
             "cpu_baseline": base,

@@ -48,6 +48,12 @@ const char *engine_last_error(const LLMModel *model);
 /* Bytes of packed weights resident on the device. */
 size_t engine_weight_bytes(const LLMModel *model);
 
+/* Kernel launches one decode step makes: 2 in the default mode (the
+ * cooperative step kernel and the one-thread token kernel), one per phase
+ * plus one (5 * n_layers + 2) with POCKET_CUDA_PERSISTENT=0 or when the GPU
+ * cannot co-schedule the step kernel; 0 for a NULL handle. */
+int engine_launches_per_step(const LLMModel *model);
+
 #ifdef __cplusplus
 }
 #endif

@@ -768,6 +768,11 @@ size_t engine_weight_bytes(const LLMModel *m)
     return m == NULL ? 0 : (size_t)m->weight_bytes;
 }
 
+int engine_launches_per_step(const LLMModel *m)
+{
+    return m == NULL ? 0 : pkd_launches_per_step(m->dev);
+}
+
 const Config *engine_config(const LLMModel *m)
 {
     return m == NULL ? NULL : &m->config;

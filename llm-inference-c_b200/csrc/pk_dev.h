@@ -68,6 +68,10 @@ int pkd_trace(PkdCtx *ctx, unsigned long long *out, int cap);
 /* Last device error message ("" if none). */
 const char *pkd_error(const PkdCtx *ctx);
 
+/* Kernel launches per decode step (2 with the cooperative step kernel,
+ * phases + 1 otherwise). */
+int pkd_launches_per_step(const PkdCtx *ctx);
+
 #ifdef __cplusplus
 }
 #endif

@@ -884,6 +884,12 @@ extern "C" const char *pkd_error(const PkdCtx *c)
     return c ? c->msg : "";
 }
 
+extern "C" int pkd_launches_per_step(const PkdCtx *c)
+{
+    if (c == NULL) return 0;
+    return c->persistent ? 2 : c->nphases + 1;
+}
+
 extern "C" void pkd_destroy(PkdCtx *c)
 {
     if (c == NULL) return;

@@ -26,8 +26,8 @@ EXPORTS = [
     "engine_open", "engine_close", "engine_forward", "engine_config", "engine_file_context",
     "engine_format", "engine_tokenizer", "engine_kv_cache_bytes", "engine_description",
     "engine_is_stop_token", "engine_open_device", "engine_forward_greedy", "engine_last_error",
-    "engine_weight_bytes", "engine_generate_greedy", "engine_trace", "gguf_cuda_matvec", "gguf_cuda_dequantize_rows", "gguf_cuda_fp16_table",
-    "tokenizer_free",
+    "engine_weight_bytes", "engine_generate_greedy", "engine_trace", "engine_launches_per_step",
+    "gguf_cuda_matvec", "gguf_cuda_dequantize_rows", "gguf_cuda_fp16_table", "tokenizer_free",
 ]
 
 
@@ -115,6 +115,8 @@ def lib(path=LIB_PATH):
                                          ctypes.POINTER(ctypes.c_float)]
     L.engine_trace.restype = ctypes.c_int
     L.engine_trace.argtypes = [_P, _P, ctypes.c_int]
+    L.engine_launches_per_step.restype = ctypes.c_int
+    L.engine_launches_per_step.argtypes = [_P]
     L.gguf_cuda_matvec.restype = ctypes.c_int
     L.gguf_cuda_matvec.argtypes = [ctypes.POINTER(GGUFWeight), _P, _P, _P]
     L.gguf_cuda_dequantize_rows.restype = ctypes.c_int
@@ -185,6 +187,9 @@ class Engine:
 
     def weight_bytes(self):
         return lib().engine_weight_bytes(self.h)
+
+    def launches_per_step(self):
+        return lib().engine_launches_per_step(self.h)
 
     def file_context(self):
         return lib().engine_file_context(self.h)
