@@ -14,6 +14,7 @@
 #ifndef GGUF_CUDA_H
 #define GGUF_CUDA_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -54,6 +55,42 @@ int gguf_cuda_dequantize_rows(const GGUFWeight *weight, uint64_t row0, uint64_t 
  * payloads included.
  */
 int gguf_cuda_fp16_table(float *out65536, void *stream);
+
+/*
+ * Column limit of gguf_cuda_matvec_noalloc: its scratch holds x in integer
+ * form for at most this many columns (640 units of 64).
+ */
+#define GGUF_CUDA_NOALLOC_MAX_COLS 40960
+
+/*
+ * gguf_cuda_matvec without any device allocation, ever: the same product,
+ * bit for bit, as gguf_cuda_matvec, for callers that must not allocate
+ * device memory - a runtime that has reserved all free memory for its own
+ * pool, or a latency-critical loop that cannot take cudaMalloc's implicit
+ * synchronisation (gguf_cuda_matvec allocates a 4-byte error word on its
+ * first call on each device). This entry point has no counterpart in the
+ * reference.
+ *
+ * Scratch: a fixed 184,576-byte array in this library's device code (one
+ * per device, created when the device code is loaded): a 256-byte header
+ * whose first word is the tile kernel's error word, cleared by every call,
+ * then x in integer form, written by a staging kernel and read by every
+ * CTA of the tile kernel.
+ *
+ * - The first call on each device resolves the scratch address with that
+ *   device current (cudaGetSymbolAddress, which also loads the device code
+ *   when loading is lazy); make that first call before any stream capture.
+ * - cols > GGUF_CUDA_NOALLOC_MAX_COLS is rejected (returns 0, message in
+ *   `error`).
+ * - Calls on one device share the scratch: calls that may overlap in time
+ *   (different streams, not ordered by events) race and can return wrong
+ *   results. Serialise them, e.g. on one stream.
+ *
+ * Returns 1 when the kernels were enqueued on `stream`, 0 otherwise with a
+ * message in error[0 .. error_capacity) (may be NULL).
+ */
+int gguf_cuda_matvec_noalloc(const GGUFWeight *weight, const float *x, float *out, void *stream,
+                             char *error, size_t error_capacity);
 
 #ifdef __cplusplus
 }

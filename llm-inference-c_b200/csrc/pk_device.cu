@@ -415,6 +415,182 @@ extern "C" int gguf_cuda_fp16_table(float *out65536, void *stream)
     return cudaGetLastError() == cudaSuccess;
 }
 
+// ------------------------------------------------------------------ //
+// gguf_cuda_matvec_noalloc: the matvec with its scratch in device code //
+// ------------------------------------------------------------------ //
+
+// Scratch layout: [0, 256) header (word 0: error word of the tile kernel),
+// then the integer form of x for up to GGUF_CUDA_NOALLOC_MAX_COLS columns:
+// digits (XQ_UNIT_BYTES per unit) at NA_Q_OFF, group info (XG_UNIT_WORDS
+// words per unit) at NA_G_OFF - the layout stage_x writes to shared memory.
+constexpr int NA_UNITS = GGUF_CUDA_NOALLOC_MAX_COLS / 64;
+constexpr size_t NA_Q_OFF = 256;
+constexpr size_t NA_G_OFF = NA_Q_OFF + (size_t)NA_UNITS * XQ_UNIT_BYTES;
+constexpr size_t NA_SCRATCH_BYTES = NA_G_OFF + (size_t)NA_UNITS * XG_UNIT_WORDS * 4;
+static_assert(NA_SCRATCH_BYTES == 184576, "scratch size is stated in gguf_cuda.h");
+static_assert(NA_G_OFF % 16 == 0, "16-byte copies of the group info");
+
+static __device__ __align__(256) uint8_t na_scratch[NA_SCRATCH_BYTES];
+
+// One CTA: clear the error word, then write x's integer form into the
+// scratch (stage_x with global instead of shared destinations).
+__global__ void __launch_bounds__(DK_WARPS * 32, 1) na_stage_kernel(const __grid_constant__ Phase p, uint8_t *scratch)
+{
+    if (threadIdx.x == 0) *reinterpret_cast<int *>(scratch) = 0;
+    stage_x(p, nullptr, scratch + NA_Q_OFF, reinterpret_cast<float *>(scratch + NA_G_OFF));
+}
+
+// The matvec tiles of phase_kernel (same ring, same tiles, same row sums)
+// with x's integer form copied from the scratch instead of staged per CTA.
+__global__ void __launch_bounds__(DK_WARPS * 32, 1) na_matvec_kernel(const __grid_constant__ DecodeArgs a,
+                                                                      const uint8_t *scratch)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    const Phase &p = a.one;
+    const int W = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gw = blockIdx.x * W + warp, NW = gridDim.x * W;
+
+    Ring r;
+    r.bars = reinterpret_cast<uint64_t *>(smem) + warp * a.stages;
+    r.buf = smem + a.bar_bytes + a.xs_bytes + (size_t)warp * a.stages * a.stage_bytes;
+    r.stages = a.stages;
+    r.stage_bytes = a.stage_bytes;
+    r.issued = r.consumed = 0;
+    r.cp = r.ck = 0;
+    uint8_t *xq = smem + a.bar_bytes;
+    float *xg = reinterpret_cast<float *>(smem + a.bar_bytes + a.xq_bytes);
+
+    if (lane == 0) {
+        for (int s = 0; s < a.stages; s++) mbar_init(r.bars + s, 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    if (lane == 0) ring_fill(r, &p, 1, gw, NW);
+
+    const uint4 *sq = reinterpret_cast<const uint4 *>(scratch + NA_Q_OFF);
+    const uint4 *sg = reinterpret_cast<const uint4 *>(scratch + NA_G_OFF);
+    const int nq = p.nunits * XQ_UNIT_BYTES / 16, ng = p.nunits * XG_UNIT_WORDS * 4 / 16;
+    for (int i = threadIdx.x; i < nq; i += blockDim.x) reinterpret_cast<uint4 *>(xq)[i] = __ldcg(sq + i);
+    for (int i = threadIdx.x; i < ng; i += blockDim.x) reinterpret_cast<uint4 *>(xg)[i] = __ldcg(sg + i);
+    __syncthreads();
+
+    for (int t = gw; t < p.ntiles; t += NW) {
+        const uint32_t slot = r.consumed % (uint32_t)a.stages;
+        const uint32_t par = (r.consumed / (uint32_t)a.stages) & 1u;
+        const bool ok = __all_sync(0xFFFFFFFFu, !aborted(a.err) && mbar_wait_bounded(r.bars + slot, par));
+        if (!ok) {
+            if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_MV);
+        } else {
+            run_tile(p, t, r.buf + slot * a.stage_bytes, a.stage_bytes, xq, xg, nullptr, lane, nullptr);
+        }
+        __syncwarp();
+        r.consumed++;
+        if (lane == 0 && ok) ring_fill(r, &p, 1, gw, NW);
+    }
+    if (lane == 0 && r.issued != r.consumed) ring_drain(r);
+}
+
+static int na_fail(char *error, size_t cap, const char *msg)
+{
+    if (error != NULL && cap > 0) snprintf(error, cap, "%s", msg);
+    return 0;
+}
+
+// Device address of the scratch, resolved once per device with that device
+// current (cudaGetSymbolAddress allocates nothing; the array exists once
+// the device code is loaded).
+static uint8_t *na_scratch_addr(char *error, size_t cap)
+{
+    static uint8_t *addr[64] = {NULL};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        na_fail(error, cap, "gguf_cuda_matvec_noalloc: no current CUDA device.");
+        return NULL;
+    }
+    if (addr[dev] == NULL) {
+        void *p = NULL;
+        const cudaError_t e = cudaGetSymbolAddress(&p, na_scratch);
+        if (e != cudaSuccess || p == NULL) {
+            if (error != NULL && cap > 0) {
+                snprintf(error, cap, "gguf_cuda_matvec_noalloc: cudaGetSymbolAddress of the scratch failed on device %d: %s",
+                         dev, cudaGetErrorString(e));
+            }
+            return NULL;
+        }
+        addr[dev] = (uint8_t *)p;
+    }
+    return addr[dev];
+}
+
+extern "C" int gguf_cuda_matvec_noalloc(const GGUFWeight *weight, const float *x, float *out, void *stream,
+                                        char *error, size_t error_capacity)
+{
+    if (!weight_ok(weight) || x == NULL || out == NULL || (const void *)x == (const void *)out) {
+        return na_fail(error, error_capacity,
+                       "gguf_cuda_matvec_noalloc: invalid arguments (weight record, type, alignment, or x/out).");
+    }
+    if (weight->cols > (uint64_t)GGUF_CUDA_NOALLOC_MAX_COLS) {
+        if (error != NULL && error_capacity > 0) {
+            snprintf(error, error_capacity,
+                     "gguf_cuda_matvec_noalloc: %llu columns exceed the scratch limit of %d "
+                     "(GGUF_CUDA_NOALLOC_MAX_COLS); use gguf_cuda_matvec.",
+                     (unsigned long long)weight->cols, GGUF_CUDA_NOALLOC_MAX_COLS);
+        }
+        return 0;
+    }
+    uint8_t *scratch = na_scratch_addr(error, error_capacity);
+    if (scratch == NULL) return 0;
+    cudaStream_t st = (cudaStream_t)stream;
+    Phase p;
+    memset(&p, 0, sizeof(p));
+    p.kind = PH_MV;
+    p.pro = PRO_PLAIN;
+    p.epi = EPI_STORE;
+    p.nseg = 1;
+    p.seg[0].w = (const uint8_t *)weight->data;
+    p.seg[0].rb = weight->row_bytes;
+    p.seg[0].rows = (int)weight->rows;
+    p.seg[0].type = (int)weight->type;
+    p.seg[0].type2 = p.seg[0].type;
+    p.cols = (int)weight->cols;
+    p.xin = x;
+    p.y = out;
+    tile_phase(p, sm_count() * DK_WARPS, 8192, false);  // the tiles of gguf_cuda_matvec
+    Layout L;
+    if (!make_layout(L, p.nunits, stage_need(p), 0, 3)) {
+        if (weight->type != T_F32 && weight->type != T_F16) {
+            return na_fail(error, error_capacity, "gguf_cuda_matvec_noalloc: rows too long to stage.");
+        }
+        const int rows = (int)weight->rows;
+        mv_direct_kernel<<<(rows + 7) / 8, 256, 0, st>>>((const uint8_t *)weight->data, weight->row_bytes,
+                                                         (int)weight->type, rows, (int)weight->cols, x, out);
+    } else {
+        DecodeArgs a;
+        memset(&a, 0, sizeof(a));
+        a.one = p;
+        a.nphases = 1;
+        a.err = reinterpret_cast<int *>(scratch);
+        fill_args(a, L);
+        if (cudaFuncSetAttribute(na_matvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem) !=
+            cudaSuccess) {
+            return na_fail(error, error_capacity, "gguf_cuda_matvec_noalloc: shared-memory plan rejected.");
+        }
+        int grid = (p.ntiles + L.warps - 1) / L.warps;
+        if (grid > sm_count()) grid = sm_count();
+        if (grid < 1) grid = 1;
+        na_stage_kernel<<<1, DK_WARPS * 32, 0, st>>>(p, scratch);
+        na_matvec_kernel<<<grid, L.warps * 32, L.smem, st>>>(a, scratch);
+    }
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        if (error != NULL && error_capacity > 0) {
+            snprintf(error, error_capacity, "gguf_cuda_matvec_noalloc: launch failed: %s", cudaGetErrorString(e));
+        }
+        return 0;
+    }
+    return 1;
+}
+
 // ================================================================== //
 // Device half of the engine                                          //
 // ================================================================== //

@@ -27,7 +27,8 @@ EXPORTS = [
     "engine_format", "engine_tokenizer", "engine_kv_cache_bytes", "engine_description",
     "engine_is_stop_token", "engine_open_device", "engine_forward_greedy", "engine_last_error",
     "engine_weight_bytes", "engine_generate_greedy", "engine_trace", "engine_launches_per_step",
-    "gguf_cuda_matvec", "gguf_cuda_dequantize_rows", "gguf_cuda_fp16_table", "tokenizer_free",
+    "gguf_cuda_matvec", "gguf_cuda_dequantize_rows", "gguf_cuda_fp16_table", "gguf_cuda_matvec_noalloc",
+    "tokenizer_free",
 ]
 
 
@@ -124,6 +125,9 @@ def lib(path=LIB_PATH):
                                             ctypes.c_uint64, _P, _P]
     L.gguf_cuda_fp16_table.restype = ctypes.c_int
     L.gguf_cuda_fp16_table.argtypes = [_P, _P]
+    L.gguf_cuda_matvec_noalloc.restype = ctypes.c_int
+    L.gguf_cuda_matvec_noalloc.argtypes = [ctypes.POINTER(GGUFWeight), _P, _P, _P, ctypes.c_char_p,
+                                           ctypes.c_size_t]
     _lib = L
     return L
 
@@ -225,6 +229,13 @@ def make_weight(dev_ptr, qtype, rows, cols):
 
 def matvec(weight, x_ptr, y_ptr, stream=0):
     return lib().gguf_cuda_matvec(ctypes.byref(weight), x_ptr, y_ptr, stream)
+
+
+def matvec_noalloc(weight, x_ptr, y_ptr, stream=0):
+    """gguf_cuda_matvec_noalloc: returns (status, message)."""
+    err = ctypes.create_string_buffer(256)
+    rc = lib().gguf_cuda_matvec_noalloc(ctypes.byref(weight), x_ptr, y_ptr, stream, err, 256)
+    return rc, err.value.decode()
 
 
 def dequantize_rows(weight, row0, nrows, out_ptr, stream=0):
