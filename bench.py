@@ -46,9 +46,10 @@ WORKLOADS = {
 PUBLISHED_TOKS = 8.03  # reference, TinyLlama-1.1B-Chat Q4_K_M, 8 threads (documentation/PERFORMANCE.md:60)
 
 # DRAM bytes (read + write) of one decode-step launch of phase_kernel, from
-# the ncu capture summarised in profiles/phase_kernel_tinyllama_decode.md;
-# None until a capture exists for the workload.
-NCU_TRAFFIC = {}
+# the ncu capture summarised in profiles/phase_kernel_tinyllama_decode.md
+# (dram__bytes_read.sum + dram__bytes_write.sum); None for workloads without
+# a capture.
+NCU_TRAFFIC = {"tinyllama-1.1b-q4km": 635241216 + 3894016}
 FALLBACK_HBM_GBS = 6650.0
 MODEL_SEED = 1234
 
@@ -347,7 +348,7 @@ def main():
                     "path": "engine_forward (host logits) + host argmax",
                     "same_tokens_as_device_loop": bool(e2e_tokens_match)},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": NCU_TRAFFIC.get(wl["name"]),
+                         "frac": achieved / hbm, "traffic": NCU_TRAFFIC.get(wl["preset"]),
                          "kernel": kernel,
                          "duration": "CUDA events around the graph replays of the timed steps, per step",
                          "algorithmic_bytes_per_step": wbytes + kvb,
