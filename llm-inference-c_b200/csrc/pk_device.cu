@@ -4,9 +4,10 @@
 // phase_kernel runs phases of pk_stream.cuh:
 //   * persistent (cooperative launch, one CTA per SM): every phase of one
 //     decode step - per layer QKV(+RoPE, KV append) | attention | Wo(+residual)
-//     | gate/up(+SiLU*up) | down(+residual), then the logits - separated by
-//     grid barriers, while each warp's bulk-copy ring streams the following
-//     phases' weights across the barriers. One launch per token.
+//     | gate/up(+SiLU*up) | down(+residual), then the logits - handing
+//     activations over as tagged words (no grid barrier), while each warp's
+//     bulk-copy ring streams the following phases' weights. One launch per
+//     token.
 //   * one phase per launch: the standalone gguf_cuda_matvec, and the step as
 //     a sequence of launches (POCKET_CUDA_PERSISTENT=0).
 // Small kernels: bit-exact row decode, the fp16 table, the greedy hand-off
@@ -35,15 +36,15 @@ constexpr int SMEM_LIMIT = 227 * 1024;
 
 struct DecodeArgs {
     Phase one;             // the phase to run when `phases` is null
-    const Phase *phases;   // device array of nphases phases (persistent mode)
+    const Phase *phases;   // device array of nphases phases (one launch per step)
     int nphases;
-    int persistent;        // grid barrier between phases (cooperative launch)
     int stages, stage_bytes, bar_bytes, xq_bytes, xs_bytes, attn_bytes;
-    unsigned *bar;         // grid barrier counter, zeroed before the launch
-    const int *step;       // {token, pos, generated count, last token}
+    const int *step;       // {token, pos, generated count, last token, tag}
+    const float *rope_cs;  // RoPE cos/sin table [position][rope_dim]
+    int rope_dim;
     int *err;
-    unsigned long long *trace;  // optional, CTA 0: %globaltimer at start, then per phase after
-                                //   staging x, after its work, after its barrier
+    unsigned long long *trace;  // optional, CTA 0: %globaltimer at start, then per phase: after
+                                //   staging x, after its work, and again at its end
 };
 
 __device__ __forceinline__ unsigned long long global_ns()
@@ -53,33 +54,12 @@ __device__ __forceinline__ unsigned long long global_ns()
     return t;
 }
 
-__device__ __forceinline__ bool aborted(const int *err)
-{
-    return (*(volatile const int *)err & (ERR_TIMEOUT_MV | ERR_TIMEOUT_BARRIER)) != 0;
-}
-
-// All CTAs of the grid: arrive, then wait (bounded) for the others.
-__device__ __forceinline__ void grid_barrier(unsigned *bar, unsigned target, int *err)
-{
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(bar, 1u);
-        if (ld_acquire(bar) < target) {
-            const long long t0 = clock64();
-            while (ld_acquire(bar) < target) {
-                if (aborted(err)) break;
-                if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
-                    atomicOr(err, ERR_TIMEOUT_BARRIER);
-                    break;
-                }
-            }
-        }
-        __threadfence();
-    }
-    __syncthreads();
-}
-
+// The decode step (or one phase of it). The phases run in order in every
+// CTA, with no grid-wide barrier: inputs are tagged words that each CTA
+// polls, so a CTA enters a phase when the words it needs carry this step's
+// tag, and skips a phase in which it has no tile or item. All CTAs must be
+// resident together (cooperative launch), since consumers wait on producers
+// in other CTAs; every wait is bounded.
 __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_constant__ DecodeArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -87,6 +67,8 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
     const int nph = a.phases != nullptr ? a.nphases : 1;
     const int W = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gw = blockIdx.x * W + warp, NW = gridDim.x * W;
+    const uint32_t tag = a.step != nullptr ? (uint32_t)a.step[4] : 0u;
+    const bool tracing = a.trace != nullptr && blockIdx.x == 0;
 
     Ring r;
     r.bars = reinterpret_cast<uint64_t *>(smem) + warp * a.stages;
@@ -100,6 +82,7 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
     float *xg = reinterpret_cast<float *>(smem + a.bar_bytes + a.xq_bytes);
     float *att = reinterpret_cast<float *>(smem + a.bar_bytes);
     __shared__ unsigned long long cta_amax[2];
+    __shared__ float rope[256];  // this position's RoPE cos/sin pairs
 
     if (lane == 0) {
         for (int s = 0; s < a.stages; s++) mbar_init(r.bars + s, 1);
@@ -108,50 +91,63 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
     __syncwarp();
     // Weights do not depend on activations: start streaming at once.
     if (lane == 0) ring_fill(r, ph, nph, gw, NW);
-    if (a.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0) a.trace[0] = global_ns();
+    if (tracing && threadIdx.x == 0) a.trace[0] = global_ns();
+    if (a.rope_cs != nullptr) {
+        const float *row = a.rope_cs + (size_t)a.step[1] * a.rope_dim;
+        for (int i = threadIdx.x; i < a.rope_dim; i += blockDim.x) rope[i] = row[i];
+    }
 
     for (int pi = 0; pi < nph; pi++) {
         const Phase &p = ph[pi];
         if (p.kind == PH_MV) {
-            if (p.epi == EPI_LOGITS && threadIdx.x == 0) cta_amax[0] = cta_amax[1] = 0ull;
-            stage_x(p, a.step, xq, xg);
-            if (a.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0) a.trace[3 * pi + 1] = global_ns();
-            for (int t = gw; t < p.ntiles; t += NW) {
-                const uint32_t slot = r.consumed % (uint32_t)a.stages;
-                const uint32_t par = (r.consumed / (uint32_t)a.stages) & 1u;
-                // warp-uniform: run_tile's shuffles name every lane
-                const bool ok = __all_sync(0xFFFFFFFFu, !aborted(a.err) && mbar_wait_bounded(r.bars + slot, par));
-                if (!ok) {
-                    if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_MV);
-                } else {
-                    run_tile(p, t, r.buf + slot * a.stage_bytes, a.stage_bytes, xq, xg, a.step, lane, cta_amax);
+            if (cta_has_tiles(p, blockIdx.x, W, NW)) {
+                __syncthreads();  // every warp is done with the previous phase's x
+                if (p.epi == EPI_LOGITS && threadIdx.x == 0) cta_amax[0] = cta_amax[1] = 0ull;
+                stage_x(p, a.step, xq, xg, tag, a.err);  // ends with __syncthreads
+                if (tracing && threadIdx.x == 0) a.trace[3 * pi + 1] = global_ns();
+                for (int k = 0;; k++) {
+                    const int t = tile_at(p, gw, NW, k);
+                    if (t >= p.ntiles) break;
+                    const uint32_t slot = r.consumed % (uint32_t)a.stages;
+                    const uint32_t par = (r.consumed / (uint32_t)a.stages) & 1u;
+                    // warp-uniform: run_tile's shuffles name every lane
+                    const bool ok =
+                        __all_sync(0xFFFFFFFFu, !aborted(a.err) && mbar_wait_bounded(r.bars + slot, par));
+                    if (!ok) {
+                        if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_MV);
+                    } else {
+                        run_tile(p, t, r.buf + slot * a.stage_bytes, a.stage_bytes, xq, xg, a.step, rope, tag,
+                                 a.err, lane, cta_amax);
+                    }
+                    __syncwarp();
+                    r.consumed++;
+                    if (lane == 0 && ok) ring_fill(r, ph, nph, gw, NW);
                 }
-                __syncwarp();
-                r.consumed++;
-                if (lane == 0 && ok) ring_fill(r, ph, nph, gw, NW);
-            }
-            if (p.epi == EPI_LOGITS) {
-                __syncthreads();
-                if (threadIdx.x == 0) {
-                    if (cta_amax[0] != 0ull) atomicMax(p.amax, cta_amax[0]);
-                    if (cta_amax[1] != 0ull) atomicOr(p.amax + 1, 1ull);
+                if (p.epi == EPI_LOGITS) {
+                    __syncthreads();
+                    if (threadIdx.x == 0) {
+                        if (cta_amax[0] != 0ull) atomicMax(p.amax, cta_amax[0]);
+                        if (cta_amax[1] != 0ull) atomicOr(p.amax + 1, 1ull);
+                    }
                 }
+            } else if (tracing && threadIdx.x == 0) {
+                a.trace[3 * pi + 1] = global_ns();
             }
         } else {
             const int n = a.step[1] + 1;
             const int span = attn_span(n, p.n_kv, gridDim.x);
             const int items = p.n_kv * ((n + span - 1) / span);
-            if (a.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0) a.trace[3 * pi + 1] = global_ns();
-            for (int it = blockIdx.x; it < items; it += gridDim.x) {
-                attn_item(p, it % p.n_kv, it / p.n_kv, n, span, att);
+            if (tracing && threadIdx.x == 0) a.trace[3 * pi + 1] = global_ns();
+            for (int it = (blockIdx.x + gridDim.x - p.off % gridDim.x) % gridDim.x; it < items;
+                 it += gridDim.x) {
+                __syncthreads();  // the scratch aliases the previous phase's x
+                attn_item(p, it % p.n_kv, it / p.n_kv, n, span, att, tag, a.err);
             }
         }
-        if (a.trace != nullptr && blockIdx.x == 0) {
+        if (tracing) {
             __syncthreads();
-            if (threadIdx.x == 0) a.trace[3 * pi + 2] = global_ns();
+            if (threadIdx.x == 0) a.trace[3 * pi + 2] = a.trace[3 * pi + 3] = global_ns();
         }
-        if (a.persistent && pi + 1 < nph) grid_barrier(a.bar, (unsigned)(pi + 1) * gridDim.x, a.err);
-        if (a.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0) a.trace[3 * pi + 3] = global_ns();
     }
     if (lane == 0 && r.issued != r.consumed) ring_drain(r);
 }
@@ -174,6 +170,7 @@ __global__ void finish_kernel(int *step, unsigned long long *amax, int *tokens, 
     step[0] = tok < 0 ? 0 : tok;
     step[1] = step[1] + 1;
     step[2] = n + 1;
+    step[4] = step[4] + 1;  // the next step's tag
     amax[0] = 0ull;
     amax[1] = 0ull;
 }
@@ -300,15 +297,17 @@ static void fill_args(DecodeArgs &a, const Layout &L)
 }
 
 // Launch one phase as its own kernel on `st`.
-static int launch_phase(const Phase &p, const int *step, int *err, cudaStream_t st, int grid_cap)
+static int launch_phase(const Phase &p, const int *step, int *err, cudaStream_t st, int grid_cap,
+                        const float *rope_cs = nullptr, int rope_dim = 0)
 {
     DecodeArgs a;
     memset(&a, 0, sizeof(a));
     a.one = p;
     a.phases = nullptr;
     a.nphases = 1;
-    a.persistent = 0;
     a.step = step;
+    a.rope_cs = rope_cs;
+    a.rope_dim = rope_dim;
     a.err = err;
     Layout L;
     const int attn_floats = p.kind == PH_ATTN ? attn_scratch_floats(p.kv_mul, p.hs, p.nsplit_max) : 0;
@@ -437,7 +436,8 @@ static __device__ __align__(256) uint8_t na_scratch[NA_SCRATCH_BYTES];
 __global__ void __launch_bounds__(DK_WARPS * 32, 1) na_stage_kernel(const __grid_constant__ Phase p, uint8_t *scratch)
 {
     if (threadIdx.x == 0) *reinterpret_cast<int *>(scratch) = 0;
-    stage_x(p, nullptr, scratch + NA_Q_OFF, reinterpret_cast<float *>(scratch + NA_G_OFF));
+    stage_x(p, nullptr, scratch + NA_Q_OFF, reinterpret_cast<float *>(scratch + NA_G_OFF), 0u,
+            reinterpret_cast<int *>(scratch));
 }
 
 // The matvec tiles of phase_kernel (same ring, same tiles, same row sums)
@@ -481,7 +481,8 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) na_matvec_kernel(const __gri
         if (!ok) {
             if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_MV);
         } else {
-            run_tile(p, t, r.buf + slot * a.stage_bytes, a.stage_bytes, xq, xg, nullptr, lane, nullptr);
+            run_tile(p, t, r.buf + slot * a.stage_bytes, a.stage_bytes, xq, xg, nullptr, nullptr, 0u, a.err, lane,
+                     nullptr);
         }
         __syncwarp();
         r.consumed++;
@@ -602,8 +603,10 @@ struct PkdCtx {
     uint64_t arena_bytes;
     void *staging;  // pinned upload staging
     // run state
-    float *x, *xb, *q, *hb, *logits, *kc, *vc, *part, *norms, *rope_cs;
-    unsigned *count, *bar;
+    float *logits, *kc, *vc, *part, *norms, *rope_cs;
+    uint64_t *ll;  // tagged activations, per layer: q, k, v, attention out, x after Wo, hb, x after down
+    int rope_dim;
+    unsigned *count;
     int *step_d, *err_d, *tokens_d;
     int tokens_cap;
     unsigned long long *amax_d;
@@ -689,17 +692,49 @@ static void seg_of(MvSeg &s, const PkdCtx *c, const PkdTensor &t, int kind)
     s.kind = kind;
 }
 
-// The phases of one decode step.
+// Tagged activation words of one layer (offsets in words, each vector
+// starting on a 256-byte boundary).
+struct LLPlan {
+    size_t q, k, v, att, xmid, hb, xout, per_layer;
+};
+
+static LLPlan ll_plan(const PkdModel *m)
+{
+    auto r32 = [](size_t n) { return (n + 31) / 32 * 32; };
+    const size_t dim = (size_t)m->dim, kvd = dim / (size_t)m->n_heads * (size_t)m->n_kv_heads;
+    LLPlan p;
+    p.q = 0;
+    p.k = p.q + r32(dim);
+    p.v = p.k + r32(kvd);
+    p.att = p.v + r32(kvd);
+    p.xmid = p.att + r32(dim);
+    p.hb = p.xmid + r32(dim);
+    p.xout = p.hb + r32((size_t)m->hidden_dim);
+    p.per_layer = p.xout + r32(dim);
+    return p;
+}
+
+// The phases of one decode step. Each phase's work starts where the
+// previous phase's ended (tile rotation), so small phases do not all land
+// on the first CTAs.
 static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
 {
     const int L = m->n_layers, dim = m->dim, hs = m->dim / m->n_heads;
     const int kvd = hs * m->n_kv_heads, km = m->n_heads / m->n_kv_heads;
     const int nsplit = (m->seq_len + ATT_SUB - 1) / ATT_SUB;
+    const LLPlan lp = ll_plan(m);
     c->nphases = 5 * L + 1;
     c->phases = (Phase *)calloc((size_t)c->nphases, sizeof(Phase));
     if (c->phases == NULL) return 0;
     const int cap = 8192;
+    int acc = 0;  // the warp after the last tile of the previous phase
+    auto rotate = [&](Phase &p) {
+        p.off = acc;
+        acc = (acc + p.ntiles) % nw_total;
+    };
     for (int l = 0; l < L; l++) {
+        uint64_t *ll = c->ll + (size_t)l * lp.per_layer;
+        const uint64_t *xin = l == 0 ? nullptr : c->ll + (size_t)(l - 1) * lp.per_layer + lp.xout;
         Phase *P = c->phases + 5 * l;
         Phase &qkv = P[0], &att = P[1], &wo = P[2], &up = P[3], &dn = P[4];
         qkv.kind = PH_MV;
@@ -710,29 +745,33 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
         seg_of(qkv.seg[1], c, m->wk[l], KIND_K);
         seg_of(qkv.seg[2], c, m->wv[l], KIND_V);
         qkv.cols = dim;
-        qkv.xin = c->x;
+        qkv.xin_ll = xin;
         qkv.norm = c->norms + (size_t)(2 * l) * dim;
         qkv.eps = m->rms_eps;
         qkv.embd = c->arena + m->embd.offset;
         qkv.embd_rb = m->embd.row_bytes;
         qkv.embd_type = (int)m->embd.type;
-        qkv.xout = c->x;
-        qkv.q = c->q;
+        qkv.q_ll = ll + lp.q;
+        qkv.k_ll = ll + lp.k;
+        qkv.v_ll = ll + lp.v;
         qkv.kc = c->kc;
         qkv.vc = c->vc;
-        qkv.rope_cs = c->rope_cs;
         qkv.hs = hs;
         qkv.rope_dim = m->rope_dim;
         qkv.kv_dim = kvd;
         qkv.seq_len = m->seq_len;
         qkv.layer = l;
         tile_phase(qkv, nw_total, cap, true);
+        rotate(qkv);
 
         att.kind = PH_ATTN;
-        att.aq = c->q;
+        att.off = (acc + DK_WARPS - 1) / DK_WARPS;  // the CTAs after the QKV tiles
+        att.aq_ll = ll + lp.q;
+        att.ak_ll = ll + lp.k;
+        att.av_ll = ll + lp.v;
+        att.aout_ll = ll + lp.att;
         att.kc = c->kc;
         att.vc = c->vc;
-        att.aout = c->xb;
         att.part = c->part;
         att.count = c->count + (size_t)l * m->n_kv_heads;
         att.layer = l;
@@ -750,9 +789,14 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
         wo.nseg = 1;
         seg_of(wo.seg[0], c, m->wo[l], KIND_PLAIN);
         wo.cols = dim;
-        wo.xin = c->xb;
-        wo.y = c->x;
+        wo.xin_ll = ll + lp.att;
+        wo.res_ll = xin;  // null on layer 0: the embedding row
+        wo.embd = c->arena + m->embd.offset;
+        wo.embd_rb = m->embd.row_bytes;
+        wo.embd_type = (int)m->embd.type;
+        wo.y_ll = ll + lp.xmid;
         tile_phase(wo, nw_total, cap, false);
+        rotate(wo);
 
         up.kind = PH_MV;
         up.pro = PRO_NORM;
@@ -763,11 +807,12 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
         up.seg[0].rb2 = m->up[l].row_bytes;
         up.seg[0].type2 = (int)m->up[l].type;
         up.cols = dim;
-        up.xin = c->x;
+        up.xin_ll = ll + lp.xmid;
         up.norm = c->norms + (size_t)(2 * l + 1) * dim;
         up.eps = m->rms_eps;
-        up.y = c->hb;
+        up.y_ll = ll + lp.hb;
         tile_phase(up, nw_total, cap, false);
+        rotate(up);
 
         dn.kind = PH_MV;
         dn.pro = PRO_PLAIN;
@@ -775,9 +820,11 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
         dn.nseg = 1;
         seg_of(dn.seg[0], c, m->down[l], KIND_PLAIN);
         dn.cols = m->hidden_dim;
-        dn.xin = c->hb;
-        dn.y = c->x;
+        dn.xin_ll = ll + lp.hb;
+        dn.res_ll = ll + lp.xmid;
+        dn.y_ll = ll + lp.xout;
         tile_phase(dn, nw_total, cap, false);
+        rotate(dn);
     }
     Phase &lg = c->phases[5 * L];
     lg.kind = PH_MV;
@@ -786,12 +833,13 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
     lg.nseg = 1;
     seg_of(lg.seg[0], c, m->output, KIND_PLAIN);
     lg.cols = dim;
-    lg.xin = c->x;
+    lg.xin_ll = c->ll + (size_t)(L - 1) * lp.per_layer + lp.xout;
     lg.norm = c->norms + (size_t)(2 * L) * dim;
     lg.eps = m->rms_eps;
     lg.y = c->logits;
     lg.amax = c->amax_d;
     tile_phase(lg, nw_total, cap, false);
+    rotate(lg);
     return 1;
 }
 
@@ -800,14 +848,13 @@ static int record_step(PkdCtx *c)
 {
     cudaStream_t st = c->stream;
     if (c->persistent) {
-        if (cudaMemsetAsync(c->bar, 0, sizeof(unsigned), st) != cudaSuccess) return 0;
         DecodeArgs a;
         memset(&a, 0, sizeof(a));
         a.phases = c->phases_d;
         a.nphases = c->nphases;
-        a.persistent = 1;
-        a.bar = c->bar;
         a.step = c->step_d;
+        a.rope_cs = c->rope_cs;
+        a.rope_dim = c->rope_dim;
         a.err = c->err_d;
         a.trace = c->trace_d;
         fill_args(a, c->layout);
@@ -824,10 +871,9 @@ static int record_step(PkdCtx *c)
         cfg.numAttrs = 1;
         if (cudaLaunchKernelEx(&cfg, phase_kernel, a) != cudaSuccess) return 0;
     } else {
-        // One launch per phase; layer 0's QKV phase decodes the embedding
-        // itself, and CTA 0 writes it to x for the residual.
+        // One launch per phase (the tagged words are complete by then).
         for (int i = 0; i < c->nphases; i++) {
-            if (!launch_phase(c->phases[i], c->step_d, c->err_d, st, c->grid)) return 0;
+            if (!launch_phase(c->phases[i], c->step_d, c->err_d, st, c->grid, c->rope_cs, c->rope_dim)) return 0;
         }
     }
     finish_kernel<<<1, 1, 0, st>>>(c->step_d, c->amax_d, c->tokens_d, c->tokens_cap, c->err_d);
@@ -855,10 +901,9 @@ extern "C" int pkd_build(PkdCtx *c, const PkdModel *m, char *err, size_t cap)
     cudaSetDevice(c->device);
     sm_count();
     const size_t part = (size_t)m->n_heads * nsplit * (hs + 2);
-    if (cuda_fail(c, cudaMalloc(&c->x, dim * 4), "cudaMalloc", err, cap) ||
-        cuda_fail(c, cudaMalloc(&c->xb, dim * 4), "cudaMalloc", err, cap) ||
-        cuda_fail(c, cudaMalloc(&c->q, dim * 4), "cudaMalloc", err, cap) ||
-        cuda_fail(c, cudaMalloc(&c->hb, hid * 4), "cudaMalloc", err, cap) ||
+    const size_t ll_words = ll_plan(m).per_layer * (size_t)m->n_layers;
+    (void)hid;
+    if (cuda_fail(c, cudaMalloc(&c->ll, ll_words * 8), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->logits, (size_t)m->vocab_size * 4), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->kc, cache * 4), "cudaMalloc(KV cache)", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->vc, cache * 4), "cudaMalloc(KV cache)", err, cap) ||
@@ -866,14 +911,13 @@ extern "C" int pkd_build(PkdCtx *c, const PkdModel *m, char *err, size_t cap)
         cuda_fail(c, cudaMalloc(&c->norms, nnorm * 4), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->rope_cs, (size_t)m->seq_len * m->rope_dim * 4 + 4), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->count, (size_t)m->n_layers * m->n_kv_heads * 4), "cudaMalloc", err, cap) ||
-        cuda_fail(c, cudaMalloc(&c->bar, 16), "cudaMalloc", err, cap) ||
-        cuda_fail(c, cudaMalloc(&c->step_d, 16), "cudaMalloc", err, cap) ||
+        cuda_fail(c, cudaMalloc(&c->step_d, 32), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->err_d, 16), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->amax_d, 16), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->tokens_d, (size_t)m->seq_len * 4), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaEventCreate(&c->ev0), "cudaEventCreate", err, cap) ||
         cuda_fail(c, cudaEventCreate(&c->ev1), "cudaEventCreate", err, cap) ||
-        cuda_fail(c, cudaMallocHost(&c->step_h, 16), "cudaMallocHost", err, cap) ||
+        cuda_fail(c, cudaMallocHost(&c->step_h, 32), "cudaMallocHost", err, cap) ||
         cuda_fail(c, cudaMallocHost(&c->logits_h, (size_t)m->vocab_size * 4), "cudaMallocHost", err, cap) ||
         cuda_fail(c, cudaMallocHost(&c->err_h, 16), "cudaMallocHost", err, cap)) {
         return 0;
@@ -885,8 +929,12 @@ extern "C" int pkd_build(PkdCtx *c, const PkdModel *m, char *err, size_t cap)
     cudaMemsetAsync(c->vc, 0, cache * 4, st);
     cudaMemsetAsync(c->count, 0, (size_t)m->n_layers * m->n_kv_heads * 4, st);
     cudaMemsetAsync(c->err_d, 0, 16, st);
-    cudaMemsetAsync(c->step_d, 0, 16, st);
     cudaMemsetAsync(c->amax_d, 0, 16, st);
+    cudaMemsetAsync(c->ll, 0, ll_words * 8, st);  // tag 0: never a step's tag
+    memset(c->step_h, 0, 32);
+    c->step_h[4] = 1;  // the first step's tag
+    cudaMemcpyAsync(c->step_d, c->step_h, 32, cudaMemcpyHostToDevice, st);
+    c->rope_dim = m->rope_dim;
     // Norm weights decoded once on the device (src/gguf_forward.c:116-144).
     for (int l = 0; l <= m->n_layers; l++) {
         for (int k = 0; k < 2; k++) {
@@ -999,7 +1047,7 @@ static int run_step(PkdCtx *c, int token, int pos, int want_logits)
         return 0;
     }
     if (c->err_h[0] & ERR_NONFINITE) cudaMemsetAsync(c->err_d, 0, 4, st);  // a value, not a failure
-    if (c->err_h[0] & (ERR_TIMEOUT_MV | ERR_TIMEOUT_BARRIER)) {
+    if (c->err_h[0] & ERR_FATAL) {
         snprintf(c->msg, sizeof(c->msg), "decode step: device wait timed out (code %d)", c->err_h[0]);
         c->failed = 1;
         return 0;
@@ -1037,7 +1085,7 @@ extern "C" int pkd_generate_greedy(PkdCtx *c, int token, int pos, int n, int *ou
         c->failed = 1;
         return 0;
     }
-    if (c->err_h[0] & (ERR_TIMEOUT_MV | ERR_TIMEOUT_BARRIER)) {
+    if (c->err_h[0] & ERR_FATAL) {
         snprintf(c->msg, sizeof(c->msg), "generate: device wait timed out (code %d)", c->err_h[0]);
         c->failed = 1;
         return 0;
@@ -1075,8 +1123,8 @@ extern "C" void pkd_destroy(PkdCtx *c)
     if (c->graph) cudaGraphDestroy(c->graph);
     if (c->ev0) cudaEventDestroy(c->ev0);
     if (c->ev1) cudaEventDestroy(c->ev1);
-    void *dev[] = {c->arena, c->x, c->xb, c->q, c->hb, c->logits, c->kc, c->vc, c->part, c->norms,
-                   c->rope_cs, c->count, c->bar, c->step_d, c->err_d, c->amax_d, c->tokens_d, c->phases_d,
+    void *dev[] = {c->arena, c->ll, c->logits, c->kc, c->vc, c->part, c->norms,
+                   c->rope_cs, c->count, c->step_d, c->err_d, c->amax_d, c->tokens_d, c->phases_d,
                    c->trace_d};
     for (size_t i = 0; i < sizeof(dev) / sizeof(dev[0]); i++) {
         if (dev[i]) cudaFree(dev[i]);

@@ -7,10 +7,18 @@
 // TMA engine) of whole packed rows into the ring; the tiles a warp will
 // consume are known in advance for every phase, so in the persistent decode
 // kernel the ring keeps streaming the NEXT phases' weights while the warp
-// waits at a grid barrier. Weights never depend on activations.
+// waits for its inputs. Weights never depend on activations.
 //
 // Compute. x is staged once per phase and CTA in integer form (pk_quant.cuh);
 // each lane owns 64-column units; a row's units are summed over the warp.
+//
+// Hand-offs. Activations that one phase produces and the next consumes are
+// "tagged words" (the scheme of NCCL's LL protocol): one 64-bit word per
+// value, the step's tag in the high half and the float in the low half,
+// stored and loaded as single 64-bit accesses. A consumer polls exactly the
+// words it needs until they carry the current step's tag, so there is no
+// grid-wide barrier between phases: a phase starts in a CTA as soon as its
+// own inputs have landed, and a CTA with no work in a phase skips it.
 #pragma once
 #include <cuda_runtime.h>
 #include <math.h>
@@ -26,7 +34,8 @@ enum { PH_MV = 0, PH_ATTN = 1 };
 enum { PRO_PLAIN = 0, PRO_NORM = 1, PRO_EMBED_NORM = 2 };
 enum { EPI_STORE = 0, EPI_ADD = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
 enum { KIND_PLAIN = 0, KIND_Q = 1, KIND_K = 2, KIND_V = 3 };
-enum { ERR_TIMEOUT_MV = 1, ERR_TIMEOUT_BARRIER = 2, ERR_NONFINITE = 4 };
+enum { ERR_TIMEOUT_MV = 1, ERR_TIMEOUT_WAIT = 2, ERR_NONFINITE = 4 };
+constexpr int ERR_FATAL = ERR_TIMEOUT_MV | ERR_TIMEOUT_WAIT;
 
 // ------------------------------------------------------------------ //
 // PTX helpers                                                        //
@@ -93,6 +102,94 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned *p)
     return v;
 }
 
+__device__ __forceinline__ bool aborted(const int *err)
+{
+    return (*(volatile const int *)err & ERR_FATAL) != 0;
+}
+
+// ------------------------------------------------------------------ //
+// Tagged words                                                       //
+// ------------------------------------------------------------------ //
+
+__device__ __forceinline__ void st_ll(uint64_t *p, float v, uint32_t tag)
+{
+    const uint64_t w = ((uint64_t)tag << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_ll(const uint64_t *p)
+{
+    uint64_t w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+// Two words from a 16-byte aligned address (each one a single access).
+__device__ __forceinline__ void ld_ll2(const uint64_t *p, uint64_t &a, uint64_t &b)
+{
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+__device__ __forceinline__ bool ll_is(uint64_t w, uint32_t tag)
+{
+    return (uint32_t)(w >> 32) == tag;
+}
+
+__device__ __forceinline__ float ll_val(uint64_t w)
+{
+    return __uint_as_float((uint32_t)w);
+}
+
+// Value of the tagged word at p once it carries `tag` (bounded wait; on a
+// timeout the error word is set and whatever is there is returned).
+__device__ __forceinline__ float ll_read(const uint64_t *p, uint32_t tag, int *err)
+{
+    uint64_t w = ld_ll(p);
+    if (ll_is(w, tag)) return ll_val(w);
+    const long long t0 = clock64();
+    do {
+        w = ld_ll(p);
+        if (ll_is(w, tag)) break;
+        if (aborted(err)) break;
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+            atomicOr(err, ERR_TIMEOUT_WAIT);
+            break;
+        }
+    } while (true);
+    return ll_val(w);
+}
+
+// Values of the n (<= 8) tagged words at p (64-byte aligned when n == 8),
+// waiting (bounded) until all carry `tag`; v[e] = 0 for e >= n.
+__device__ __forceinline__ void ll_read8(const uint64_t *p, int n, uint32_t tag, float *v, int *err)
+{
+    uint64_t w[8];
+    long long t0 = 0;
+    bool first = true;
+    for (;;) {
+        if (n >= 8) {
+#pragma unroll
+            for (int k = 0; k < 4; k++) ld_ll2(p + 2 * k, w[2 * k], w[2 * k + 1]);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) w[e] = e < n ? ld_ll(p + e) : ((uint64_t)tag << 32);
+        }
+        bool ok = true;
+#pragma unroll
+        for (int e = 0; e < 8; e++) ok = ok && ll_is(w[e], tag);
+        if (ok || aborted(err)) break;
+        if (first) {
+            t0 = clock64();
+            first = false;
+        } else if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+            atomicOr(err, ERR_TIMEOUT_WAIT);
+            break;
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; e++) v[e] = e < n ? ll_val(w[e]) : 0.0f;
+}
+
 __device__ __forceinline__ float warp_sum(float v)
 {
 #pragma unroll
@@ -127,28 +224,47 @@ struct MvSeg {
 
 struct Phase {
     int kind, pro, epi;
+    int off;              // work rotation: tile t goes to warp (t + off) % warps,
+                          // attention item i to CTA (i + off) % CTAs
     // fused matvec
     MvSeg seg[3];
     int nseg, ntiles, cols, nunits;
-    const float *xin;     // input vector (PRO_PLAIN / PRO_NORM)
-    const float *norm;    // RMSNorm weights (PRO_NORM / PRO_EMBED_NORM)
+    const float *xin;         // input vector as floats (device seam), or
+    const uint64_t *xin_ll;   // as tagged words (decode step)
+    const float *norm;        // RMSNorm weights (PRO_NORM / PRO_EMBED_NORM)
     float eps;
-    float *y;             // output / residual / SwiGLU result / logits
-    const uint8_t *embd;  // PRO_EMBED_NORM: embedding table, row bytes, type
-    uint64_t embd_rb;
+    float *y;                 // float output (EPI_STORE of the seam, EPI_LOGITS)
+    uint64_t *y_ll;           // tagged output (EPI_STORE / EPI_ADD / EPI_SWIGLU)
+    const uint64_t *res_ll;   // EPI_ADD residual (null: the embedding row)
+    const uint8_t *embd;      // embedding table, row bytes, type (PRO_EMBED_NORM,
+    uint64_t embd_rb;         //   and the residual of layer 0's EPI_ADD)
     int embd_type;
-    float *xout;          // PRO_EMBED_NORM: CTA 0 stores the raw embedding row here
-    float *q, *kc, *vc;   // EPI_QKV
-    const float *rope_cs;
+    uint64_t *q_ll, *k_ll, *v_ll;  // EPI_QKV outputs (tagged)
+    float *kc, *vc;                // KV cache (EPI_QKV appends, attention reads)
     int hs, rope_dim, kv_dim, seq_len, layer;
     unsigned long long *amax;  // EPI_LOGITS: [0] packed argmax, [1] non-finite flag
     // attention
-    const float *aq;
-    float *aout, *part;
+    const uint64_t *aq_ll, *ak_ll, *av_ll;  // q, and this position's k, v
+    uint64_t *aout_ll;
+    float *part;
     unsigned *count;
     int kv_mul, n_kv, nsplit_max;
     float scale;
 };
+
+// Tile k (0, 1, ...) of warp gw among nw warps (>= ntiles: none).
+__host__ __device__ inline int tile_at(const Phase &p, int gw, int nw, int k)
+{
+    return (gw + nw - p.off % nw) % nw + k * nw;
+}
+
+// Does any of the W warps of CTA b own a tile of p?
+__host__ __device__ inline bool cta_has_tiles(const Phase &p, int b, int W, int nw)
+{
+    if (p.ntiles <= 0) return false;
+    const int f0 = (b * W + nw - p.off % nw) % nw;
+    return f0 + W > nw || f0 < p.ntiles;
+}
 
 // ------------------------------------------------------------------ //
 // Bulk-copy ring                                                     //
@@ -219,7 +335,7 @@ __device__ __forceinline__ void ring_fill(Ring &r, const Phase *ph, int nph, int
 {
     while (r.issued - r.consumed < (uint32_t)r.stages && r.cp < nph) {
         const Phase &p = ph[r.cp];
-        const int t = gw + r.ck * nw_total;
+        const int t = p.kind == PH_MV ? tile_at(p, gw, nw_total, r.ck) : 0;
         if (p.kind != PH_MV || t >= p.ntiles) {
             r.cp++;
             r.ck = 0;
@@ -258,8 +374,10 @@ __device__ __forceinline__ float pow2f(int k)
 //
 // Four threads own a 32-column group (eight columns each, kept in
 // registers from one load to the digits), so there are no per-element
-// round trips and only two-step shuffles within the quad.
-__device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t *xq, float *xg)
+// round trips and only two-step shuffles within the quad. Tagged inputs
+// (xin_ll) are polled until they carry `tag`.
+__device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t *xq, float *xg, uint32_t tag,
+                                        int *err)
 {
     constexpr int MAXP = 4;  // groups per quad per pass
     __shared__ float red[32];
@@ -282,6 +400,8 @@ __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t
             for (int e = 0; e < 8; e++) {
                 if (c0 + e < n) v[e] = decode_col(etype, erow, c0 + e);
             }
+        } else if (p.xin_ll != nullptr) {
+            if (c0 < n) ll_read8(p.xin_ll + c0, min(8, n - c0), tag, v, err);
         } else if (c0 + 8 <= n) {
             // x was written by other CTAs (possibly in this launch): read L2
             const float4 a = __ldcg(reinterpret_cast<const float4 *>(xin + c0));
@@ -325,12 +445,6 @@ __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t
         for (int k = 0; k < MAXP; k++) {
             const int g = base + quad + k * nquads;
             load8(32 * g + 8 * t, v[k]);  // beyond ng: zeros (c0 >= n)
-            if (pro == PRO_EMBED_NORM && blockIdx.x == 0 && g < ng) {
-#pragma unroll
-                for (int e = 0; e < 8; e++) {
-                    if (32 * g + 8 * t + e < n) p.xout[32 * g + 8 * t + e] = v[k][e];
-                }
-            }
 #pragma unroll
             for (int e = 0; e < 8; e++) ss = fmaf(v[k][e], v[k][e], ss);
         }
@@ -484,9 +598,11 @@ __device__ __forceinline__ float2 tile_dispatch(int type, const uint8_t *ra, uin
 }
 
 // Compute tile t of phase p from its ring slot and apply the epilogue.
+// rope: this position's cos/sin pairs (EPI_QKV); tag: the step's tag for
+// tagged outputs and the residual.
 __device__ __forceinline__ void run_tile(const Phase &p, int t, const uint8_t *buf, int stage_bytes,
-                                         const uint8_t *xq, const float *xg, const int *step, int lane,
-                                         unsigned long long *cta_amax)
+                                         const uint8_t *xq, const float *xg, const int *step, const float *rope,
+                                         uint32_t tag, int *err, int lane, unsigned long long *cta_amax)
 {
     const MvSeg &s = find_seg(p, t);
     const int r0 = (t - s.tile0) * s.R;
@@ -519,15 +635,19 @@ __device__ __forceinline__ void run_tile(const Phase &p, int t, const uint8_t *b
             if (s.kind != KIND_V && (d & ~1) < p.rope_dim) {
                 // rope_head, src/gguf_forward.c:50-66 (cos/sin from the host table)
                 const int i0 = d & ~1;
-                const float c = p.rope_cs[(size_t)pos * p.rope_dim + i0];
-                const float sn = p.rope_cs[(size_t)pos * p.rope_dim + i0 + 1];
+                const float c = rope[i0], sn = rope[i0 + 1];
                 const float v0 = (d & 1) ? other : va, v1 = (d & 1) ? va : other;
                 v = (d & 1) ? __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, c))
                             : __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, sn));
             }
-            const size_t cache_row = ((size_t)p.layer * p.seq_len + pos) * p.kv_dim;
-            float *dst = s.kind == KIND_Q ? p.q + r : (s.kind == KIND_K ? p.kc : p.vc) + cache_row + r;
-            *dst = v;
+            if (s.kind == KIND_Q) {
+                st_ll(p.q_ll + r, v, tag);
+            } else {
+                // the cache row serves later steps; this step reads the tagged copy
+                const size_t cache_row = ((size_t)p.layer * p.seq_len + pos) * p.kv_dim;
+                (s.kind == KIND_K ? p.kc : p.vc)[cache_row + r] = v;
+                st_ll((s.kind == KIND_K ? p.k_ll : p.v_ll) + r, v, tag);
+            }
         }
     } else if (p.epi == EPI_LOGITS) {
         // logits + greedy argmax: the warp's best (value, lowest row) goes to
@@ -550,12 +670,20 @@ __device__ __forceinline__ void run_tile(const Phase &p, int t, const uint8_t *b
         if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) cta_amax[1] = 1ull;
         if (lane == 0 && key != 0ull) atomicMax(cta_amax, key);
     } else if (lane < nr) {
-        if (p.epi == EPI_STORE) {
-            p.y[r] = va;
-        } else if (p.epi == EPI_ADD) {
-            p.y[r] = __fadd_rn(__ldcg(p.y + r), va);
+        float out = va;
+        if (p.epi == EPI_ADD) {
+            // residual stream, src/gguf_forward.c:274-276,297-299 (layer 0's input
+            // is the embedding row, decoded again here)
+            const float res = p.res_ll != nullptr ? ll_read(p.res_ll + r, tag, err)
+                                                  : decode_col(p.embd_type, p.embd + (size_t)step[0] * p.embd_rb, r);
+            out = __fadd_rn(res, va);
         } else if (p.epi == EPI_SWIGLU) {
-            p.y[r] = __fmul_rn(__fdiv_rn(va, __fadd_rn(1.0f, expf(-va))), vb);
+            out = __fmul_rn(__fdiv_rn(va, __fadd_rn(1.0f, expf(-va))), vb);
+        }
+        if (p.y_ll != nullptr) {
+            st_ll(p.y_ll + r, out, tag);
+        } else {
+            p.y[r] = out;
         }
     }
 }
@@ -597,8 +725,11 @@ __device__ __forceinline__ void cp_async4(float *dst, const float *src)
 // outputs directly; otherwise the last item of the group to finish merges the
 // splits' (max, sum, weighted V) partials in split order.
 // src/gguf_forward.c:228-267 with the softmax of src/transformer.c:85-109.
+// q and this position's K/V row are read as tagged words (the QKV phase of
+// the same step wrote them); earlier positions come from the KV cache.
 // All threads of the CTA.
-__device__ __forceinline__ void attn_item(const Phase &p, int g, int s, int n, int span, float *sm)
+__device__ __forceinline__ void attn_item(const Phase &p, int g, int s, int n, int span, float *sm, uint32_t tag,
+                                          int *err)
 {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     const int hs = p.hs, km = p.kv_mul, kvd = p.kv_dim;
@@ -621,15 +752,20 @@ __device__ __forceinline__ void attn_item(const Phase &p, int g, int s, int n, i
         float *K = sK + buf * ATT_SUB * ks, *V = sV + buf * ATT_SUB * hs;
         for (int i = tid; i < tc * hs; i += blockDim.x) {
             const int t = i / hs, d = i % hs;
-            const size_t off = lbase + (size_t)(tb + t) * kvd + d;
-            cp_async4(K + t * ks + d, p.kc + off);
-            cp_async4(V + t * hs + d, p.vc + off);
+            if (tb + t == n - 1) {  // this step's row
+                K[t * ks + d] = ll_read(p.ak_ll + (size_t)g * hs + d, tag, err);
+                V[t * hs + d] = ll_read(p.av_ll + (size_t)g * hs + d, tag, err);
+            } else {
+                const size_t off = lbase + (size_t)(tb + t) * kvd + d;
+                cp_async4(K + t * ks + d, p.kc + off);
+                cp_async4(V + t * hs + d, p.vc + off);
+            }
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
     load_tile(0, 0);
     for (int i = tid; i < km * hs; i += blockDim.x) {
-        qs[i] = __ldcg(p.aq + (size_t)g * km * hs + i);
+        qs[i] = ll_read(p.aq_ll + (size_t)g * km * hs + i, tag, err);
         orun[i] = 0.0f;
     }
     if (tid < km) {
@@ -683,7 +819,9 @@ __device__ __forceinline__ void attn_item(const Phase &p, int g, int s, int n, i
         __syncthreads();
     }
     if (nsplit == 1) {
-        for (int i = tid; i < km * hs; i += blockDim.x) p.aout[(size_t)g * km * hs + i] = orun[i] / lrun[i / hs];
+        for (int i = tid; i < km * hs; i += blockDim.x) {
+            st_ll(p.aout_ll + (size_t)g * km * hs + i, orun[i] / lrun[i / hs], tag);
+        }
         return;
     }
     const int stride = hs + 2;
@@ -724,7 +862,7 @@ __device__ __forceinline__ void attn_item(const Phase &p, int g, int s, int n, i
             float O = 0.0f;
 #pragma unroll 4
             for (int j = 0; j < nsplit; j++) O = fmaf(__ldcg(P + (size_t)j * stride), w[j], O);
-            p.aout[(size_t)(g * km + h) * hs + d] = O;
+            st_ll(p.aout_ll + (size_t)(g * km + h) * hs + d, O, tag);
         }
         if (tid == 0) p.count[g] = 0;
     }
