@@ -30,7 +30,7 @@
 
 namespace pk {
 
-constexpr int DK_WARPS = 8;       // warps per CTA of phase_kernel
+constexpr int DK_WARPS = 12;      // warps per CTA of phase_kernel
 constexpr int RMAX = 8;           // rows per tile (per matrix)
 constexpr int SMEM_LIMIT = 227 * 1024;
 
@@ -60,6 +60,7 @@ __device__ __forceinline__ unsigned long long global_ns()
 // tag, and skips a phase in which it has no tile or item. All CTAs must be
 // resident together (cooperative launch), since consumers wait on producers
 // in other CTAs; every wait is bounded.
+template <unsigned MASK>
 __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_constant__ DecodeArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -116,8 +117,8 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
                     if (!ok) {
                         if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_MV);
                     } else {
-                        run_tile(p, t, r.buf + slot * a.stage_bytes, a.stage_bytes, xq, xg, a.step, rope, tag,
-                                 a.err, lane, cta_amax);
+                        run_tile<MASK>(p, t, r.buf + slot * a.stage_bytes, xq, xg, a.step, rope, tag, a.err, lane,
+                                       cta_amax);
                     }
                     __syncwarp();
                     r.consumed++;
@@ -134,14 +135,14 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
                 a.trace[3 * pi + 1] = global_ns();
             }
         } else {
-            const int n = a.step[1] + 1;
-            const int span = attn_span(n, p.n_kv, gridDim.x);
-            const int items = p.n_kv * ((n + span - 1) / span);
+            const int n = a.step[1] + 1, nh = p.n_kv * p.kv_mul;
+            const int span = attn_span(n, p.nsplit_max);
+            const int nsplit = (n + span - 1) / span;
             if (tracing && threadIdx.x == 0) a.trace[3 * pi + 1] = global_ns();
-            for (int it = (blockIdx.x + gridDim.x - p.off % gridDim.x) % gridDim.x; it < items;
+            for (int it = (blockIdx.x + gridDim.x - p.off % gridDim.x) % gridDim.x; it < nh * nsplit;
                  it += gridDim.x) {
                 __syncthreads();  // the scratch aliases the previous phase's x
-                attn_item(p, it % p.n_kv, it / p.n_kv, n, span, att, tag, a.err);
+                attn_item(p, it % nh, it / nh, nsplit, n, span, att, tag, a.err);
             }
         }
         if (tracing) {
@@ -173,6 +174,52 @@ __global__ void finish_kernel(int *step, unsigned long long *amax, int *tokens, 
     step[4] = step[4] + 1;  // the next step's tag
     amax[0] = 0ull;
     amax[1] = 0ull;
+}
+
+typedef void (*PhaseFn)(DecodeArgs);
+
+// The compiled phase_kernel variants: one per format for the device seam,
+// and format sets of common GGUF mixes for the decode step (Q4_K_M:
+// Q4_K + Q6_K; K-quant mixes with Q5_K and Q8_0; legacy Q4_0/Q8_0; float),
+// then everything.
+struct Variant {
+    unsigned mask;
+    PhaseFn fn;
+};
+#define PK_VARIANT(M) {(M), phase_kernel<(M)>}
+static const Variant VARIANTS[] = {
+    PK_VARIANT(tbit(T_Q4_K)),
+    PK_VARIANT(tbit(T_Q5_K)),
+    PK_VARIANT(tbit(T_Q6_K)),
+    PK_VARIANT(tbit(T_Q4_0)),
+    PK_VARIANT(tbit(T_Q8_0)),
+    PK_VARIANT(tbit(T_F32)),
+    PK_VARIANT(tbit(T_F16)),
+    PK_VARIANT(tbit(T_Q4_K) | tbit(T_Q6_K)),
+    PK_VARIANT(tbit(T_Q4_K) | tbit(T_Q5_K) | tbit(T_Q6_K) | tbit(T_Q8_0)),
+    PK_VARIANT(tbit(T_Q4_0) | tbit(T_Q8_0)),
+    PK_VARIANT(tbit(T_F32) | tbit(T_F16)),
+    PK_VARIANT(FMT_ALL),
+};
+#undef PK_VARIANT
+
+// The first (smallest) variant that has every format in `need`.
+static PhaseFn pick_variant(unsigned need)
+{
+    const int n = (int)(sizeof(VARIANTS) / sizeof(VARIANTS[0]));
+    for (int i = 0; i < n; i++) {
+        if ((need & ~VARIANTS[i].mask) == 0u) return VARIANTS[i].fn;
+    }
+    return VARIANTS[n - 1].fn;
+}
+
+// Formats a phase's matrices use.
+static unsigned phase_formats(const Phase &p)
+{
+    unsigned need = 0u;
+    if (p.kind != PH_MV) return need;
+    for (int i = 0; i < p.nseg; i++) need |= tbit(p.seg[i].type);
+    return need;
 }
 
 __global__ void dequant_kernel(const uint8_t *w, uint64_t rb, int type, uint64_t rows, uint64_t cols,
@@ -227,15 +274,13 @@ static int sm_count()
 // and stages of at most `cap` bytes. even: tiles hold whole RoPE pairs.
 static void tile_phase(Phase &p, int nw_total, int cap, bool even)
 {
-    const int mult = p.epi == EPI_SWIGLU ? 2 : 1;
     int total_rows = 0;
     for (int i = 0; i < p.nseg; i++) total_rows += p.seg[i].rows;
     const int r_par = (total_rows + nw_total - 1) / nw_total;
     int t = 0;
     for (int i = 0; i < p.nseg; i++) {
         MvSeg &s = p.seg[i];
-        const uint64_t rbmax = s.w2 != nullptr && s.rb2 > s.rb ? s.rb2 : s.rb;
-        int R = (int)((uint64_t)(cap / mult - 32) / rbmax);
+        int R = (int)((uint64_t)(cap - 32) / s.rb);
         if (R > r_par) R = r_par;
         if (even && (R & 1)) R++;
         if (R < (even ? 2 : 1)) R = even ? 2 : 1;
@@ -251,12 +296,10 @@ static void tile_phase(Phase &p, int nw_total, int cap, bool even)
 // Bytes a stage needs to hold a tile of the phase.
 static int stage_need(const Phase &p)
 {
-    const int mult = p.epi == EPI_SWIGLU ? 2 : 1;
     int need = 0;
     for (int i = 0; i < p.nseg; i++) {
         const MvSeg &s = p.seg[i];
-        const uint64_t rbmax = s.w2 != nullptr && s.rb2 > s.rb ? s.rb2 : s.rb;
-        const int b = (int)(((uint64_t)s.R * rbmax + 32 + 127) / 128 * 128) * mult;
+        const int b = (int)(((uint64_t)s.R * s.rb + 32 + 127) / 128 * 128);
         if (b > need) need = b;
     }
     return need;
@@ -298,8 +341,9 @@ static void fill_args(DecodeArgs &a, const Layout &L)
 
 // Launch one phase as its own kernel on `st`.
 static int launch_phase(const Phase &p, const int *step, int *err, cudaStream_t st, int grid_cap,
-                        const float *rope_cs = nullptr, int rope_dim = 0)
+                        const float *rope_cs = nullptr, int rope_dim = 0, PhaseFn fn = nullptr)
 {
+    if (fn == nullptr) fn = pick_variant(phase_formats(p));
     DecodeArgs a;
     memset(&a, 0, sizeof(a));
     a.one = p;
@@ -310,12 +354,11 @@ static int launch_phase(const Phase &p, const int *step, int *err, cudaStream_t 
     a.rope_dim = rope_dim;
     a.err = err;
     Layout L;
-    const int attn_floats = p.kind == PH_ATTN ? attn_scratch_floats(p.kv_mul, p.hs, p.nsplit_max) : 0;
+    const int attn_floats = p.kind == PH_ATTN ? attn_scratch_floats(p.hs, DK_WARPS) : 0;
     const int stage = p.kind == PH_MV ? stage_need(p) : 128;
     if (!make_layout(L, p.kind == PH_MV ? p.nunits : 1, stage, attn_floats, 3)) return 0;
     fill_args(a, L);
-    if (cudaFuncSetAttribute(phase_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem) != cudaSuccess)
         return 0;
     int grid = grid_cap;
     if (p.kind == PH_MV) {
@@ -323,7 +366,7 @@ static int launch_phase(const Phase &p, const int *step, int *err, cudaStream_t 
         if (want < grid) grid = want;
     }
     if (grid < 1) grid = 1;
-    phase_kernel<<<grid, L.warps * 32, L.smem, st>>>(a);
+    fn<<<grid, L.warps * 32, L.smem, st>>>(a);
     return cudaGetLastError() == cudaSuccess;
 }
 
@@ -377,7 +420,6 @@ extern "C" int gguf_cuda_matvec(const GGUFWeight *weight, const float *x, float 
     p.seg[0].rb = weight->row_bytes;
     p.seg[0].rows = (int)weight->rows;
     p.seg[0].type = (int)weight->type;
-    p.seg[0].type2 = p.seg[0].type;
     p.cols = (int)weight->cols;
     p.xin = x;
     p.y = out;
@@ -481,7 +523,7 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) na_matvec_kernel(const __gri
         if (!ok) {
             if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_MV);
         } else {
-            run_tile(p, t, r.buf + slot * a.stage_bytes, a.stage_bytes, xq, xg, nullptr, nullptr, 0u, a.err, lane,
+            run_tile<FMT_ALL>(p, t, r.buf + slot * a.stage_bytes, xq, xg, nullptr, nullptr, 0u, a.err, lane,
                      nullptr);
         }
         __syncwarp();
@@ -552,7 +594,6 @@ extern "C" int gguf_cuda_matvec_noalloc(const GGUFWeight *weight, const float *x
     p.seg[0].rb = weight->row_bytes;
     p.seg[0].rows = (int)weight->rows;
     p.seg[0].type = (int)weight->type;
-    p.seg[0].type2 = p.seg[0].type;
     p.cols = (int)weight->cols;
     p.xin = x;
     p.y = out;
@@ -604,7 +645,7 @@ struct PkdCtx {
     void *staging;  // pinned upload staging
     // run state
     float *logits, *kc, *vc, *part, *norms, *rope_cs;
-    uint64_t *ll;  // tagged activations, per layer: q, k, v, attention out, x after Wo, hb, x after down
+    uint64_t *ll;  // tagged activations, per layer: q, k, v, attention out, x after Wo, gate and up, x after down
     int rope_dim;
     unsigned *count;
     int *step_d, *err_d, *tokens_d;
@@ -623,6 +664,7 @@ struct PkdCtx {
     int nphases;
     Layout layout;
     int grid;
+    PhaseFn fn;      // the phase_kernel variant for this model's formats
     int persistent;  // one cooperative launch per step (else one launch per phase)
     int use_graph;   // replay a captured graph (else launch directly)
     cudaGraph_t graph;
@@ -688,7 +730,6 @@ static void seg_of(MvSeg &s, const PkdCtx *c, const PkdTensor &t, int kind)
     s.rb = t.row_bytes;
     s.rows = (int)t.rows;
     s.type = (int)t.type;
-    s.type2 = s.type;
     s.kind = kind;
 }
 
@@ -709,7 +750,7 @@ static LLPlan ll_plan(const PkdModel *m)
     p.att = p.v + r32(kvd);
     p.xmid = p.att + r32(dim);
     p.hb = p.xmid + r32(dim);
-    p.xout = p.hb + r32((size_t)m->hidden_dim);
+    p.xout = p.hb + r32(2 * (size_t)m->hidden_dim);  // gate, then up
     p.per_layer = p.xout + r32(dim);
     return p;
 }
@@ -721,7 +762,7 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
 {
     const int L = m->n_layers, dim = m->dim, hs = m->dim / m->n_heads;
     const int kvd = hs * m->n_kv_heads, km = m->n_heads / m->n_kv_heads;
-    const int nsplit = (m->seq_len + ATT_SUB - 1) / ATT_SUB;
+    const int nsplit = attn_max_splits(m->n_heads, c->grid, m->seq_len);
     const LLPlan lp = ll_plan(m);
     c->nphases = 5 * L + 1;
     c->phases = (Phase *)calloc((size_t)c->nphases, sizeof(Phase));
@@ -773,7 +814,7 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
         att.kc = c->kc;
         att.vc = c->vc;
         att.part = c->part;
-        att.count = c->count + (size_t)l * m->n_kv_heads;
+        att.count = c->count + (size_t)l * m->n_heads;
         att.layer = l;
         att.seq_len = m->seq_len;
         att.kv_dim = kvd;
@@ -798,14 +839,15 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
         tile_phase(wo, nw_total, cap, false);
         rotate(wo);
 
+        // gate and up as two row sets of one phase: gate rows to hb[0, hid),
+        // up rows to hb[hid, 2 hid); the down phase stages silu(gate) * up
         up.kind = PH_MV;
         up.pro = PRO_NORM;
-        up.epi = EPI_SWIGLU;
-        up.nseg = 1;
+        up.epi = EPI_STORE;
+        up.nseg = 2;
         seg_of(up.seg[0], c, m->gate[l], KIND_PLAIN);
-        up.seg[0].w2 = c->arena + m->up[l].offset;
-        up.seg[0].rb2 = m->up[l].row_bytes;
-        up.seg[0].type2 = (int)m->up[l].type;
+        seg_of(up.seg[1], c, m->up[l], KIND_PLAIN);
+        up.seg[1].yoff = m->hidden_dim;
         up.cols = dim;
         up.xin_ll = ll + lp.xmid;
         up.norm = c->norms + (size_t)(2 * l + 1) * dim;
@@ -815,7 +857,7 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
         rotate(up);
 
         dn.kind = PH_MV;
-        dn.pro = PRO_PLAIN;
+        dn.pro = PRO_SWIGLU;
         dn.epi = EPI_ADD;
         dn.nseg = 1;
         seg_of(dn.seg[0], c, m->down[l], KIND_PLAIN);
@@ -869,11 +911,13 @@ static int record_step(PkdCtx *c)
         attr[0].val.cooperative = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        if (cudaLaunchKernelEx(&cfg, phase_kernel, a) != cudaSuccess) return 0;
+        if (cudaLaunchKernelEx(&cfg, c->fn, a) != cudaSuccess) return 0;
     } else {
         // One launch per phase (the tagged words are complete by then).
         for (int i = 0; i < c->nphases; i++) {
-            if (!launch_phase(c->phases[i], c->step_d, c->err_d, st, c->grid, c->rope_cs, c->rope_dim)) return 0;
+            if (!launch_phase(c->phases[i], c->step_d, c->err_d, st, c->grid, c->rope_cs, c->rope_dim, c->fn)) {
+                return 0;
+            }
         }
     }
     finish_kernel<<<1, 1, 0, st>>>(c->step_d, c->amax_d, c->tokens_d, c->tokens_cap, c->err_d);
@@ -892,14 +936,12 @@ extern "C" int pkd_build(PkdCtx *c, const PkdModel *m, char *err, size_t cap)
     const size_t hs = dim / (size_t)m->n_heads, kvd = hs * (size_t)m->n_kv_heads;
     const size_t cache = (size_t)m->n_layers * (size_t)m->seq_len * kvd;
     const size_t nnorm = (2 * (size_t)m->n_layers + 1) * dim;
-    const int km = m->n_heads / m->n_kv_heads;
-    const int nsplit = (m->seq_len + ATT_SUB - 1) / ATT_SUB;
     if ((size_t)m->rope_dim > hs || hs % 4 || hs > 256) {
         if (err && cap) snprintf(err, cap, "Unsupported model shape.");
         return 0;
     }
     cudaSetDevice(c->device);
-    sm_count();
+    const int nsplit = attn_max_splits(m->n_heads, sm_count(), m->seq_len);
     const size_t part = (size_t)m->n_heads * nsplit * (hs + 2);
     const size_t ll_words = ll_plan(m).per_layer * (size_t)m->n_layers;
     (void)hid;
@@ -910,7 +952,7 @@ extern "C" int pkd_build(PkdCtx *c, const PkdModel *m, char *err, size_t cap)
         cuda_fail(c, cudaMalloc(&c->part, part * 4), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->norms, nnorm * 4), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->rope_cs, (size_t)m->seq_len * m->rope_dim * 4 + 4), "cudaMalloc", err, cap) ||
-        cuda_fail(c, cudaMalloc(&c->count, (size_t)m->n_layers * m->n_kv_heads * 4), "cudaMalloc", err, cap) ||
+        cuda_fail(c, cudaMalloc(&c->count, (size_t)m->n_layers * m->n_heads * 4), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->step_d, 32), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->err_d, 16), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->amax_d, 16), "cudaMalloc", err, cap) ||
@@ -927,7 +969,7 @@ extern "C" int pkd_build(PkdCtx *c, const PkdModel *m, char *err, size_t cap)
     cudaStream_t st = c->stream;
     cudaMemsetAsync(c->kc, 0, cache * 4, st);
     cudaMemsetAsync(c->vc, 0, cache * 4, st);
-    cudaMemsetAsync(c->count, 0, (size_t)m->n_layers * m->n_kv_heads * 4, st);
+    cudaMemsetAsync(c->count, 0, (size_t)m->n_layers * m->n_heads * 4, st);
     cudaMemsetAsync(c->err_d, 0, 16, st);
     cudaMemsetAsync(c->amax_d, 0, 16, st);
     cudaMemsetAsync(c->ll, 0, ll_words * 8, st);  // tag 0: never a step's tag
@@ -966,6 +1008,9 @@ extern "C" int pkd_build(PkdCtx *c, const PkdModel *m, char *err, size_t cap)
         if (err && cap) snprintf(err, cap, "Out of memory.");
         return 0;
     }
+    unsigned need = 0u;
+    for (int i = 0; i < c->nphases; i++) need |= phase_formats(c->phases[i]);
+    c->fn = pick_variant(need);
     int max_units = 1, stage = 128;
     for (int i = 0; i < c->nphases; i++) {
         if (c->phases[i].kind != PH_MV) continue;
@@ -973,7 +1018,7 @@ extern "C" int pkd_build(PkdCtx *c, const PkdModel *m, char *err, size_t cap)
         const int need = stage_need(c->phases[i]);
         if (need > stage) stage = need;
     }
-    const int attn_floats = attn_scratch_floats(km, (int)hs, nsplit);
+    const int attn_floats = attn_scratch_floats((int)hs, DK_WARPS);
     if (!make_layout(c->layout, max_units, stage, attn_floats, 4)) {
         if (err && cap) snprintf(err, cap, "Model rows or context too large for the shared-memory plan.");
         return 0;
@@ -981,9 +1026,9 @@ extern "C" int pkd_build(PkdCtx *c, const PkdModel *m, char *err, size_t cap)
     if (c->persistent) {
         int per_sm = 0;
         if (c->layout.warps != DK_WARPS ||  // tiles were numbered for DK_WARPS warps per CTA
-            cudaFuncSetAttribute(phase_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->layout.smem) !=
+            cudaFuncSetAttribute(c->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->layout.smem) !=
                 cudaSuccess ||
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, phase_kernel, c->layout.warps * 32,
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, c->fn, c->layout.warps * 32,
                                                           c->layout.smem) != cudaSuccess ||
             per_sm < 1) {
             c->persistent = 0;  // no co-residency guarantee: one launch per phase instead

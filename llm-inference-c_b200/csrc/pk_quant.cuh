@@ -195,6 +195,14 @@ __device__ __forceinline__ float decode_col(int t, const uint8_t *row, int c)
     }
 }
 
+// decode_col as a real call: for the cold paths of the decode step (the
+// embedding row of layer 0), where inlining all seven decoders at every
+// use would only bloat the hot kernel's code.
+__device__ __noinline__ float decode_col_call(int t, const uint8_t *row, int c)
+{
+    return decode_col(t, row, c);
+}
+
 // ------------------------------------------------------------------ //
 // Fused dequant-dot of one 64-column unit                            //
 // ------------------------------------------------------------------ //
@@ -286,6 +294,14 @@ __device__ __forceinline__ float hf(uint32_t bits16)
     return __half2float(__ushort_as_half((unsigned short)bits16));
 }
 
+// Byte b of w as a float, exactly: the byte goes into the mantissa of
+// 2^23 (one byte permute) and 2^23 is subtracted (one add), which avoids
+// the slower integer-to-float conversion.
+__device__ __forceinline__ float byte_f(uint32_t w, int b)
+{
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | (uint32_t)b)) - 8388608.0f;
+}
+
 // The two 6-bit (scale, min) pairs of sub-blocks 2j and 2j+1 of a Q4_K /
 // Q5_K block, from the scale bytes held in three words s0 = bytes 0..3,
 // s1 = 4..7, s2 = 8..11 (src/gguf_quant.c:65-90): pairs come out packed as
@@ -350,8 +366,9 @@ __device__ __forceinline__ float unit_q4k(const uint8_t *row, int u, const XUnit
     const float d = hf(hdr.x & 0xFFFFu), dmin = hf(hdr.x >> 16);
     const float s0v = x.scale[0] * planes(A[0][0], A[0][1], A[0][2]);
     const float s1v = (x.scale[1] * 0.0625f) * planes(A[1][0], A[1][1], A[1][2]);
-    return (d * (float)(sc & 255u)) * s0v - (dmin * (float)(mn & 255u)) * x.sum[0] +
-           (d * (float)(sc >> 8)) * s1v - (dmin * (float)(mn >> 8)) * x.sum[1];
+    const float ds = fmaf(byte_f(sc, 1), s1v, byte_f(sc, 0) * s0v);
+    const float dm = fmaf(byte_f(mn, 1), x.sum[1], byte_f(mn, 0) * x.sum[0]);
+    return fmaf(d, ds, -dmin * dm);
 }
 
 // Q5_K unit: as Q4_K with the fifth bit from qh (bits 2j, 2j+1),
@@ -383,8 +400,9 @@ __device__ __forceinline__ float unit_q5k(const uint8_t *row, int u, const XUnit
     const float d = hf(hdr.x & 0xFFFFu), dmin = hf(hdr.x >> 16);
     const float s0v = x.scale[0] * planes(A[0][0], A[0][1], A[0][2]);
     const float s1v = x.scale[1] * planes(A[1][0], A[1][1], A[1][2]);
-    return (d * (float)(sc & 255u)) * s0v - (dmin * (float)(mn & 255u)) * x.sum[0] +
-           (d * (float)(sc >> 8)) * s1v - (dmin * (float)(mn >> 8)) * x.sum[1];
+    const float ds = fmaf(byte_f(sc, 1), s1v, byte_f(sc, 0) * s0v);
+    const float dm = fmaf(byte_f(mn, 1), x.sum[1], byte_f(mn, 0) * x.sum[0]);
+    return fmaf(d, ds, -dmin * dm);
 }
 
 // Q6_K unit: columns 128h + 64mm + [0, 64) of block u/4. Weight
@@ -414,14 +432,18 @@ __device__ __forceinline__ float unit_q6k(const uint8_t *row, int u, const XUnit
         }
     }
     const float d = hf(ld_u16(blk + 208));
-    const int8_t *sc = reinterpret_cast<const int8_t *>(blk + 192 + 8 * h + 4 * mm);
+    // the four int8 scales of these 64 weights, biased to unsigned bytes
+    const uint8_t *scp = blk + 192 + 8 * h + 4 * mm;
+    const uint32_t scw = (ld_u16(scp) | (ld_u16(scp + 2) << 16)) ^ 0x80808080u;
     float total = 0.0f;
 #pragma unroll
     for (int g16 = 0; g16 < 4; g16++) {
         const int g = g16 >> 1, half = g16 & 1;
         const float v = x.scale[g] * planes(A[g16][0] - 32 * x.dsum[g][half][0], A[g16][1] - 32 * x.dsum[g][half][1],
                                             A[g16][2] - 32 * x.dsum[g][half][2]);
-        total = fmaf(d * (float)sc[g16], v, total);
+        // byte + 128 as a float, minus 128: the signed scale, exactly
+        const float scf = __uint_as_float(__byte_perm(scw, 0x4B000000u, 0x7440u | (uint32_t)g16)) - 8388736.0f;
+        total = fmaf(d * scf, v, total);
     }
     return total;
 }

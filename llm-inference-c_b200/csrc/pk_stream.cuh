@@ -31,8 +31,8 @@ namespace pk {
 constexpr long long WAIT_LIMIT_CYCLES = 4000000000LL;  // ~2 s at 2 GHz
 
 enum { PH_MV = 0, PH_ATTN = 1 };
-enum { PRO_PLAIN = 0, PRO_NORM = 1, PRO_EMBED_NORM = 2 };
-enum { EPI_STORE = 0, EPI_ADD = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
+enum { PRO_PLAIN = 0, PRO_NORM = 1, PRO_EMBED_NORM = 2, PRO_SWIGLU = 3 };
+enum { EPI_STORE = 0, EPI_ADD = 1, EPI_QKV = 2, EPI_LOGITS = 4 };
 enum { KIND_PLAIN = 0, KIND_Q = 1, KIND_K = 2, KIND_V = 3 };
 enum { ERR_TIMEOUT_MV = 1, ERR_TIMEOUT_WAIT = 2, ERR_NONFINITE = 4 };
 constexpr int ERR_FATAL = ERR_TIMEOUT_MV | ERR_TIMEOUT_WAIT;
@@ -216,10 +216,10 @@ __device__ __forceinline__ uint32_t order_key(float f)
 // ------------------------------------------------------------------ //
 
 struct MvSeg {
-    const uint8_t *w;   // row 0 of the (first) matrix
-    const uint8_t *w2;  // row 0 of the paired matrix (EPI_SWIGLU) or null
-    uint64_t rb, rb2;   // bytes per row of each
-    int rows, type, type2, R, tile0, kind;
+    const uint8_t *w;  // row 0 of the matrix
+    uint64_t rb;       // bytes per row
+    int rows, type, R, tile0, kind;
+    int yoff;          // EPI_STORE: row r goes to output element yoff + r
 };
 
 struct Phase {
@@ -231,10 +231,11 @@ struct Phase {
     int nseg, ntiles, cols, nunits;
     const float *xin;         // input vector as floats (device seam), or
     const uint64_t *xin_ll;   // as tagged words (decode step)
-    const float *norm;        // RMSNorm weights (PRO_NORM / PRO_EMBED_NORM)
+    const float *norm;        // RMSNorm weights (PRO_NORM / PRO_EMBED_NORM); PRO_SWIGLU
+                              //   reads gate at xin_ll[c] and up at xin_ll[cols + c]
     float eps;
     float *y;                 // float output (EPI_STORE of the seam, EPI_LOGITS)
-    uint64_t *y_ll;           // tagged output (EPI_STORE / EPI_ADD / EPI_SWIGLU)
+    uint64_t *y_ll;           // tagged output (EPI_STORE / EPI_ADD)
     const uint64_t *res_ll;   // EPI_ADD residual (null: the embedding row)
     const uint8_t *embd;      // embedding table, row bytes, type (PRO_EMBED_NORM,
     uint64_t embd_rb;         //   and the residual of layer 0's EPI_ADD)
@@ -303,21 +304,14 @@ __device__ __forceinline__ const MvSeg &find_seg(const Phase &p, int t)
 }
 
 // Lane 0: issue the copies of tile t of phase p into buf; completes on bar.
-__device__ __forceinline__ void issue_tile(const Phase &p, int t, uint8_t *buf, int stage_bytes, uint64_t *bar)
+__device__ __forceinline__ void issue_tile(const Phase &p, int t, uint8_t *buf, uint64_t *bar)
 {
     const MvSeg &s = find_seg(p, t);
     const int r0 = (t - s.tile0) * s.R;
     const int nr = min(s.R, s.rows - r0);
     const Span sa = make_span(reinterpret_cast<uintptr_t>(s.w) + (uintptr_t)r0 * s.rb, (uint64_t)nr * s.rb);
-    if (s.w2 != nullptr) {
-        const Span sb = make_span(reinterpret_cast<uintptr_t>(s.w2) + (uintptr_t)r0 * s.rb2, (uint64_t)nr * s.rb2);
-        mbar_expect_tx(bar, sa.bulk + sb.bulk);
-        fill_span(sa, buf, bar);
-        fill_span(sb, buf + stage_bytes / 2, bar);
-    } else {
-        mbar_expect_tx(bar, sa.bulk);
-        fill_span(sa, buf, bar);
-    }
+    mbar_expect_tx(bar, sa.bulk);
+    fill_span(sa, buf, bar);
 }
 
 // A warp's ring and its producer cursor (phase index, tile ordinal).
@@ -342,7 +336,7 @@ __device__ __forceinline__ void ring_fill(Ring &r, const Phase *ph, int nph, int
             continue;
         }
         const uint32_t slot = r.issued % (uint32_t)r.stages;
-        issue_tile(p, t, r.buf + slot * r.stage_bytes, r.stage_bytes, r.bars + slot);
+        issue_tile(p, t, r.buf + slot * r.stage_bytes, r.bars + slot);
         r.issued++;
         r.ck++;
     }
@@ -379,9 +373,10 @@ __device__ __forceinline__ float pow2f(int k)
 __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t *xq, float *xg, uint32_t tag,
                                         int *err)
 {
-    constexpr int MAXP = 4;  // groups per quad per pass
+    constexpr int MAXP = 2;  // groups per quad per pass
     __shared__ float red[32];
     const int pro = p.pro, n = p.cols, ng = 2 * p.nunits;
+    const bool normed = pro == PRO_NORM || pro == PRO_EMBED_NORM;
     const float *xin = p.xin, *norm = p.norm;
     const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
     const int quad = tid >> 2, t = tid & 3, nquads = nt >> 2;
@@ -398,7 +393,16 @@ __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t
         if (pro == PRO_EMBED_NORM) {
 #pragma unroll
             for (int e = 0; e < 8; e++) {
-                if (c0 + e < n) v[e] = decode_col(etype, erow, c0 + e);
+                if (c0 + e < n) v[e] = decode_col_call(etype, erow, c0 + e);
+            }
+        } else if (pro == PRO_SWIGLU) {
+            // hb = silu(gate) * up, src/gguf_forward.c:287-290
+            if (c0 < n) {
+                float u[8];
+                ll_read8(p.xin_ll + c0, min(8, n - c0), tag, v, err);
+                ll_read8(p.xin_ll + n + c0, min(8, n - c0), tag, u, err);
+#pragma unroll
+                for (int e = 0; e < 8; e++) v[e] = __fmul_rn(__fdiv_rn(v[e], __fadd_rn(1.0f, expf(-v[e]))), u[e]);
             }
         } else if (p.xin_ll != nullptr) {
             if (c0 < n) ll_read8(p.xin_ll + c0, min(8, n - c0), tag, v, err);
@@ -428,7 +432,7 @@ __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t
         return __fdiv_rn(1.0f, __fsqrt_rn(m));
     };
     float sc = 1.0f;
-    if (pro != PRO_PLAIN && !one_pass) {
+    if (normed && !one_pass) {
         float ss = 0.0f;
         for (int g = quad; g < ng; g += nquads) {
             float v[8];
@@ -448,7 +452,7 @@ __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t
 #pragma unroll
             for (int e = 0; e < 8; e++) ss = fmaf(v[k][e], v[k][e], ss);
         }
-        if (pro != PRO_PLAIN && one_pass) sc = norm_scale(ss);
+        if (normed && one_pass) sc = norm_scale(ss);
 #pragma unroll
         for (int k = 0; k < MAXP; k++) {
             // The shuffles below name all 32 lanes, so the loop may only be
@@ -457,7 +461,7 @@ __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t
             const int g = base + quad + k * nquads;
             const bool act = g < ng;
             const int c0 = 32 * g + 8 * t;
-            if (pro != PRO_PLAIN) {
+            if (normed) {
 #pragma unroll
                 for (int e = 0; e < 8; e++) {
                     if (c0 + e < n) v[k][e] = __fmul_rn(norm[c0 + e], __fmul_rn(sc, v[k][e]));
@@ -538,21 +542,21 @@ __device__ __forceinline__ float unit_dot(const uint8_t *row, int u, int nblk, i
     return unit_float(T, row, u, cols, xq, xg);
 }
 
-// Row sums of a tile: lane i (< nr) returns row i's dot in .x (and the
-// paired row's in .y). Rows go in unrolled chunks of RU (independent dp4a
-// chains for ILP, accumulated in registers); units are taken 32 at a time,
-// one per lane, and each row is reduced over the warp once.
-template <int T, bool PAIR>
-__device__ __forceinline__ float2 tile_rows(const uint8_t *ra, uint64_t rba, const uint8_t *rb, uint64_t rbb, int nr,
-                                           int nunits, int cols, const uint8_t *xq, const float *xg, int lane)
+// Row sums of a tile: lane i (< nr) returns row i's dot. Rows go in
+// unrolled chunks of RU (independent dp4a chains for ILP, accumulated in
+// registers); units are taken 32 at a time, one per lane, and each row is
+// reduced over the warp once.
+template <int T>
+__device__ __forceinline__ float tile_rows(const uint8_t *ra, uint64_t rba, int nr, int nunits, int cols,
+                                          const uint8_t *xq, const float *xg, int lane)
 {
-    constexpr int RU = PAIR ? 2 : 4;
+    constexpr int RU = 4;
     const int nblk = cols / block_weights(T);
-    float a = 0.0f, b = 0.0f;
+    float a = 0.0f;
     for (int i0 = 0; i0 < nr; i0 += RU) {
-        float va[RU], vb[RU];
+        float va[RU];
 #pragma unroll
-        for (int j = 0; j < RU; j++) va[j] = vb[j] = 0.0f;
+        for (int j = 0; j < RU; j++) va[j] = 0.0f;
         for (int u0 = 0; u0 < nunits; u0 += 32) {
             const int u = u0 + lane;
             if (u < nunits) {
@@ -560,10 +564,7 @@ __device__ __forceinline__ float2 tile_rows(const uint8_t *ra, uint64_t rba, con
                 if (T != T_F32 && T != T_F16) load_xunit(xq, xg, u, x);
 #pragma unroll
                 for (int j = 0; j < RU; j++) {
-                    if (i0 + j < nr) {
-                        va[j] += unit_dot<T>(ra + (size_t)(i0 + j) * rba, u, nblk, cols, x, xq, xg);
-                        if (PAIR) vb[j] += unit_dot<T>(rb + (size_t)(i0 + j) * rbb, u, nblk, cols, x, xq, xg);
-                    }
+                    if (i0 + j < nr) va[j] += unit_dot<T>(ra + (size_t)(i0 + j) * rba, u, nblk, cols, x, xq, xg);
                 }
             }
         }
@@ -571,58 +572,58 @@ __device__ __forceinline__ float2 tile_rows(const uint8_t *ra, uint64_t rba, con
         for (int j = 0; j < RU; j++) {
             const float sa = warp_sum(va[j]);
             if (lane == i0 + j) a = sa;
-            if (PAIR) {
-                const float sb = warp_sum(vb[j]);
-                if (lane == i0 + j) b = sb;
-            }
         }
     }
-    return make_float2(a, b);
+    return a;
 }
 
-template <bool PAIR>
-__device__ __forceinline__ float2 tile_dispatch(int type, const uint8_t *ra, uint64_t rba, const uint8_t *rb,
-                                                uint64_t rbb, int nr, int nunits, int cols, const uint8_t *xq,
-                                                const float *xg, int lane)
+// Format sets a kernel is compiled for (bit t = GGML type t): a kernel
+// carries only the unit loops of the formats its model uses, which keeps
+// its code small enough for the instruction caches.
+__host__ __device__ constexpr unsigned tbit(int t)
 {
+    return 1u << t;
+}
+constexpr unsigned FMT_ALL =
+    tbit(T_F32) | tbit(T_F16) | tbit(T_Q4_0) | tbit(T_Q8_0) | tbit(T_Q4_K) | tbit(T_Q5_K) | tbit(T_Q6_K);
+
+template <unsigned MASK>
+__device__ __forceinline__ float tile_dispatch(int type, const uint8_t *ra, uint64_t rba, int nr, int nunits,
+                                               int cols, const uint8_t *xq, const float *xg, int lane)
+{
+#define PK_CASE(T)                                                          \
+    case T:                                                                 \
+        if constexpr ((MASK & tbit(T)) != 0u) {                             \
+            return tile_rows<T>(ra, rba, nr, nunits, cols, xq, xg, lane); \
+        }                                                                   \
+        break;
     switch (type) {
-    case T_Q4_K: return tile_rows<T_Q4_K, PAIR>(ra, rba, rb, rbb, nr, nunits, cols, xq, xg, lane);
-    case T_Q5_K: return tile_rows<T_Q5_K, PAIR>(ra, rba, rb, rbb, nr, nunits, cols, xq, xg, lane);
-    case T_Q6_K: return tile_rows<T_Q6_K, PAIR>(ra, rba, rb, rbb, nr, nunits, cols, xq, xg, lane);
-    case T_Q4_0: return tile_rows<T_Q4_0, PAIR>(ra, rba, rb, rbb, nr, nunits, cols, xq, xg, lane);
-    case T_Q8_0: return tile_rows<T_Q8_0, PAIR>(ra, rba, rb, rbb, nr, nunits, cols, xq, xg, lane);
-    case T_F32: return tile_rows<T_F32, PAIR>(ra, rba, rb, rbb, nr, nunits, cols, xq, xg, lane);
-    case T_F16: return tile_rows<T_F16, PAIR>(ra, rba, rb, rbb, nr, nunits, cols, xq, xg, lane);
-    default: return make_float2(0.0f, 0.0f);
+        PK_CASE(T_Q4_K)
+        PK_CASE(T_Q5_K)
+        PK_CASE(T_Q6_K)
+        PK_CASE(T_Q4_0)
+        PK_CASE(T_Q8_0)
+        PK_CASE(T_F32)
+        PK_CASE(T_F16)
+    default: break;
     }
+#undef PK_CASE
+    return 0.0f;
 }
 
 // Compute tile t of phase p from its ring slot and apply the epilogue.
 // rope: this position's cos/sin pairs (EPI_QKV); tag: the step's tag for
-// tagged outputs and the residual.
-__device__ __forceinline__ void run_tile(const Phase &p, int t, const uint8_t *buf, int stage_bytes,
-                                         const uint8_t *xq, const float *xg, const int *step, const float *rope,
-                                         uint32_t tag, int *err, int lane, unsigned long long *cta_amax)
+// tagged outputs and the residual. MASK: the formats compiled in.
+template <unsigned MASK>
+__device__ __forceinline__ void run_tile(const Phase &p, int t, const uint8_t *buf, const uint8_t *xq,
+                                         const float *xg, const int *step, const float *rope, uint32_t tag, int *err,
+                                         int lane, unsigned long long *cta_amax)
 {
     const MvSeg &s = find_seg(p, t);
     const int r0 = (t - s.tile0) * s.R;
     const int nr = min(s.R, s.rows - r0);
     const uint8_t *ra = buf + ((reinterpret_cast<uintptr_t>(s.w) + (uintptr_t)r0 * s.rb) & 15);
-    float va, vb = 0.0f;
-    if (p.epi == EPI_SWIGLU && s.type == s.type2) {
-        const uint8_t *rb =
-            buf + stage_bytes / 2 + ((reinterpret_cast<uintptr_t>(s.w2) + (uintptr_t)r0 * s.rb2) & 15);
-        const float2 v = tile_dispatch<true>(s.type, ra, s.rb, rb, s.rb2, nr, p.nunits, p.cols, xq, xg, lane);
-        va = v.x;
-        vb = v.y;
-    } else {
-        va = tile_dispatch<false>(s.type, ra, s.rb, nullptr, 0, nr, p.nunits, p.cols, xq, xg, lane).x;
-        if (p.epi == EPI_SWIGLU) {  // gate and up stored in different formats
-            const uint8_t *rb =
-                buf + stage_bytes / 2 + ((reinterpret_cast<uintptr_t>(s.w2) + (uintptr_t)r0 * s.rb2) & 15);
-            vb = tile_dispatch<false>(s.type2, rb, s.rb2, nullptr, 0, nr, p.nunits, p.cols, xq, xg, lane).x;
-        }
-    }
+    const float va = tile_dispatch<MASK>(s.type, ra, s.rb, nr, p.nunits, p.cols, xq, xg, lane);
     // Epilogue: lane i owns row r0 + i.
     const int r = r0 + lane;
     if (p.epi == EPI_QKV) {
@@ -675,198 +676,217 @@ __device__ __forceinline__ void run_tile(const Phase &p, int t, const uint8_t *b
             // residual stream, src/gguf_forward.c:274-276,297-299 (layer 0's input
             // is the embedding row, decoded again here)
             const float res = p.res_ll != nullptr ? ll_read(p.res_ll + r, tag, err)
-                                                  : decode_col(p.embd_type, p.embd + (size_t)step[0] * p.embd_rb, r);
+                                                  : decode_col_call(p.embd_type, p.embd + (size_t)step[0] * p.embd_rb, r);
             out = __fadd_rn(res, va);
-        } else if (p.epi == EPI_SWIGLU) {
-            out = __fmul_rn(__fdiv_rn(va, __fadd_rn(1.0f, expf(-va))), vb);
         }
         if (p.y_ll != nullptr) {
-            st_ll(p.y_ll + r, out, tag);
+            st_ll(p.y_ll + s.yoff + r, out, tag);
         } else {
-            p.y[r] = out;
+            p.y[s.yoff + r] = out;
         }
     }
 }
 
 // ------------------------------------------------------------------ //
-// Attention item                                                     //
+// Attention                                                          //
 // ------------------------------------------------------------------ //
 
-// Positions per attention sub-chunk (one K/V tile in shared memory).
-constexpr int ATT_SUB = 32;
+// Positions one attention item covers at least: one pass of a CTA's
+// warps (8 warps x 32 lanes, one position per lane).
+constexpr int ATT_MIN_SPAN = 256;
 
-// Scratch floats an attention item needs: queries, two K tiles (rows padded
-// to hs + 1 floats: conflict-free per-position dot products), two V tiles,
-// probabilities, the running output and softmax state, merge weights.
-__host__ __device__ inline int attn_scratch_floats(int kv_mul, int hs, int nsplit_max)
+// Splits of a head's positions over CTAs at most: enough items to cover
+// the grid at long contexts; none below ATT_MIN_SPAN positions.
+__host__ __device__ inline int attn_max_splits(int n_heads, int grid, int seq_len)
 {
-    return kv_mul * hs + 2 * ATT_SUB * (hs + 1) + 2 * ATT_SUB * hs + kv_mul * ATT_SUB + kv_mul * hs + 3 * kv_mul +
-           kv_mul * nsplit_max;
+    int s = grid / n_heads;
+    if (s < 1) s = 1;
+    const int by_len = (seq_len + ATT_MIN_SPAN - 1) / ATT_MIN_SPAN;
+    return s < by_len ? s : by_len;
 }
 
-// Positions one attention item covers at context length n: enough items to
-// cover the GPU (n_kv * splits ~ grid), in whole sub-chunks.
-__device__ __forceinline__ int attn_span(int n, int n_kv, int grid)
+// Positions per item at context length n.
+__host__ __device__ inline int attn_span(int n, int max_splits)
 {
-    const int splits = max(1, grid / n_kv);
-    const int per = (n + splits - 1) / splits;
-    return max(ATT_SUB, (per + ATT_SUB - 1) / ATT_SUB * ATT_SUB);
+    const int per = (n + max_splits - 1) / max_splits;
+    return per < ATT_MIN_SPAN ? ATT_MIN_SPAN : per;
 }
 
-__device__ __forceinline__ void cp_async4(float *dst, const float *src)
+// Positions per shared-memory tile: a K or V tile is <= 8 KB, and a power
+// of two between 8 and 64 so that 256 threads split it evenly.
+__host__ __device__ inline int attn_tile(int hs)
 {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+    int t = 64;
+    while (t > 8 && t * hs > 2048) t >>= 1;
+    return t;
 }
 
-// Item (g, s): positions [s * span, s * span + span) of the kv_mul query heads
-// sharing KV head g, so each K/V row is read once per group. K/V tiles of 32
-// positions are double-buffered with cp.async; the softmax runs online over
-// the tiles (running max and sum). With one split the item writes the head
-// outputs directly; otherwise the last item of the group to finish merges the
-// splits' (max, sum, weighted V) partials in split order.
-// src/gguf_forward.c:228-267 with the softmax of src/transformer.c:85-109.
-// q and this position's K/V row are read as tagged words (the QKV phase of
-// the same step wrote them); earlier positions come from the KV cache.
-// All threads of the CTA.
-__device__ __forceinline__ void attn_item(const Phase &p, int g, int s, int n, int span, float *sm, uint32_t tag,
-                                          int *err)
+// Shared-memory floats an item needs: the query, this step's K and V rows,
+// two K and two V tiles, the tile's probabilities and reduction slots.
+__host__ __device__ inline int attn_scratch_floats(int hs, int nwarps)
 {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    const int hs = p.hs, km = p.kv_mul, kvd = p.kv_dim;
-    const int nsplit = (n + span - 1) / span;
-    const int t0 = s * span, cnt = min(span, n - t0);
-    const int nsub = (cnt + ATT_SUB - 1) / ATT_SUB;
-    const int ks = hs + 1;
-    float *qs = sm;                                  // km * hs
-    float *sK = qs + km * hs;                        // 2 * ATT_SUB * ks
-    float *sV = sK + 2 * ATT_SUB * ks;               // 2 * ATT_SUB * hs
-    float *pr = sV + 2 * ATT_SUB * hs;               // km * ATT_SUB
-    float *orun = pr + km * ATT_SUB;                 // km * hs
-    float *mrun = orun + km * hs, *lrun = mrun + km, *alpha = lrun + km;
-    float *wts = alpha + km;                         // km * nsplit_max
+    const int T = attn_tile(hs);
+    return 3 * hs + 4 * T * hs + T + 2 * nwarps;
+}
+
+__device__ __forceinline__ void cp_async16(float *dst, const float *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+// Item (h, s): query head h over positions [s * span, s * span + span) of
+// the n in the cache, src/gguf_forward.c:233-266 with the softmax of
+// src/transformer.c:85-109. The head's K/V rows stream through shared
+// memory in double-buffered tiles of T positions (16-byte cp.async); per
+// tile, tpp = 256 / T threads score each position (q . K[t] * scale), the
+// online softmax rescales the running sum and output, and threads
+// (dimension, position subset) accumulate p * V[t]. With one split the item
+// writes the head's output; otherwise the last split to finish (per-head
+// counter) merges the splits' (max, sum, output) in split order. q and this
+// position's K/V row are tagged words (the QKV phase of the same step wrote
+// them); earlier positions come from the KV cache. All threads of the CTA
+// (blockDim.x >= 256, a multiple of 32: threads beyond the first 256 take
+// no position when scoring).
+__device__ __forceinline__ void attn_item(const Phase &p, int h, int s, int nsplit, int n, int span, float *sm,
+                                          uint32_t tag, int *err)
+{
+    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
+    const int hs = p.hs, hs4 = hs >> 2, kvd = p.kv_dim, g = h / p.kv_mul;
+    const int T = attn_tile(hs), tpp = 256 / T, nsub = nt / hs;
+    const int t0 = s * span, t1 = min(n, t0 + span);
+    float *qs = sm;                // hs
+    float *kcur = qs + hs;         // hs: K row of this step
+    float *vcur = kcur + hs;       // hs: V row of this step
+    float *Kt = vcur + hs;         // 2 x T x hs
+    float *Vt = Kt + 2 * T * hs;   // 2 x T x hs
+    float *pt = Vt + 2 * T * hs;   // T probabilities
+    float *red = pt + T;           // 2 x nw
     __shared__ int last_sh;
 
+    const bool has_cur = t1 == n;  // the item covers this step's position
+    for (int i = tid; i < hs; i += nt) {
+        qs[i] = ll_read(p.aq_ll + (size_t)h * hs + i, tag, err);
+        if (has_cur) {
+            kcur[i] = ll_read(p.ak_ll + (size_t)g * hs + i, tag, err);
+            vcur[i] = ll_read(p.av_ll + (size_t)g * hs + i, tag, err);
+        }
+    }
+    __syncthreads();
+
     const size_t lbase = (size_t)p.layer * p.seq_len * kvd + (size_t)g * hs;
-    auto load_tile = [&](int sub, int buf) {
-        const int tb = t0 + sub * ATT_SUB, tc = min(ATT_SUB, t0 + cnt - tb);
-        float *K = sK + buf * ATT_SUB * ks, *V = sV + buf * ATT_SUB * hs;
-        for (int i = tid; i < tc * hs; i += blockDim.x) {
-            const int t = i / hs, d = i % hs;
-            if (tb + t == n - 1) {  // this step's row
-                K[t * ks + d] = ll_read(p.ak_ll + (size_t)g * hs + d, tag, err);
-                V[t * hs + d] = ll_read(p.av_ll + (size_t)g * hs + d, tag, err);
+    const float *kc = p.kc + lbase, *vc = p.vc + lbase;
+    const int ntile = (t1 - t0 + T - 1) / T;
+    auto load_tile = [&](int k, int buf) {
+        const int tb = t0 + k * T, tc = min(T, t1 - tb);
+        float *K = Kt + buf * T * hs, *V = Vt + buf * T * hs;
+        for (int i = tid; i < tc * hs4; i += nt) {
+            const int r = i / hs4, c = (i - r * hs4) * 4;
+            if (tb + r == n - 1) {
+                *reinterpret_cast<float4 *>(K + r * hs + c) = *reinterpret_cast<const float4 *>(kcur + c);
+                *reinterpret_cast<float4 *>(V + r * hs + c) = *reinterpret_cast<const float4 *>(vcur + c);
             } else {
-                const size_t off = lbase + (size_t)(tb + t) * kvd + d;
-                cp_async4(K + t * ks + d, p.kc + off);
-                cp_async4(V + t * hs + d, p.vc + off);
+                cp_async16(K + r * hs + c, kc + (size_t)(tb + r) * kvd + c);
+                cp_async16(V + r * hs + c, vc + (size_t)(tb + r) * kvd + c);
             }
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
+
+    float m_run = -INFINITY, l_run = 0.0f, o_acc = 0.0f;
+    const int pr = tid / tpp, pi = tid - pr * tpp;  // scoring: position pr of the tile (< T: a position), part pi
+    const int od = tid % hs, osub = tid / hs;       // output: dimension od, position subset osub
     load_tile(0, 0);
-    for (int i = tid; i < km * hs; i += blockDim.x) {
-        qs[i] = ll_read(p.aq_ll + (size_t)g * km * hs + i, tag, err);
-        orun[i] = 0.0f;
-    }
-    if (tid < km) {
-        mrun[tid] = -INFINITY;
-        lrun[tid] = 0.0f;
-    }
-    for (int sub = 0; sub < nsub; sub++) {
-        const int buf = sub & 1;
-        if (sub + 1 < nsub) {
-            load_tile(sub + 1, buf ^ 1);
+    for (int k = 0; k < ntile; k++) {
+        const int buf = k & 1, tb = t0 + k * T, tc = min(T, t1 - tb);
+        if (k + 1 < ntile) {
+            load_tile(k + 1, buf ^ 1);
             asm volatile("cp.async.wait_group 1;" ::: "memory");
         } else {
             asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();
-        const int tc = min(ATT_SUB, cnt - sub * ATT_SUB);
-        const float *K = sK + buf * ATT_SUB * ks, *V = sV + buf * ATT_SUB * hs;
-        // scores: thread (head h, position t)
-        for (int i = tid; i < km * ATT_SUB; i += blockDim.x) {
-            const int h = i / ATT_SUB, t = i % ATT_SUB;
-            float sc = -INFINITY;
-            if (t < tc) {
-                float acc = 0.0f;
-                for (int d = 0; d < hs; d++) acc = fmaf(qs[h * hs + d], K[t * ks + d], acc);
-                sc = acc * p.scale;
-            }
-            pr[i] = sc;
-        }
-        __syncthreads();
-        // online softmax per head (one warp per head, one lane per position)
-        for (int h = warp; h < km; h += nw) {
-            const float sc = pr[h * ATT_SUB + lane];
-            const float mnew = fmaxf(mrun[h], warp_max(sc));
-            const float e = lane < tc ? expf(sc - mnew) : 0.0f;
-            pr[h * ATT_SUB + lane] = e;
-            const float lsum = warp_sum(e);
-            if (lane == 0) {
-                const float a = expf(mrun[h] - mnew);  // 0 on the first tile (mrun = -inf)
-                alpha[h] = a;
-                lrun[h] = fmaf(lrun[h], a, lsum);
-                mrun[h] = mnew;
+        const float *K = Kt + buf * T * hs, *V = Vt + buf * T * hs;
+        // scores: tpp threads per position, float4 slices i, i + tpp, ...
+        float acc = 0.0f;
+        if (pr < tc) {  // pr >= T for threads beyond the first 256, and tc <= T
+            const float4 *k4 = reinterpret_cast<const float4 *>(K + pr * hs);
+            const float4 *q4 = reinterpret_cast<const float4 *>(qs);
+            for (int d4 = pi; d4 < hs4; d4 += tpp) {
+                const float4 kv = k4[d4], qv = q4[d4];
+                acc = fmaf(qv.x, kv.x, acc);
+                acc = fmaf(qv.y, kv.y, acc);
+                acc = fmaf(qv.z, kv.z, acc);
+                acc = fmaf(qv.w, kv.w, acc);
             }
         }
+        for (int o = tpp >> 1; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+        const float sc = pr < tc ? acc * p.scale : -INFINITY;
+        const float wmax = warp_max(sc);
+        if (lane == 0) red[warp] = wmax;
         __syncthreads();
-        for (int i = tid; i < km * hs; i += blockDim.x) {
-            const int h = i / hs, d = i % hs;
-            float o = orun[i] * alpha[h];
-            for (int t = 0; t < tc; t++) o = fmaf(pr[h * ATT_SUB + t], V[t * hs + d], o);
-            orun[i] = o;
-        }
+        float mt = red[0];
+        for (int w = 1; w < nw; w++) mt = fmaxf(mt, red[w]);
+        const float m_new = fmaxf(m_run, mt);
+        const float e = pr < tc ? expf(sc - m_new) : 0.0f;
+        if (pi == 0 && pr < T) pt[pr] = e;
+        const float wsum = warp_sum(pi == 0 ? e : 0.0f);
+        if (lane == 0) red[nw + warp] = wsum;
         __syncthreads();
-    }
-    if (nsplit == 1) {
-        for (int i = tid; i < km * hs; i += blockDim.x) {
-            st_ll(p.aout_ll + (size_t)g * km * hs + i, orun[i] / lrun[i / hs], tag);
+        float lt = 0.0f;
+        for (int w = 0; w < nw; w++) lt += red[nw + w];
+        const float alpha = expf(m_run - m_new);  // 0 on the first tile (m_run = -inf)
+        l_run = fmaf(l_run, alpha, lt);
+        m_run = m_new;
+        if (osub < nsub) {
+            float ov = o_acc * alpha;
+            for (int t = osub; t < tc; t += nsub) ov = fmaf(pt[t], V[t * hs + od], ov);
+            o_acc = ov;
         }
-        return;
+        __syncthreads();  // tile buffer, pt and red are reused
     }
+
+    // sum the position subsets (the K tiles are free now)
+    float *osum = Kt;
+    if (osub < nsub) osum[osub * hs + od] = o_acc;
+    __syncthreads();
     const int stride = hs + 2;
-    for (int i = tid; i < km * hs; i += blockDim.x) {
-        const int h = i / hs, d = i % hs;
-        float *P = p.part + ((size_t)(g * km + h) * p.nsplit_max + s) * stride;
-        P[2 + d] = orun[i];
-        if (d == 0) {
-            P[0] = mrun[h];
-            P[1] = lrun[h];
+    for (int d = tid; d < hs; d += nt) {
+        float O = 0.0f;
+        for (int j = 0; j < nsub; j++) O += osum[j * hs + d];
+        if (nsplit == 1) {
+            st_ll(p.aout_ll + (size_t)h * hs + d, O / l_run, tag);
+        } else {
+            float *P = p.part + ((size_t)h * p.nsplit_max + s) * stride;
+            P[2 + d] = O;
+            if (d == 0) {
+                P[0] = m_run;
+                P[1] = l_run;
+            }
         }
     }
+    if (nsplit == 1) return;
+
     __threadfence();
     __syncthreads();
-    if (tid == 0) last_sh = (atomicAdd(p.count + g, 1u) == (unsigned)(nsplit - 1));
+    if (tid == 0) last_sh = (atomicAdd(p.count + h, 1u) == (unsigned)(nsplit - 1));
     __syncthreads();
-    if (last_sh) {
-        __threadfence();
-        for (int h = warp; h < km; h += nw) {
-            const float *P = p.part + (size_t)(g * km + h) * p.nsplit_max * stride;
-            float M = -INFINITY;
-            for (int j = lane; j < nsplit; j += 32) M = fmaxf(M, __ldcg(P + (size_t)j * stride));
-            M = warp_max(M);
-            float L = 0.0f;
-            for (int j = lane; j < nsplit; j += 32) {
-                const float w = expf(__ldcg(P + (size_t)j * stride) - M);
-                wts[h * p.nsplit_max + j] = w;
-                L = fmaf(__ldcg(P + (size_t)j * stride + 1), w, L);
-            }
-            L = warp_sum(L);
-            for (int j = lane; j < nsplit; j += 32) wts[h * p.nsplit_max + j] /= L;
-        }
-        __syncthreads();
-        for (int i = tid; i < km * hs; i += blockDim.x) {
-            const int h = i / hs, d = i % hs;
-            const float *P = p.part + (size_t)(g * km + h) * p.nsplit_max * stride + 2 + d;
-            const float *w = wts + h * p.nsplit_max;
-            float O = 0.0f;
-#pragma unroll 4
-            for (int j = 0; j < nsplit; j++) O = fmaf(__ldcg(P + (size_t)j * stride), w[j], O);
-            st_ll(p.aout_ll + (size_t)(g * km + h) * hs + d, O, tag);
-        }
-        if (tid == 0) p.count[g] = 0;
+    if (!last_sh) return;
+    __threadfence();
+    const float *P = p.part + (size_t)h * p.nsplit_max * stride;
+    float MM = -INFINITY;
+    for (int j = 0; j < nsplit; j++) MM = fmaxf(MM, __ldcg(P + (size_t)j * stride));
+    float LL = 0.0f;
+    for (int j = 0; j < nsplit; j++) {
+        LL = fmaf(__ldcg(P + (size_t)j * stride + 1), expf(__ldcg(P + (size_t)j * stride) - MM), LL);
     }
-    __syncthreads();
+    for (int d = tid; d < hs; d += nt) {
+        float O = 0.0f;
+        for (int j = 0; j < nsplit; j++) {
+            O = fmaf(__ldcg(P + (size_t)j * stride + 2 + d), expf(__ldcg(P + (size_t)j * stride) - MM), O);
+        }
+        st_ll(p.aout_ll + (size_t)h * hs + d, O / LL, tag);
+    }
+    if (tid == 0) p.count[h] = 0;
 }
 
 }  // namespace pk
