@@ -48,6 +48,54 @@ const char *engine_last_error(const LLMModel *model);
 /* Bytes of packed weights resident on the device. */
 size_t engine_weight_bytes(const LLMModel *model);
 
+/* ---- Tensor parallelism over the GPUs of one box -------------------
+ *
+ * One process per GPU; the ranks' decode kernels exchange partial sums
+ * over NVLink peer memory inside the decode step (two all-reduces per
+ * layer, no library collective). Query/KV heads, the FFN hidden slice and
+ * the output's vocabulary rows are split over the ranks; the embedding,
+ * the norms and the residual stream are replicated. Every rank's
+ * engine_forward returns the full logits, every rank's greedy token is the
+ * global argmax. Usage, on each rank:
+ *
+ *   m = engine_open_tp(&opts, device, rank, world, err, cap);
+ *   engine_tp_handle(m, mine);            // 64 bytes
+ *   ... all-gather the ranks' 64-byte handles in rank order ...
+ *   engine_tp_connect(m, all, err, cap);  // then decode as usual, every
+ *                                         // rank feeding the same tokens
+ */
+
+/* Placement of one rank. */
+typedef struct {
+    int q_head0, q_heads;   /* query heads */
+    int kv_head0, kv_heads; /* KV heads (shared by ranks when world > n_kv_heads) */
+    int hid0, hid;          /* ffn_gate / ffn_up rows = ffn_down columns */
+    int voc0, voc;          /* output (logits) rows */
+    int own0, own;          /* residual-stream elements this rank reduces */
+} EngineTpPlan;
+
+/* The placement of rank `rank` of `world` (1..8) for a model of these
+ * dimensions; wo_block and down_block are the block widths (weights per
+ * block, e.g. 256 for Q4_K) of attn_output and ffn_down. Returns 1, or 0
+ * with a message when the model cannot be split that way. */
+int engine_tp_plan(int dim, int hidden_dim, int n_heads, int n_kv_heads, int vocab_size,
+                   int wo_block, int down_block, int rank, int world, EngineTpPlan *out,
+                   char *error, size_t error_capacity);
+
+/* engine_open_device for rank `rank` of a tensor-parallel group of
+ * `world` GPUs: loads only this rank's slices. The handle decodes after
+ * engine_tp_connect. world 1 is engine_open_device. */
+LLMModel *engine_open_tp(const LLMOptions *options, int device, int rank, int world,
+                         char *error, size_t error_capacity);
+
+/* This rank's 64-byte exchange handle. Returns 1, or 0 for a handle that is
+ * not tensor-parallel. */
+int engine_tp_handle(LLMModel *model, void *out64);
+
+/* Connect the ranks: `handles` holds world 64-byte handles in rank order.
+ * Returns 1, or 0 with a message (the handle then stays unusable). */
+int engine_tp_connect(LLMModel *model, const void *handles, char *error, size_t error_capacity);
+
 /* Kernel launches one decode step makes: 2 in the default mode (the
  * cooperative step kernel and the one-thread token kernel), one per phase
  * plus one (5 * n_layers + 2) with POCKET_CUDA_PERSISTENT=0 or when the GPU

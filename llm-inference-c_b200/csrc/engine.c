@@ -90,7 +90,9 @@ typedef struct {
 
 typedef struct {
     const GTensor *t;
-    PkdTensor dev;
+    PkdTensor dev;     /* this rank's slice of the tensor */
+    uint64_t r0, c0;   /* its first row and column in the file tensor */
+    uint64_t file_rb;  /* bytes per row in the file */
 } Bound;
 
 struct LLMModel {
@@ -101,6 +103,8 @@ struct LLMModel {
     char description[256];
     PkdCtx *dev;
     uint64_t weight_bytes;
+    int tp_world;      /* tensor-parallel ranks (1: single GPU) */
+    int connected;     /* the decode step exists (tensor parallel: after engine_tp_connect) */
     char last_error[256];
 };
 
@@ -472,6 +476,104 @@ static int bind(const Parsed *p, const char *name, uint64_t cols, uint64_t rows,
     b->dev.rows = nr;
     b->dev.cols = cols;
     b->dev.row_bytes = rb;
+    b->r0 = 0;
+    b->c0 = 0;
+    b->file_rb = rb;
+    return 1;
+}
+
+/* Keep rows [r0, r0 + nr) and columns [c0, c0 + nc) of a bound tensor
+ * (columns on whole quant blocks). */
+static void slice(Bound *b, uint64_t r0, uint64_t nr, uint64_t c0, uint64_t nc)
+{
+    const TypeRow *tr = type_row(b->dev.type);
+    b->r0 = r0;
+    b->c0 = c0;
+    b->dev.rows = nr;
+    b->dev.cols = nc;
+    b->dev.row_bytes = nc / tr->block * tr->bytes;
+}
+
+/* Tensor-parallel placement (see EngineTpPlan in engine_ext.h). */
+static int tp_plan(int dim, int hid, int nh, int nkv, int voc, int wo_bw, int dn_bw, int rank, int world, PkdTp *t,
+                   char *err, size_t cap)
+{
+    memset(t, 0, sizeof(*t));
+    if (world < 1 || world > PKD_TP_MAX || rank < 0 || rank >= world) {
+        seterr(err, cap, "Tensor-parallel world must be 1..8 with 0 <= rank < world.");
+        return 0;
+    }
+    if (dim <= 0 || hid <= 0 || nh <= 0 || nkv <= 0 || voc <= 0 || wo_bw <= 0 || dn_bw <= 0 || dim % nh ||
+        nh % nkv) {
+        seterr(err, cap, "Invalid model dimensions.");
+        return 0;
+    }
+    if (nh % world) {
+        if (err && cap) snprintf(err, cap, "%d attention heads cannot be split over %d ranks.", nh, world);
+        return 0;
+    }
+    const int hs = dim / nh, kvm = nh / nkv;
+    t->rank = rank;
+    t->world = world;
+    t->q_heads = nh / world;
+    t->q_head0 = rank * t->q_heads;
+    if (nkv % world == 0) {
+        t->kv_heads = nkv / world;
+        t->kv_head0 = rank * t->kv_heads;
+    } else if (world % nkv == 0 && kvm % (world / nkv) == 0) {
+        t->kv_heads = 1;  /* ranks share a KV head; each computes it */
+        t->kv_head0 = t->q_head0 / kvm;
+    } else {
+        if (err && cap) snprintf(err, cap, "%d KV heads cannot be split over %d ranks.", nkv, world);
+        return 0;
+    }
+    if ((t->q_heads * hs) % wo_bw) {
+        seterr(err, cap, "attn_output quant blocks straddle the head split.");
+        return 0;
+    }
+    if (hid % dn_bw || hid / dn_bw < world) {
+        seterr(err, cap, "ffn_down has fewer quant blocks than ranks.");
+        return 0;
+    }
+    const long nb = hid / dn_bw;
+    for (int r = 0; r < world; r++) {
+        const int h0 = (int)(dn_bw * (nb * r / world)), h1 = (int)(dn_bw * (nb * (r + 1) / world));
+        if (h1 - h0 > t->hid_max) t->hid_max = h1 - h0;
+        if (r == rank) {
+            t->hid0 = h0;
+            t->hid = h1 - h0;
+        }
+        t->own0[r] = (int)((long)dim * r / world);
+        t->own[r] = (int)((long)dim * (r + 1) / world) - t->own0[r];
+        if (t->own[r] > t->own_max) t->own_max = t->own[r];
+    }
+    t->voc0 = (int)((long)voc * rank / world);
+    t->voc = (int)((long)voc * (rank + 1) / world) - t->voc0;
+    return 1;
+}
+
+int engine_tp_plan(int dim, int hidden_dim, int n_heads, int n_kv_heads, int vocab_size, int wo_block,
+                   int down_block, int rank, int world, EngineTpPlan *out, char *err, size_t cap)
+{
+    PkdTp t;
+    if (out == NULL) {
+        seterr(err, cap, "No output given.");
+        return 0;
+    }
+    if (!tp_plan(dim, hidden_dim, n_heads, n_kv_heads, vocab_size, wo_block, down_block, rank, world, &t, err,
+                 cap))
+        return 0;
+    out->q_head0 = t.q_head0;
+    out->q_heads = t.q_heads;
+    out->kv_head0 = t.kv_head0;
+    out->kv_heads = t.kv_heads;
+    out->hid0 = t.hid0;
+    out->hid = t.hid;
+    out->voc0 = t.voc0;
+    out->voc = t.voc;
+    out->own0 = t.own0[rank];
+    out->own = t.own[rank];
+    if (err && cap) err[0] = '\0';
     return 1;
 }
 
@@ -506,7 +608,7 @@ void engine_close(LLMModel *m)
     free(m);
 }
 
-LLMModel *engine_open_device(const LLMOptions *o, int device, char *err, size_t cap)
+static LLMModel *open_impl(const LLMOptions *o, int device, int rank, int world, char *err, size_t cap)
 {
     if (o == NULL || o->model_path == NULL || o->model_path[0] == '\0') {
         seterr(err, cap, "No model path given.");
@@ -596,10 +698,39 @@ LLMModel *engine_open_device(const LLMOptions *o, int device, char *err, size_t 
             seterr(err, cap, "Unsupported RoPE dimension.");
             goto fail;
         }
-        /* Arena layout; a tied output shares the embedding bytes. */
+        /* This rank's slices (world 1: every tensor whole). The block
+         * widths that bound the column splits are the widest over layers. */
+        int wo_bw = 1, dn_bw = 1;
+        for (int l = 0; l < L; l++) {
+            const int w1 = (int)type_row(b[3 + 9 * (size_t)l + 4].dev.type)->block;
+            const int w2 = (int)type_row(b[3 + 9 * (size_t)l + 8].dev.type)->block;
+            if (w1 > wo_bw) wo_bw = w1;
+            if (w2 > dn_bw) dn_bw = w2;
+        }
+        PkdTp tp;
+        if (!tp_plan(c->dim, c->hidden_dim, c->n_heads, c->n_kv_heads, c->vocab_size, wo_bw, dn_bw, rank, world,
+                     &tp, err, cap))
+            goto fail;
+        const int tied = b[2].t == b[0].t;
+        if (world > 1) {
+            const uint64_t qr0 = (uint64_t)tp.q_head0 * hs, qn = (uint64_t)tp.q_heads * hs;
+            const uint64_t kr0 = (uint64_t)tp.kv_head0 * hs, kn = (uint64_t)tp.kv_heads * hs;
+            slice(&b[2], (uint64_t)tp.voc0, (uint64_t)tp.voc, 0, dim);
+            for (int l = 0; l < L; l++) {
+                Bound *lb = b + 3 + 9 * (size_t)l;
+                slice(&lb[1], qr0, qn, 0, dim);                               /* wq rows */
+                slice(&lb[2], kr0, kn, 0, dim);                               /* wk rows */
+                slice(&lb[3], kr0, kn, 0, dim);                               /* wv rows */
+                slice(&lb[4], 0, dim, qr0, qn);                               /* wo columns */
+                slice(&lb[6], (uint64_t)tp.hid0, (uint64_t)tp.hid, 0, dim);   /* gate rows */
+                slice(&lb[7], (uint64_t)tp.hid0, (uint64_t)tp.hid, 0, dim);   /* up rows */
+                slice(&lb[8], 0, dim, (uint64_t)tp.hid0, (uint64_t)tp.hid);   /* down columns */
+            }
+        }
+        /* Arena layout; a whole tied output shares the embedding bytes. */
         uint64_t arena = 0;
         for (size_t i = 0; i < nb; i++) {
-            if (i == 2 && b[2].t == b[0].t) {
+            if (i == 2 && tied && world == 1) {
                 b[2].dev.offset = b[0].dev.offset;
                 continue;
             }
@@ -649,18 +780,38 @@ LLMModel *engine_open_device(const LLMOptions *o, int device, char *err, size_t 
         m->dev = pkd_create(device, arena, err, cap);
         if (m->dev == NULL) goto fail;
         for (size_t i = 0; i < nb; i++) {
-            if (i == 2 && b[2].t == b[0].t) continue;
-            const uint64_t bytes = b[i].dev.rows * b[i].dev.row_bytes;
-            if (!pkd_upload(m->dev, b[i].dev.offset, p.map + p.data_off + b[i].t->offset, bytes, err, cap))
+            if (i == 2 && tied && world == 1) continue;
+            const Bound *bi = &b[i];
+            const unsigned char *src = p.map + p.data_off + bi->t->offset + bi->r0 * bi->file_rb;
+            const uint64_t bytes = bi->dev.rows * bi->dev.row_bytes;
+            if (bi->dev.row_bytes == bi->file_rb) {  /* whole rows: one contiguous range */
+                if (!pkd_upload(m->dev, bi->dev.offset, src, bytes, err, cap)) goto fail;
+                continue;
+            }
+            /* a column slice: gather each row's byte range */
+            const TypeRow *tr = type_row(bi->dev.type);
+            const uint64_t cb = bi->c0 / tr->block * tr->bytes;
+            unsigned char *tmp = (unsigned char *)malloc((size_t)bytes);
+            if (tmp == NULL) {
+                seterr(err, cap, "Out of memory.");
                 goto fail;
+            }
+            for (uint64_t r = 0; r < bi->dev.rows; r++) {
+                memcpy(tmp + r * bi->dev.row_bytes, src + r * bi->file_rb + cb, (size_t)bi->dev.row_bytes);
+            }
+            const int ok = pkd_upload(m->dev, bi->dev.offset, tmp, bytes, err, cap);
+            free(tmp);
+            if (!ok) goto fail;
         }
         PkdModel dm;
         memset(&dm, 0, sizeof(dm));
         dm.dim = c->dim;
-        dm.hidden_dim = c->hidden_dim;
+        dm.hidden_dim = tp.hid;
         dm.n_layers = L;
-        dm.n_heads = c->n_heads;
-        dm.n_kv_heads = c->n_kv_heads;
+        dm.n_heads = tp.q_heads;
+        dm.n_kv_heads = tp.kv_heads;
+        dm.head_size = (int)hs;
+        dm.tp = tp;
         dm.vocab_size = c->vocab_size;
         dm.seq_len = ctx;
         dm.rope_dim = c->rope_dim;
@@ -694,6 +845,8 @@ LLMModel *engine_open_device(const LLMOptions *o, int device, char *err, size_t 
         dm.down = dn;
         dm.rope_cs = rope;
         if (!pkd_build(m->dev, &dm, err, cap)) goto fail;
+        m->tp_world = world;
+        m->connected = world == 1;
         describe(m, &p);
     }
     free(rope);
@@ -714,6 +867,37 @@ fail:
     return NULL;
 }
 
+LLMModel *engine_open_device(const LLMOptions *o, int device, char *err, size_t cap)
+{
+    return open_impl(o, device, 0, 1, err, cap);
+}
+
+LLMModel *engine_open_tp(const LLMOptions *o, int device, int rank, int world, char *err, size_t cap)
+{
+    return open_impl(o, device, rank, world, err, cap);
+}
+
+int engine_tp_handle(LLMModel *m, void *out64)
+{
+    if (m == NULL || m->tp_world < 2 || out64 == NULL) return 0;
+    return pkd_tp_handle(m->dev, out64, m->last_error, sizeof(m->last_error));
+}
+
+int engine_tp_connect(LLMModel *m, const void *handles, char *err, size_t cap)
+{
+    if (m == NULL || m->tp_world < 2 || handles == NULL || m->connected) {
+        seterr(err, cap, "Not a tensor-parallel handle waiting to be connected.");
+        return 0;
+    }
+    if (!pkd_tp_connect(m->dev, handles, err, cap)) {
+        snprintf(m->last_error, sizeof(m->last_error), "%s", err != NULL && cap > 0 ? err : "connect failed");
+        return 0;
+    }
+    m->connected = 1;
+    if (err && cap) err[0] = '\0';
+    return 1;
+}
+
 LLMModel *engine_open(const LLMOptions *o, char *err, size_t cap)
 {
     return engine_open_device(o, env_device(), err, cap);
@@ -721,7 +905,7 @@ LLMModel *engine_open(const LLMOptions *o, char *err, size_t cap)
 
 static int step_ok(const LLMModel *m, int token, int pos)
 {
-    return m != NULL && m->dev != NULL && token >= 0 && token < m->config.vocab_size && pos >= 0 &&
+    return m != NULL && m->dev != NULL && m->connected && token >= 0 && token < m->config.vocab_size && pos >= 0 &&
            pos < m->config.seq_len;
 }
 

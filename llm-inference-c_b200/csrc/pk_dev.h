@@ -21,8 +21,28 @@ typedef struct {
     uint64_t offset;    /* byte offset of row 0 inside the arena */
 } PkdTensor;
 
+/* Most ranks of one tensor-parallel group. */
+#define PKD_TP_MAX 8
+
+/* Tensor-parallel placement of one rank (world 1: everything local). Query
+ * and KV heads, the hidden slice (gate/up rows = down columns, whole
+ * quant blocks) and the output's vocabulary rows are this rank's; the
+ * residual stream x is replicated, and rank r reduces elements
+ * [own0[r], own0[r] + own[r]) of each all-reduce. */
+typedef struct {
+    int rank, world;
+    int q_head0, q_heads;
+    int kv_head0, kv_heads;
+    int hid0, hid, hid_max;
+    int voc0, voc;
+    int own0[PKD_TP_MAX], own[PKD_TP_MAX];
+    int own_max;
+} PkdTp;
+
 typedef struct {
     int dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, seq_len, rope_dim;
+    int head_size;              /* dim / the model's head count */
+    PkdTp tp;                   /* n_heads, n_kv_heads, hidden_dim above are this rank's */
     float rms_eps;
     float att_scale;            /* 1/sqrtf(head_size), computed as the reference does */
     PkdTensor embd, output;
@@ -42,8 +62,17 @@ void pkd_destroy(PkdCtx *ctx);
 int pkd_upload(PkdCtx *ctx, uint64_t offset, const void *src, uint64_t bytes, char *err, size_t cap);
 
 /* Allocate run state (KV cache, activations), upload norms and the RoPE
- * table, and capture the decode-step graph. */
+ * table, and - for a single rank - build and capture the decode step. A
+ * tensor-parallel rank builds its step in pkd_tp_connect. */
 int pkd_build(PkdCtx *ctx, const PkdModel *m, char *err, size_t cap);
+
+/* Tensor parallel: this rank's exchange-buffer handle (64 bytes, a CUDA IPC
+ * memory handle) for the other ranks. */
+int pkd_tp_handle(PkdCtx *ctx, void *out64, char *err, size_t cap);
+
+/* Tensor parallel: map the other ranks' exchange buffers (world handles of
+ * 64 bytes in rank order), then build and capture the decode step. */
+int pkd_tp_connect(PkdCtx *ctx, const void *handles, char *err, size_t cap);
 
 /* One decode step. Returns host (pinned) logits owned by ctx, or NULL on a
  * device error (ctx then stays failed). */

@@ -129,10 +129,34 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
                     if (threadIdx.x == 0) {
                         if (cta_amax[0] != 0ull) atomicMax(p.amax, cta_amax[0]);
                         if (cta_amax[1] != 0ull) atomicOr(p.amax + 1, 1ull);
+                        if (p.world > 1) {
+                            // this CTA's logits stores to the other ranks precede its count;
+                            // the last CTA publishes the rank's argmax to every rank
+                            __threadfence_system();
+                            if (atomicAdd(p.done, 1u) == (unsigned)(p.ncta - 1)) {
+                                __threadfence();
+                                const unsigned long long k = *reinterpret_cast<volatile unsigned long long *>(p.amax);
+                                const unsigned long long nf = *reinterpret_cast<volatile unsigned long long *>(p.amax + 1);
+                                const uint64_t tg = (uint64_t)tag << 32;
+                                for (int q = 0; q < p.world; q++) {
+                                    uint64_t *slot = p.keys[q] + (size_t)p.rank * 4;
+                                    st_u64_sys(slot, tg | (k >> 32));
+                                    st_u64_sys(slot + 1, tg | (k & 0xFFFFFFFFull));
+                                    st_u64_sys(slot + 2, tg | (nf != 0ull ? 1ull : 0ull));
+                                }
+                                *p.done = 0u;
+                            }
+                        }
                     }
                 }
             } else if (tracing && threadIdx.x == 0) {
                 a.trace[3 * pi + 1] = global_ns();
+            }
+        } else if (p.kind == PH_AR) {
+            const int items = (p.own[p.rank] + (int)blockDim.x - 1) / (int)blockDim.x;
+            if (tracing && threadIdx.x == 0) a.trace[3 * pi + 1] = global_ns();
+            for (int it = (blockIdx.x + gridDim.x - p.off % gridDim.x) % gridDim.x; it < items; it += gridDim.x) {
+                ar_item(p, it, a.step, tag, a.err);
             }
         } else {
             const int n = a.step[1] + 1, nh = p.n_kv * p.kv_mul;
@@ -220,6 +244,50 @@ static unsigned phase_formats(const Phase &p)
     if (p.kind != PH_MV) return need;
     for (int i = 0; i < p.nseg; i++) need |= tbit(p.seg[i].type);
     return need;
+}
+
+// finish_kernel for a tensor-parallel rank: the greedy token is the best of
+// the ranks' argmax keys (each rank's logits phase published its key, as
+// tagged words, to every rank's slots [world][4]).
+__global__ void finish_kernel_tp(int *step, unsigned long long *amax, const uint64_t *keys, int world, int *tokens,
+                                 int cap, int *err)
+{
+    const uint32_t tag = (uint32_t)step[4];
+    unsigned long long best = 0ull;
+    bool bad = false;
+    for (int q = 0; q < world; q++) {
+        uint32_t v[3];
+        for (int i = 0; i < 3; i++) {
+            const uint64_t *w = keys + (size_t)q * 4 + i;
+            uint64_t x = ld_ll(w);
+            const long long t0 = clock64();
+            while (!ll_is(x, tag)) {
+                if (aborted(err) || clock64() - t0 > LL_WAIT_LIMIT_CYCLES) {
+                    atomicOr(err, ERR_TIMEOUT_WAIT);
+                    break;
+                }
+                x = ld_ll(w);
+            }
+            v[i] = (uint32_t)x;
+        }
+        const unsigned long long k = ((unsigned long long)v[0] << 32) | v[1];
+        if (k > best) best = k;
+        if (v[2] != 0u) bad = true;
+    }
+    int tok = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
+    if (bad || best == 0ull) {
+        tok = -1;
+        atomicOr(err, ERR_NONFINITE);
+    }
+    const int n = step[2];
+    if (n < cap) tokens[n] = tok;
+    step[3] = tok;
+    step[0] = tok < 0 ? 0 : tok;
+    step[1] = step[1] + 1;
+    step[2] = n + 1;
+    step[4] = step[4] + 1;
+    amax[0] = 0ull;
+    amax[1] = 0ull;
 }
 
 __global__ void dequant_kernel(const uint8_t *w, uint64_t rb, int type, uint64_t rows, uint64_t cols,
@@ -366,6 +434,10 @@ static int launch_phase(const Phase &p, const int *step, int *err, cudaStream_t 
         if (want < grid) grid = want;
     }
     if (grid < 1) grid = 1;
+    if (p.epi == EPI_LOGITS && p.world > 1) {  // the CTAs of this launch that hold logits tiles
+        a.one.ncta = 0;
+        for (int b = 0; b < grid; b++) a.one.ncta += cta_has_tiles(p, b, L.warps, grid * L.warps) ? 1 : 0;
+    }
     fn<<<grid, L.warps * 32, L.smem, st>>>(a);
     return cudaGetLastError() == cudaSuccess;
 }
@@ -669,6 +741,14 @@ struct PkdCtx {
     int use_graph;   // replay a captured graph (else launch directly)
     cudaGraph_t graph;
     cudaGraphExec_t exec;
+    // tensor parallel (tp.world > 1)
+    PkdTp tp;
+    uint64_t *peers[PKD_TP_MAX];  // each rank's exchange buffer (ll of that rank; peers[rank] = ll)
+    int peer_mapped[PKD_TP_MAX];  // opened through IPC
+    unsigned *lcount;             // logits CTAs finished
+    // the model, kept for a build deferred to pkd_tp_connect
+    PkdModel model;
+    PkdTensor *tensors;           // 9 * n_layers, owned copies of the model's arrays
     char msg[256];
 };
 
@@ -733,38 +813,56 @@ static void seg_of(MvSeg &s, const PkdCtx *c, const PkdTensor &t, int kind)
     s.kind = kind;
 }
 
-// Tagged activation words of one layer (offsets in words, each vector
-// starting on a 256-byte boundary).
+// Tagged activation words (offsets in words, each vector on a 256-byte
+// boundary): per layer q, k, v, the attention output, the receive buffer
+// of the Wo all-reduce, x after Wo, gate and up, the receive buffer of the
+// down all-reduce, x after down; then the ranks' argmax slots and the
+// logits (floats). The layout depends only on sizes common to all ranks, so
+// it is the same on every rank of a tensor-parallel group (peers write into
+// it at the same offsets).
 struct LLPlan {
-    size_t q, k, v, att, xmid, hb, xout, per_layer;
+    size_t q, k, v, att, rwo, xmid, hb, rdn, xout, per_layer;
+    size_t keys, logits, total;
 };
 
 static LLPlan ll_plan(const PkdModel *m)
 {
     auto r32 = [](size_t n) { return (n + 31) / 32 * 32; };
-    const size_t dim = (size_t)m->dim, kvd = dim / (size_t)m->n_heads * (size_t)m->n_kv_heads;
+    const PkdTp &t = m->tp;
+    const size_t dim = (size_t)m->dim, hs = (size_t)m->head_size;
+    const size_t qd = (size_t)t.q_heads * hs, kvd = (size_t)t.kv_heads * hs;
+    const size_t recv = t.world > 1 ? r32((size_t)t.world * (size_t)t.own_max) : 0;
     LLPlan p;
     p.q = 0;
-    p.k = p.q + r32(dim);
+    p.k = p.q + r32(qd);
     p.v = p.k + r32(kvd);
     p.att = p.v + r32(kvd);
-    p.xmid = p.att + r32(dim);
+    p.rwo = p.att + r32(qd);
+    p.xmid = p.rwo + recv;
     p.hb = p.xmid + r32(dim);
-    p.xout = p.hb + r32(2 * (size_t)m->hidden_dim);  // gate, then up
+    p.rdn = p.hb + r32(2 * (size_t)t.hid_max);  // gate, then up
+    p.xout = p.rdn + recv;
     p.per_layer = p.xout + r32(dim);
+    p.keys = p.per_layer * (size_t)m->n_layers;
+    p.logits = p.keys + r32(4 * (size_t)t.world);
+    p.total = p.logits + r32(((size_t)m->vocab_size + 1) / 2);
     return p;
 }
 
 // The phases of one decode step. Each phase's work starts where the
 // previous phase's ended (tile rotation), so small phases do not all land
-// on the first CTAs.
+// on the first CTAs. A tensor-parallel rank computes its heads, hidden
+// slice and vocabulary rows; Wo and down end in partial sums that an
+// all-reduce phase combines (two per layer).
 static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
 {
-    const int L = m->n_layers, dim = m->dim, hs = m->dim / m->n_heads;
-    const int kvd = hs * m->n_kv_heads, km = m->n_heads / m->n_kv_heads;
-    const int nsplit = attn_max_splits(m->n_heads, c->grid, m->seq_len);
+    const PkdTp &tp = m->tp;
+    const int L = m->n_layers, dim = m->dim, hs = m->head_size, W = tp.world;
+    const int kvd = hs * tp.kv_heads, qd = hs * tp.q_heads, km = tp.q_heads / tp.kv_heads;
+    const int nsplit = attn_max_splits(tp.q_heads, c->grid, m->seq_len);
     const LLPlan lp = ll_plan(m);
-    c->nphases = 5 * L + 1;
+    const int per = W > 1 ? 7 : 5;
+    c->nphases = per * L + 1;
     c->phases = (Phase *)calloc((size_t)c->nphases, sizeof(Phase));
     if (c->phases == NULL) return 0;
     const int cap = 8192;
@@ -773,11 +871,35 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
         p.off = acc;
         acc = (acc + p.ntiles) % nw_total;
     };
+    auto tp_common = [&](Phase &p) {
+        p.world = W;
+        p.rank = tp.rank;
+        p.own_max = tp.own_max;
+        for (int q = 0; q < W; q++) {
+            p.own0[q] = tp.own0[q];
+            p.own[q] = tp.own[q];
+        }
+    };
+    // all-reduce of the partials in recv (this rank's buffer) into `out`
+    // (the same vector on every rank); residual `res` (null: the embedding row)
+    auto all_reduce = [&](Phase &p, size_t recv, const uint64_t *res, size_t out) {
+        p.kind = PH_AR;
+        tp_common(p);
+        p.off = (acc + DK_WARPS - 1) / DK_WARPS;
+        p.xin_ll = c->ll + recv;
+        p.res_ll = res;
+        p.embd = c->arena + m->embd.offset;
+        p.embd_rb = m->embd.row_bytes;
+        p.embd_type = (int)m->embd.type;
+        for (int q = 0; q < W; q++) p.peer[q] = c->peers[q] + out;
+    };
     for (int l = 0; l < L; l++) {
-        uint64_t *ll = c->ll + (size_t)l * lp.per_layer;
-        const uint64_t *xin = l == 0 ? nullptr : c->ll + (size_t)(l - 1) * lp.per_layer + lp.xout;
-        Phase *P = c->phases + 5 * l;
-        Phase &qkv = P[0], &att = P[1], &wo = P[2], &up = P[3], &dn = P[4];
+        const size_t base = (size_t)l * lp.per_layer;
+        uint64_t *ll = c->ll + base;
+        const uint64_t *xin = l == 0 ? nullptr : c->ll + base - lp.per_layer + lp.xout;
+        Phase *P = c->phases + per * l;
+        Phase &qkv = P[0], &att = P[1], &wo = P[2];
+        Phase &up = P[W > 1 ? 4 : 3], &dn = P[W > 1 ? 5 : 4];
         qkv.kind = PH_MV;
         qkv.pro = l == 0 ? PRO_EMBED_NORM : PRO_NORM;
         qkv.epi = EPI_QKV;
@@ -814,30 +936,37 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
         att.kc = c->kc;
         att.vc = c->vc;
         att.part = c->part;
-        att.count = c->count + (size_t)l * m->n_heads;
+        att.count = c->count + (size_t)l * tp.q_heads;
         att.layer = l;
         att.seq_len = m->seq_len;
         att.kv_dim = kvd;
         att.hs = hs;
         att.kv_mul = km;
-        att.n_kv = m->n_kv_heads;
+        att.n_kv = tp.kv_heads;
         att.nsplit_max = nsplit;
         att.scale = m->att_scale;
 
         wo.kind = PH_MV;
         wo.pro = PRO_PLAIN;
-        wo.epi = EPI_ADD;
         wo.nseg = 1;
         seg_of(wo.seg[0], c, m->wo[l], KIND_PLAIN);
-        wo.cols = dim;
+        wo.cols = qd;
         wo.xin_ll = ll + lp.att;
-        wo.res_ll = xin;  // null on layer 0: the embedding row
-        wo.embd = c->arena + m->embd.offset;
-        wo.embd_rb = m->embd.row_bytes;
-        wo.embd_type = (int)m->embd.type;
-        wo.y_ll = ll + lp.xmid;
+        if (W > 1) {
+            wo.epi = EPI_PEER;
+            tp_common(wo);
+            for (int q = 0; q < W; q++) wo.peer[q] = c->peers[q] + base + lp.rwo;
+        } else {
+            wo.epi = EPI_ADD;
+            wo.res_ll = xin;  // null on layer 0: the embedding row
+            wo.embd = c->arena + m->embd.offset;
+            wo.embd_rb = m->embd.row_bytes;
+            wo.embd_type = (int)m->embd.type;
+            wo.y_ll = ll + lp.xmid;
+        }
         tile_phase(wo, nw_total, cap, false);
         rotate(wo);
+        if (W > 1) all_reduce(P[3], base + lp.rwo, xin, base + lp.xmid);
 
         // gate and up as two row sets of one phase: gate rows to hb[0, hid),
         // up rows to hb[hid, 2 hid); the down phase stages silu(gate) * up
@@ -858,17 +987,24 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
 
         dn.kind = PH_MV;
         dn.pro = PRO_SWIGLU;
-        dn.epi = EPI_ADD;
         dn.nseg = 1;
         seg_of(dn.seg[0], c, m->down[l], KIND_PLAIN);
         dn.cols = m->hidden_dim;
         dn.xin_ll = ll + lp.hb;
-        dn.res_ll = ll + lp.xmid;
-        dn.y_ll = ll + lp.xout;
+        if (W > 1) {
+            dn.epi = EPI_PEER;
+            tp_common(dn);
+            for (int q = 0; q < W; q++) dn.peer[q] = c->peers[q] + base + lp.rdn;
+        } else {
+            dn.epi = EPI_ADD;
+            dn.res_ll = ll + lp.xmid;
+            dn.y_ll = ll + lp.xout;
+        }
         tile_phase(dn, nw_total, cap, false);
         rotate(dn);
+        if (W > 1) all_reduce(P[6], base + lp.rdn, ll + lp.xmid, base + lp.xout);
     }
-    Phase &lg = c->phases[5 * L];
+    Phase &lg = c->phases[per * L];
     lg.kind = PH_MV;
     lg.pro = PRO_NORM;
     lg.epi = EPI_LOGITS;
@@ -882,6 +1018,16 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
     lg.amax = c->amax_d;
     tile_phase(lg, nw_total, cap, false);
     rotate(lg);
+    if (W > 1) {
+        tp_common(lg);
+        lg.voc0 = tp.voc0;
+        for (int q = 0; q < W; q++) {
+            lg.peer[q] = c->peers[q] + lp.logits;
+            lg.keys[q] = c->peers[q] + lp.keys;
+        }
+        lg.done = c->lcount;
+        for (int b = 0; b < c->grid; b++) lg.ncta += cta_has_tiles(lg, b, DK_WARPS, nw_total) ? 1 : 0;
+    }
     return 1;
 }
 
@@ -920,7 +1066,12 @@ static int record_step(PkdCtx *c)
             }
         }
     }
-    finish_kernel<<<1, 1, 0, st>>>(c->step_d, c->amax_d, c->tokens_d, c->tokens_cap, c->err_d);
+    if (c->tp.world > 1) {
+        finish_kernel_tp<<<1, 1, 0, st>>>(c->step_d, c->amax_d, c->ll + ll_plan(&c->model).keys, c->tp.world,
+                                          c->tokens_d, c->tokens_cap, c->err_d);
+    } else {
+        finish_kernel<<<1, 1, 0, st>>>(c->step_d, c->amax_d, c->tokens_d, c->tokens_cap, c->err_d);
+    }
     return cudaGetLastError() == cudaSuccess;
 }
 
@@ -930,29 +1081,29 @@ static int env_flag(const char *name, int dflt)
     return (v != NULL && *v) ? atoi(v) != 0 : dflt;
 }
 
+static int finalize(PkdCtx *c, char *err, size_t cap);
+
 extern "C" int pkd_build(PkdCtx *c, const PkdModel *m, char *err, size_t cap)
 {
-    const size_t dim = (size_t)m->dim, hid = (size_t)m->hidden_dim;
-    const size_t hs = dim / (size_t)m->n_heads, kvd = hs * (size_t)m->n_kv_heads;
+    const size_t dim = (size_t)m->dim, hs = (size_t)m->head_size, kvd = hs * (size_t)m->n_kv_heads;
     const size_t cache = (size_t)m->n_layers * (size_t)m->seq_len * kvd;
     const size_t nnorm = (2 * (size_t)m->n_layers + 1) * dim;
-    if ((size_t)m->rope_dim > hs || hs % 4 || hs > 256) {
+    if ((size_t)m->rope_dim > hs || hs % 4 || hs > 256 || hs * (size_t)m->tp.q_heads > dim) {
         if (err && cap) snprintf(err, cap, "Unsupported model shape.");
         return 0;
     }
     cudaSetDevice(c->device);
     const int nsplit = attn_max_splits(m->n_heads, sm_count(), m->seq_len);
     const size_t part = (size_t)m->n_heads * nsplit * (hs + 2);
-    const size_t ll_words = ll_plan(m).per_layer * (size_t)m->n_layers;
-    (void)hid;
-    if (cuda_fail(c, cudaMalloc(&c->ll, ll_words * 8), "cudaMalloc", err, cap) ||
-        cuda_fail(c, cudaMalloc(&c->logits, (size_t)m->vocab_size * 4), "cudaMalloc", err, cap) ||
+    const LLPlan lp = ll_plan(m);
+    if (cuda_fail(c, cudaMalloc(&c->ll, lp.total * 8), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->kc, cache * 4), "cudaMalloc(KV cache)", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->vc, cache * 4), "cudaMalloc(KV cache)", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->part, part * 4), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->norms, nnorm * 4), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->rope_cs, (size_t)m->seq_len * m->rope_dim * 4 + 4), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->count, (size_t)m->n_layers * m->n_heads * 4), "cudaMalloc", err, cap) ||
+        cuda_fail(c, cudaMalloc(&c->lcount, 16), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->step_d, 32), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->err_d, 16), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->amax_d, 16), "cudaMalloc", err, cap) ||
@@ -964,15 +1115,19 @@ extern "C" int pkd_build(PkdCtx *c, const PkdModel *m, char *err, size_t cap)
         cuda_fail(c, cudaMallocHost(&c->err_h, 16), "cudaMallocHost", err, cap)) {
         return 0;
     }
+    c->logits = reinterpret_cast<float *>(c->ll + lp.logits);  // other ranks write their shards here
     c->vocab = m->vocab_size;
     c->tokens_cap = m->seq_len;
+    c->tp = m->tp;
+    c->peers[m->tp.rank] = c->ll;
     cudaStream_t st = c->stream;
     cudaMemsetAsync(c->kc, 0, cache * 4, st);
     cudaMemsetAsync(c->vc, 0, cache * 4, st);
     cudaMemsetAsync(c->count, 0, (size_t)m->n_layers * m->n_heads * 4, st);
+    cudaMemsetAsync(c->lcount, 0, 16, st);
     cudaMemsetAsync(c->err_d, 0, 16, st);
     cudaMemsetAsync(c->amax_d, 0, 16, st);
-    cudaMemsetAsync(c->ll, 0, ll_words * 8, st);  // tag 0: never a step's tag
+    cudaMemsetAsync(c->ll, 0, lp.total * 8, st);  // tag 0: never a step's tag
     memset(c->step_h, 0, 32);
     c->step_h[4] = 1;  // the first step's tag
     cudaMemcpyAsync(c->step_d, c->step_h, 32, cudaMemcpyHostToDevice, st);
@@ -995,17 +1150,72 @@ extern "C" int pkd_build(PkdCtx *c, const PkdModel *m, char *err, size_t cap)
         cuda_fail(c, cudaStreamSynchronize(st), "build sync", err, cap)) {
         return 0;
     }
-
-    // Phases and shared-memory layout.
-    c->persistent = env_flag("POCKET_CUDA_PERSISTENT", 1);
-    if (env_flag("POCKET_CUDA_TRACE", 0) &&
-        cuda_fail(c, cudaMalloc(&c->trace_d, (size_t)(3 * (5 * m->n_layers + 1) + 1) * 8), "cudaMalloc", err, cap)) {
+    // Keep the model description for the step (built now, or at connect).
+    const int L = m->n_layers;
+    c->tensors = (PkdTensor *)malloc(9 * (size_t)L * sizeof(PkdTensor));
+    if (c->tensors == NULL) {
+        if (err && cap) snprintf(err, cap, "Out of memory.");
         return 0;
     }
+    const PkdTensor *src[9] = {m->wq, m->wk, m->wv, m->wo, m->gate, m->up, m->down, m->attn_norm, m->ffn_norm};
+    for (int j = 0; j < 9; j++) memcpy(c->tensors + (size_t)j * L, src[j], (size_t)L * sizeof(PkdTensor));
+    c->model = *m;
+    c->model.wq = c->tensors;
+    c->model.wk = c->tensors + L;
+    c->model.wv = c->tensors + 2 * L;
+    c->model.wo = c->tensors + 3 * L;
+    c->model.gate = c->tensors + 4 * L;
+    c->model.up = c->tensors + 5 * L;
+    c->model.down = c->tensors + 6 * L;
+    c->model.attn_norm = c->tensors + 7 * L;
+    c->model.ffn_norm = c->tensors + 8 * L;
+    c->model.rope_cs = nullptr;
+    return m->tp.world > 1 ? 1 : finalize(c, err, cap);
+}
+
+extern "C" int pkd_tp_handle(PkdCtx *c, void *out64, char *err, size_t cap)
+{
+    if (c == NULL || out64 == NULL || c->tp.world < 2) return 0;
+    cudaSetDevice(c->device);
+    cudaIpcMemHandle_t h;
+    if (cuda_fail(c, cudaIpcGetMemHandle(&h, c->ll), "cudaIpcGetMemHandle", err, cap)) return 0;
+    static_assert(sizeof(h) == 64, "exchange handles are 64 bytes");
+    memcpy(out64, &h, 64);
+    return 1;
+}
+
+extern "C" int pkd_tp_connect(PkdCtx *c, const void *handles, char *err, size_t cap)
+{
+    if (c == NULL || handles == NULL || c->tp.world < 2) return 0;
+    cudaSetDevice(c->device);
+    for (int q = 0; q < c->tp.world; q++) {
+        if (q == c->tp.rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, (const uint8_t *)handles + 64 * (size_t)q, 64);
+        void *ptr = nullptr;
+        if (cuda_fail(c, cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle",
+                      err, cap))
+            return 0;
+        c->peers[q] = (uint64_t *)ptr;
+        c->peer_mapped[q] = 1;
+    }
+    return finalize(c, err, cap);
+}
+
+// Phases, shared-memory plan, kernel variant and the captured step.
+static int finalize(PkdCtx *c, char *err, size_t cap)
+{
+    const PkdModel *m = &c->model;
+    cudaStream_t st = c->stream;
+    c->persistent = env_flag("POCKET_CUDA_PERSISTENT", 1);
     c->use_graph = !env_flag("POCKET_CUDA_EAGER", 0);
     c->grid = sm_count();
     if (!build_phases(c, m, c->grid * DK_WARPS)) {
         if (err && cap) snprintf(err, cap, "Out of memory.");
+        return 0;
+    }
+    if (env_flag("POCKET_CUDA_TRACE", 0) &&
+        cuda_fail(c, cudaMalloc(&c->trace_d, (size_t)(3 * c->nphases + 1) * 8), "cudaMalloc", err, cap)) {
         return 0;
     }
     unsigned need = 0u;
@@ -1018,7 +1228,7 @@ extern "C" int pkd_build(PkdCtx *c, const PkdModel *m, char *err, size_t cap)
         const int need = stage_need(c->phases[i]);
         if (need > stage) stage = need;
     }
-    const int attn_floats = attn_scratch_floats((int)hs, DK_WARPS);
+    const int attn_floats = attn_scratch_floats(m->head_size, DK_WARPS);
     if (!make_layout(c->layout, max_units, stage, attn_floats, 4)) {
         if (err && cap) snprintf(err, cap, "Model rows or context too large for the shared-memory plan.");
         return 0;
@@ -1168,7 +1378,11 @@ extern "C" void pkd_destroy(PkdCtx *c)
     if (c->graph) cudaGraphDestroy(c->graph);
     if (c->ev0) cudaEventDestroy(c->ev0);
     if (c->ev1) cudaEventDestroy(c->ev1);
-    void *dev[] = {c->arena, c->ll, c->logits, c->kc, c->vc, c->part, c->norms,
+    for (int q = 0; q < PKD_TP_MAX; q++) {
+        if (c->peer_mapped[q]) cudaIpcCloseMemHandle(c->peers[q]);
+    }
+    free(c->tensors);
+    void *dev[] = {c->arena, c->ll, c->lcount, c->kc, c->vc, c->part, c->norms,
                    c->rope_cs, c->count, c->step_d, c->err_d, c->amax_d, c->tokens_d, c->phases_d,
                    c->trace_d};
     for (size_t i = 0; i < sizeof(dev) / sizeof(dev[0]); i++) {

@@ -29,10 +29,14 @@
 namespace pk {
 
 constexpr long long WAIT_LIMIT_CYCLES = 4000000000LL;  // ~2 s at 2 GHz
+// Tagged words may come from another GPU whose step started later (ranks
+// launch independently): a longer bound.
+constexpr long long LL_WAIT_LIMIT_CYCLES = 20000000000LL;  // ~10 s at 2 GHz
+constexpr int TP_MAX = 8;  // ranks of a tensor-parallel group
 
-enum { PH_MV = 0, PH_ATTN = 1 };
+enum { PH_MV = 0, PH_ATTN = 1, PH_AR = 2 };
 enum { PRO_PLAIN = 0, PRO_NORM = 1, PRO_EMBED_NORM = 2, PRO_SWIGLU = 3 };
-enum { EPI_STORE = 0, EPI_ADD = 1, EPI_QKV = 2, EPI_LOGITS = 4 };
+enum { EPI_STORE = 0, EPI_ADD = 1, EPI_QKV = 2, EPI_LOGITS = 4, EPI_PEER = 5 };
 enum { KIND_PLAIN = 0, KIND_Q = 1, KIND_K = 2, KIND_V = 3 };
 enum { ERR_TIMEOUT_MV = 1, ERR_TIMEOUT_WAIT = 2, ERR_NONFINITE = 4 };
 constexpr int ERR_FATAL = ERR_TIMEOUT_MV | ERR_TIMEOUT_WAIT;
@@ -117,6 +121,18 @@ __device__ __forceinline__ void st_ll(uint64_t *p, float v, uint32_t tag)
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
+// The same, for words another GPU reads (system scope).
+__device__ __forceinline__ void st_ll_sys(uint64_t *p, float v, uint32_t tag)
+{
+    const uint64_t w = ((uint64_t)tag << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ void st_u64_sys(uint64_t *p, uint64_t w)
+{
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
 __device__ __forceinline__ uint64_t ld_ll(const uint64_t *p)
 {
     uint64_t w;
@@ -151,7 +167,7 @@ __device__ __forceinline__ float ll_read(const uint64_t *p, uint32_t tag, int *e
         w = ld_ll(p);
         if (ll_is(w, tag)) break;
         if (aborted(err)) break;
-        if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+        if (clock64() - t0 > LL_WAIT_LIMIT_CYCLES) {
             atomicOr(err, ERR_TIMEOUT_WAIT);
             break;
         }
@@ -181,7 +197,7 @@ __device__ __forceinline__ void ll_read8(const uint64_t *p, int n, uint32_t tag,
         if (first) {
             t0 = clock64();
             first = false;
-        } else if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+        } else if (clock64() - t0 > LL_WAIT_LIMIT_CYCLES) {
             atomicOr(err, ERR_TIMEOUT_WAIT);
             break;
         }
@@ -251,6 +267,15 @@ struct Phase {
     unsigned *count;
     int kv_mul, n_kv, nsplit_max;
     float scale;
+    // tensor parallel (world > 1)
+    int world, rank, own_max;
+    int own0[TP_MAX], own[TP_MAX];  // rank q reduces elements [own0[q], own0[q] + own[q])
+    uint64_t *peer[TP_MAX];   // EPI_PEER: each rank's receive buffer [world][own_max];
+                              // PH_AR: each rank's output vector; EPI_LOGITS: each rank's logits
+    uint64_t *keys[TP_MAX];   // EPI_LOGITS: each rank's argmax slots [world][4]
+    int voc0;                 // EPI_LOGITS: vocabulary row of local row 0
+    unsigned *done;           // EPI_LOGITS: CTAs finished; the last publishes the argmax
+    int ncta;                 // EPI_LOGITS: CTAs with logits tiles
 };
 
 // Tile k (0, 1, ...) of warp gw among nw warps (>= ntiles: none).
@@ -656,9 +681,13 @@ __device__ __forceinline__ void run_tile(const Phase &p, int t, const uint8_t *b
         unsigned long long key = 0ull;
         bool bad = false;
         if (lane < nr) {
-            p.y[r] = va;
+            const int gr = p.voc0 + r;  // vocabulary index
+            p.y[gr] = va;
+            for (int q = 0; q < p.world; q++) {
+                if (q != p.rank) reinterpret_cast<float *>(p.peer[q])[gr] = va;
+            }
             if (isfinite(va)) {
-                key = ((unsigned long long)order_key(va) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)r);
+                key = ((unsigned long long)order_key(va) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)gr);
             } else {
                 bad = true;
             }
@@ -670,6 +699,13 @@ __device__ __forceinline__ void run_tile(const Phase &p, int t, const uint8_t *b
         }
         if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) cta_amax[1] = 1ull;
         if (lane == 0 && key != 0ull) atomicMax(cta_amax, key);
+    } else if (p.epi == EPI_PEER) {
+        // partial row of a split matrix: to the rank that reduces it
+        if (lane < nr) {
+            int q = 0;
+            while (q + 1 < p.world && r >= p.own0[q + 1]) q++;
+            st_ll_sys(p.peer[q] + (size_t)p.rank * p.own_max + (r - p.own0[q]), va, tag);
+        }
     } else if (lane < nr) {
         float out = va;
         if (p.epi == EPI_ADD) {
@@ -685,6 +721,28 @@ __device__ __forceinline__ void run_tile(const Phase &p, int t, const uint8_t *b
             p.y[s.yoff + r] = out;
         }
     }
+}
+
+// ------------------------------------------------------------------ //
+// All-reduce over the tensor-parallel ranks                          //
+// ------------------------------------------------------------------ //
+
+// Item it of an all-reduce phase on this rank: elements
+// [it * blockDim.x, ...) of the slice it reduces. Each element is the sum,
+// in rank order, of the ranks' partials (tagged words the ranks' EPI_PEER
+// epilogues wrote to this rank's receive buffer xin_ll[q][e]) plus the
+// residual, and goes as a tagged word to every rank's output vector.
+__device__ __forceinline__ void ar_item(const Phase &p, int it, const int *step, uint32_t tag, int *err)
+{
+    const int e = it * blockDim.x + threadIdx.x;
+    if (e >= p.own[p.rank]) return;
+    const int g = p.own0[p.rank] + e;  // element of the full vector
+    float sum = ll_read(p.xin_ll + e, tag, err);
+    for (int q = 1; q < p.world; q++) sum = __fadd_rn(sum, ll_read(p.xin_ll + (size_t)q * p.own_max + e, tag, err));
+    const float res = p.res_ll != nullptr ? ll_read(p.res_ll + g, tag, err)
+                                          : decode_col_call(p.embd_type, p.embd + (size_t)step[0] * p.embd_rb, g);
+    const float out = __fadd_rn(res, sum);
+    for (int q = 0; q < p.world; q++) st_ll_sys(p.peer[q] + g, out, tag);
 }
 
 // ------------------------------------------------------------------ //

@@ -27,6 +27,7 @@ EXPORTS = [
     "engine_format", "engine_tokenizer", "engine_kv_cache_bytes", "engine_description",
     "engine_is_stop_token", "engine_open_device", "engine_forward_greedy", "engine_last_error",
     "engine_weight_bytes", "engine_generate_greedy", "engine_trace", "engine_launches_per_step",
+    "engine_tp_plan", "engine_open_tp", "engine_tp_handle", "engine_tp_connect",
     "gguf_cuda_matvec", "gguf_cuda_dequantize_rows", "gguf_cuda_fp16_table", "gguf_cuda_matvec_noalloc",
     "tokenizer_free",
 ]
@@ -64,6 +65,11 @@ class Tokenizer(ctypes.Structure):
                 ("bos_id", ctypes.c_int), ("eos_id", ctypes.c_int), ("byte_ids", ctypes.c_int * 256),
                 ("special_ids", ctypes.POINTER(ctypes.c_int)), ("n_special", ctypes.c_size_t),
                 ("scores_reconstructed", ctypes.c_int)]
+
+
+class EngineTpPlan(ctypes.Structure):  # include/engine_ext.h
+    _fields_ = [(n, ctypes.c_int) for n in ("q_head0", "q_heads", "kv_head0", "kv_heads", "hid0", "hid",
+                                             "voc0", "voc", "own0", "own")]
 
 
 class GGUFWeight(ctypes.Structure):
@@ -118,6 +124,15 @@ def lib(path=LIB_PATH):
     L.engine_trace.argtypes = [_P, _P, ctypes.c_int]
     L.engine_launches_per_step.restype = ctypes.c_int
     L.engine_launches_per_step.argtypes = [_P]
+    L.engine_tp_plan.restype = ctypes.c_int
+    L.engine_tp_plan.argtypes = [ctypes.c_int] * 9 + [ctypes.POINTER(EngineTpPlan), ctypes.c_char_p, ctypes.c_size_t]
+    L.engine_open_tp.restype = _P
+    L.engine_open_tp.argtypes = [ctypes.POINTER(LLMOptions), ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                 ctypes.c_char_p, ctypes.c_size_t]
+    L.engine_tp_handle.restype = ctypes.c_int
+    L.engine_tp_handle.argtypes = [_P, _P]
+    L.engine_tp_connect.restype = ctypes.c_int
+    L.engine_tp_connect.argtypes = [_P, _P, ctypes.c_char_p, ctypes.c_size_t]
     L.gguf_cuda_matvec.restype = ctypes.c_int
     L.gguf_cuda_matvec.argtypes = [ctypes.POINTER(GGUFWeight), _P, _P, _P]
     L.gguf_cuda_dequantize_rows.restype = ctypes.c_int
@@ -135,13 +150,15 @@ def lib(path=LIB_PATH):
 class Engine:
     """One engine_open() handle."""
 
-    def __init__(self, path, max_context=0, device=None, tokenizer_path=None):
+    def __init__(self, path, max_context=0, device=None, tokenizer_path=None, rank=0, world=1):
         L = lib()
         self._path = path.encode()
         self._tok = tokenizer_path.encode() if tokenizer_path else None
         opts = LLMOptions(self._path, self._tok, max_context)
         err = ctypes.create_string_buffer(512)
-        if device is None:
+        if world > 1:
+            self.h = L.engine_open_tp(ctypes.byref(opts), 0 if device is None else device, rank, world, err, 512)
+        elif device is None:
             self.h = L.engine_open(ctypes.byref(opts), err, 512)
         else:
             self.h = L.engine_open_device(ctypes.byref(opts), device, err, 512)
@@ -151,6 +168,20 @@ class Engine:
         self.config = {n: getattr(c, n) for n, _ in Config._fields_}
         self.vocab_size = c.vocab_size
         self.seq_len = c.seq_len
+
+    def tp_handle(self):
+        """This rank's 64-byte exchange handle (tensor-parallel handles)."""
+        out = ctypes.create_string_buffer(64)
+        if lib().engine_tp_handle(self.h, out) != 1:
+            raise RuntimeError("engine_tp_handle failed: " + self.last_error())
+        return out.raw
+
+    def tp_connect(self, handles):
+        """Connect with the ranks' handles (bytes of world * 64, rank order)."""
+        err = ctypes.create_string_buffer(512)
+        buf = ctypes.create_string_buffer(bytes(handles), len(handles))
+        if lib().engine_tp_connect(self.h, buf, err, 512) != 1:
+            raise RuntimeError("engine_tp_connect failed: " + err.value.decode())
 
     def forward(self, token, pos):
         """Logits as a fresh numpy array, or None when engine_forward returns NULL."""
@@ -220,6 +251,27 @@ class Engine:
             self.close()
         except Exception:
             pass
+
+
+def tp_plan(dim, hidden_dim, n_heads, n_kv_heads, vocab_size, wo_block, down_block, rank, world):
+    """engine_tp_plan as a dict; ValueError with the library's message when the split is impossible."""
+    out = EngineTpPlan()
+    err = ctypes.create_string_buffer(256)
+    if lib().engine_tp_plan(dim, hidden_dim, n_heads, n_kv_heads, vocab_size, wo_block, down_block, rank, world,
+                            ctypes.byref(out), err, 256) != 1:
+        raise ValueError(err.value.decode())
+    return {n: getattr(out, n) for n, _ in EngineTpPlan._fields_}
+
+
+def tp_exchange(handle, world):
+    """All-gather the ranks' 64-byte exchange handles in rank order over the
+    default torch.distributed group (any backend)."""
+    import torch.distributed as dist
+    out = [None] * world
+    dist.all_gather_object(out, bytes(handle))
+    if any(o is None or len(o) != 64 for o in out):
+        raise RuntimeError("tensor-parallel handle exchange failed")
+    return b"".join(out)
 
 
 def make_weight(dev_ptr, qtype, rows, cols):

@@ -65,6 +65,10 @@ PRESETS = {
                         t_embd=Q8_0, t_output=Q4_0, t_q=Q4_0, t_k=Q8_0, t_v_even=Q4_0,
                         t_v_odd=Q8_0, t_o=Q8_0, t_gate=Q4_0, t_up=Q8_0, t_down_even=Q4_0,
                         t_down_odd=Q8_0),
+    # Tensor-parallel parity: head and hidden splits on whole Q4_K blocks
+    # for 2 and 4 ranks (512 / 256 Wo columns, 8 hidden blocks), 3 layers.
+    "tp-q4km": dict(dim=1024, hidden_dim=2048, n_layers=3, n_heads=8, n_kv_heads=2,
+                    vocab_size=2048, context_length=512, rope_theta=10000.0, **_q4km()),
     "tiny-float": dict(dim=128, hidden_dim=256, n_layers=2, n_heads=4, n_kv_heads=2,
                        vocab_size=300, context_length=128, rope_theta=10000.0,
                        t_embd=F16, t_output=F32, t_q=F32, t_k=F16, t_v_even=F32, t_v_odd=F16,
