@@ -182,7 +182,8 @@ def run_reference_arm(args, wl):
         return 0
     line = {"metric": "decode tok/s (B=1)", "value": base["value"], "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / base["value"],
-            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": base["value"] / PUBLISHED_TOKS,
+            "higher_is_better": True, "scaling": "strong" if args.gpus > 1 else "weak",
+            "vs_baseline": base["value"] / PUBLISHED_TOKS,
             "dtype": "f32 (packed Q4_K/Q6_K weights)", "data": "synthetic random-init weights, seeded prompt",
             "config": cfg_line, "impl": "reference", "cpu_baseline": base,
             "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}

@@ -32,7 +32,9 @@ namespace pk {
 
 constexpr int DK_WARPS = 12;      // warps per CTA of phase_kernel
 constexpr int RMAX = 8;           // rows per tile (per matrix)
-constexpr int SMEM_LIMIT = 227 * 1024;
+constexpr int SMEM_LIMIT = 227 * 1024;  // shared memory per block (opt-in maximum) of sm_100
+
+int smem_dynamic_max();
 
 struct DecodeArgs {
     Phase one;             // the phase to run when `phases` is null
@@ -106,8 +108,9 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
                 if (p.epi == EPI_LOGITS && threadIdx.x == 0) cta_amax[0] = cta_amax[1] = 0ull;
                 stage_x(p, a.step, xq, xg, tag, a.err);  // ends with __syncthreads
                 if (tracing && threadIdx.x == 0) a.trace[3 * pi + 1] = global_ns();
+                float racc = 0.0f;  // a chunked row's running sum
                 for (int k = 0;; k++) {
-                    const int t = tile_at(p, gw, NW, k);
+                    const int t = tile_at(p, gw, NW, k / p.nchunk);
                     if (t >= p.ntiles) break;
                     const uint32_t slot = r.consumed % (uint32_t)a.stages;
                     const uint32_t par = (r.consumed / (uint32_t)a.stages) & 1u;
@@ -117,8 +120,8 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
                     if (!ok) {
                         if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_MV);
                     } else {
-                        run_tile<MASK>(p, t, r.buf + slot * a.stage_bytes, xq, xg, a.step, rope, tag, a.err, lane,
-                                       cta_amax);
+                        run_tile<MASK>(p, t, k % p.nchunk, r.buf + slot * a.stage_bytes, xq, xg, a.step, rope, tag,
+                                       a.err, lane, cta_amax, racc);
                     }
                     __syncwarp();
                     r.consumed++;
@@ -226,6 +229,25 @@ static const Variant VARIANTS[] = {
     PK_VARIANT(FMT_ALL),
 };
 #undef PK_VARIANT
+
+// Dynamic shared memory a phase kernel can use: the device's opt-in
+// per-block maximum minus the kernels' static shared memory (queried once).
+int smem_dynamic_max()
+{
+    static int v = 0;
+    if (v == 0) {
+        int dev = 0, optin = 0;
+        cudaFuncAttributes fa;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+            cudaFuncGetAttributes(&fa, phase_kernel<FMT_ALL>) != cudaSuccess) {
+            cudaGetLastError();
+            return SMEM_LIMIT - 4096;  // no device to ask: a conservative plan
+        }
+        v = optin - (int)fa.sharedSizeBytes;
+    }
+    return v;
+}
 
 // The first (smallest) variant that has every format in `need`.
 static PhaseFn pick_variant(unsigned need)
@@ -339,18 +361,35 @@ static int sm_count()
 }
 
 // Rows per tile and tile numbering of a matvec phase, for `nw_total` warps
-// and stages of at most `cap` bytes. even: tiles hold whole RoPE pairs.
+// and stages of at most `cap` bytes. even: tiles hold whole RoPE pairs. A
+// one-matrix phase whose rows do not fit a stage streams each row in column
+// chunks of whole quant blocks (one row per tile).
 static void tile_phase(Phase &p, int nw_total, int cap, bool even)
 {
     int total_rows = 0;
     for (int i = 0; i < p.nseg; i++) total_rows += p.seg[i].rows;
     const int r_par = (total_rows + nw_total - 1) / nw_total;
+    p.nunits = (p.cols + 63) / 64;
+    p.nchunk = 1;
+    p.cunits = p.nunits;
+    p.cbytes = 0;
+    if (p.nseg == 1 && p.seg[0].rb + 32 > (uint64_t)cap) {
+        const int type = p.seg[0].type, bw = block_weights(type), bb = block_bytes(type);
+        // granule: the fewest whole units that are whole blocks
+        const int gu = bw >= 64 ? bw / 64 : 1;
+        const int gb = bw >= 64 ? bb : (64 / bw) * bb;
+        int ng = (cap - 32 - 16) / gb;  // 16: a chunk may start off a 16-byte boundary
+        if (ng < 1) ng = 1;
+        p.cunits = ng * gu;
+        p.cbytes = ng * gb;
+        p.nchunk = (p.nunits + p.cunits - 1) / p.cunits;
+    }
     int t = 0;
     for (int i = 0; i < p.nseg; i++) {
         MvSeg &s = p.seg[i];
-        int R = (int)((uint64_t)(cap - 32) / s.rb);
-        if (R > r_par) R = r_par;
-        if (even && (R & 1)) R++;
+        const int rcap = p.nchunk > 1 ? 1 : (int)((uint64_t)(cap - 32) / s.rb);
+        int R = rcap < r_par ? rcap : r_par;
+        if (even && (R & 1)) R = R + 1 <= rcap ? R + 1 : R - 1;  // whole RoPE pairs, within the stage
         if (R < (even ? 2 : 1)) R = even ? 2 : 1;
         if (R > RMAX) R = RMAX;
         s.R = R;
@@ -358,19 +397,33 @@ static void tile_phase(Phase &p, int nw_total, int cap, bool even)
         t += (s.rows + R - 1) / R;
     }
     p.ntiles = t;
-    p.nunits = (p.cols + 63) / 64;
 }
 
-// Bytes a stage needs to hold a tile of the phase.
+// Bytes a stage needs to hold a tile (or a chunk) of the phase.
 static int stage_need(const Phase &p)
 {
     int need = 0;
     for (int i = 0; i < p.nseg; i++) {
         const MvSeg &s = p.seg[i];
-        const int b = (int)(((uint64_t)s.R * s.rb + 32 + 127) / 128 * 128);
+        const uint64_t bytes = p.nchunk > 1 ? (uint64_t)p.cbytes + 16 : (uint64_t)s.R * s.rb;
+        const int b = (int)((bytes + 32 + 127) / 128 * 128);
         if (b > need) need = b;
     }
     return need;
+}
+
+// Largest stage that leaves room for x in integer form (max_units units),
+// the attention scratch and two stages per warp: at most 8 KB.
+static int stage_cap(int max_units, int attn_floats)
+{
+    const int xq = (max_units * XQ_UNIT_BYTES + 127) / 128 * 128;
+    int xs = xq + (max_units * 4 * XG_UNIT_WORDS + 127) / 128 * 128;
+    const int at = (attn_floats * 4 + 127) / 128 * 128;
+    if (at > xs) xs = at;
+    const int bars = (DK_WARPS * 2 * 8 + 127) / 128 * 128;
+    int cap = (smem_dynamic_max() - bars - xs) / (2 * DK_WARPS) / 128 * 128;
+    if (cap > 8192) cap = 8192;
+    return cap;
 }
 
 struct Layout {
@@ -391,7 +444,7 @@ static bool make_layout(Layout &L, int max_units, int stage, int attn_floats, in
         for (L.stages = max_stages; L.stages >= 2; L.stages--) {
             L.bar_bytes = (L.warps * L.stages * 8 + 127) / 128 * 128;
             L.smem = (size_t)L.bar_bytes + L.xs_bytes + (size_t)L.warps * L.stages * stage;
-            if (L.smem <= (size_t)SMEM_LIMIT - 1024) return true;
+            if (L.smem <= (size_t)smem_dynamic_max()) return true;
         }
     }
     return false;
@@ -426,8 +479,10 @@ static int launch_phase(const Phase &p, const int *step, int *err, cudaStream_t 
     const int stage = p.kind == PH_MV ? stage_need(p) : 128;
     if (!make_layout(L, p.kind == PH_MV ? p.nunits : 1, stage, attn_floats, 3)) return 0;
     fill_args(a, L);
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem) != cudaSuccess) {
+        cudaGetLastError();  // a refused plan is not a context error
         return 0;
+    }
     int grid = grid_cap;
     if (p.kind == PH_MV) {
         const int want = (p.ntiles + L.warps - 1) / L.warps;
@@ -495,7 +550,7 @@ extern "C" int gguf_cuda_matvec(const GGUFWeight *weight, const float *x, float 
     p.cols = (int)weight->cols;
     p.xin = x;
     p.y = out;
-    tile_phase(p, sm_count() * DK_WARPS, 8192, false);
+    tile_phase(p, sm_count() * DK_WARPS, stage_cap((p.cols + 63) / 64, 0), false);
     Layout L;
     if (!make_layout(L, p.nunits, stage_need(p), 0, 3)) {
         if (weight->type != T_F32 && weight->type != T_F16) return 0;
@@ -588,15 +643,18 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) na_matvec_kernel(const __gri
     for (int i = threadIdx.x; i < ng; i += blockDim.x) reinterpret_cast<uint4 *>(xg)[i] = __ldcg(sg + i);
     __syncthreads();
 
-    for (int t = gw; t < p.ntiles; t += NW) {
+    float racc = 0.0f;
+    for (int k = 0;; k++) {
+        const int t = tile_at(p, gw, NW, k / p.nchunk);
+        if (t >= p.ntiles) break;
         const uint32_t slot = r.consumed % (uint32_t)a.stages;
         const uint32_t par = (r.consumed / (uint32_t)a.stages) & 1u;
         const bool ok = __all_sync(0xFFFFFFFFu, !aborted(a.err) && mbar_wait_bounded(r.bars + slot, par));
         if (!ok) {
             if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_MV);
         } else {
-            run_tile<FMT_ALL>(p, t, r.buf + slot * a.stage_bytes, xq, xg, nullptr, nullptr, 0u, a.err, lane,
-                     nullptr);
+            run_tile<FMT_ALL>(p, t, k % p.nchunk, r.buf + slot * a.stage_bytes, xq, xg, nullptr, nullptr, 0u, a.err,
+                              lane, nullptr, racc);
         }
         __syncwarp();
         r.consumed++;
@@ -669,7 +727,7 @@ extern "C" int gguf_cuda_matvec_noalloc(const GGUFWeight *weight, const float *x
     p.cols = (int)weight->cols;
     p.xin = x;
     p.y = out;
-    tile_phase(p, sm_count() * DK_WARPS, 8192, false);  // the tiles of gguf_cuda_matvec
+    tile_phase(p, sm_count() * DK_WARPS, stage_cap((p.cols + 63) / 64, 0), false);  // gguf_cuda_matvec's tiles
     Layout L;
     if (!make_layout(L, p.nunits, stage_need(p), 0, 3)) {
         if (weight->type != T_F32 && weight->type != T_F16) {
@@ -687,6 +745,7 @@ extern "C" int gguf_cuda_matvec_noalloc(const GGUFWeight *weight, const float *x
         fill_args(a, L);
         if (cudaFuncSetAttribute(na_matvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem) !=
             cudaSuccess) {
+            cudaGetLastError();
             return na_fail(error, error_capacity, "gguf_cuda_matvec_noalloc: shared-memory plan rejected.");
         }
         int grid = (p.ntiles + L.warps - 1) / L.warps;
@@ -854,7 +913,7 @@ static LLPlan ll_plan(const PkdModel *m)
 // on the first CTAs. A tensor-parallel rank computes its heads, hidden
 // slice and vocabulary rows; Wo and down end in partial sums that an
 // all-reduce phase combines (two per layer).
-static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
+static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total, int cap)
 {
     const PkdTp &tp = m->tp;
     const int L = m->n_layers, dim = m->dim, hs = m->head_size, W = tp.world;
@@ -865,7 +924,6 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total)
     c->nphases = per * L + 1;
     c->phases = (Phase *)calloc((size_t)c->nphases, sizeof(Phase));
     if (c->phases == NULL) return 0;
-    const int cap = 8192;
     int acc = 0;  // the warp after the last tile of the previous phase
     auto rotate = [&](Phase &p) {
         p.off = acc;
@@ -1210,7 +1268,11 @@ static int finalize(PkdCtx *c, char *err, size_t cap)
     c->persistent = env_flag("POCKET_CUDA_PERSISTENT", 1);
     c->use_graph = !env_flag("POCKET_CUDA_EAGER", 0);
     c->grid = sm_count();
-    if (!build_phases(c, m, c->grid * DK_WARPS)) {
+    // stages as large as the shared memory left after x and the attention
+    // scratch allows (rows longer than a stage go in column chunks)
+    const int widest = m->dim > m->hidden_dim ? m->dim : m->hidden_dim;
+    const int scap = stage_cap((widest + 63) / 64, attn_scratch_floats(m->head_size, DK_WARPS));
+    if (!build_phases(c, m, c->grid * DK_WARPS, scap)) {
         if (err && cap) snprintf(err, cap, "Out of memory.");
         return 0;
     }
@@ -1241,6 +1303,7 @@ static int finalize(PkdCtx *c, char *err, size_t cap)
             cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, c->fn, c->layout.warps * 32,
                                                           c->layout.smem) != cudaSuccess ||
             per_sm < 1) {
+            cudaGetLastError();
             c->persistent = 0;  // no co-residency guarantee: one launch per phase instead
         }
     }

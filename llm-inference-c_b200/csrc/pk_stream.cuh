@@ -245,6 +245,8 @@ struct Phase {
     // fused matvec
     MvSeg seg[3];
     int nseg, ntiles, cols, nunits;
+    int nchunk, cunits, cbytes;  // rows longer than a stage: nchunk column chunks of cunits
+                                 // 64-column units (cbytes bytes), one row per tile
     const float *xin;         // input vector as floats (device seam), or
     const uint64_t *xin_ll;   // as tagged words (decode step)
     const float *norm;        // RMSNorm weights (PRO_NORM / PRO_EMBED_NORM); PRO_SWIGLU
@@ -328,13 +330,21 @@ __device__ __forceinline__ const MvSeg &find_seg(const Phase &p, int t)
     return p.seg[0];
 }
 
-// Lane 0: issue the copies of tile t of phase p into buf; completes on bar.
-__device__ __forceinline__ void issue_tile(const Phase &p, int t, uint8_t *buf, uint64_t *bar)
+// Lane 0: issue the copies of chunk `chunk` of tile t of phase p into buf;
+// completes on bar.
+__device__ __forceinline__ void issue_tile(const Phase &p, int t, int chunk, uint8_t *buf, uint64_t *bar)
 {
     const MvSeg &s = find_seg(p, t);
     const int r0 = (t - s.tile0) * s.R;
     const int nr = min(s.R, s.rows - r0);
-    const Span sa = make_span(reinterpret_cast<uintptr_t>(s.w) + (uintptr_t)r0 * s.rb, (uint64_t)nr * s.rb);
+    uintptr_t st = reinterpret_cast<uintptr_t>(s.w) + (uintptr_t)r0 * s.rb;
+    uint64_t n = (uint64_t)nr * s.rb;
+    if (p.nchunk > 1) {  // one row, one chunk of it
+        const uint64_t off = (uint64_t)chunk * (uint64_t)p.cbytes;
+        st += off;
+        n = s.rb - off < (uint64_t)p.cbytes ? s.rb - off : (uint64_t)p.cbytes;
+    }
+    const Span sa = make_span(st, n);
     mbar_expect_tx(bar, sa.bulk);
     fill_span(sa, buf, bar);
 }
@@ -354,14 +364,14 @@ __device__ __forceinline__ void ring_fill(Ring &r, const Phase *ph, int nph, int
 {
     while (r.issued - r.consumed < (uint32_t)r.stages && r.cp < nph) {
         const Phase &p = ph[r.cp];
-        const int t = p.kind == PH_MV ? tile_at(p, gw, nw_total, r.ck) : 0;
+        const int t = p.kind == PH_MV ? tile_at(p, gw, nw_total, r.ck / p.nchunk) : 0;
         if (p.kind != PH_MV || t >= p.ntiles) {
             r.cp++;
             r.ck = 0;
             continue;
         }
         const uint32_t slot = r.issued % (uint32_t)r.stages;
-        issue_tile(p, t, r.buf + slot * r.stage_bytes, r.bars + slot);
+        issue_tile(p, t, r.ck % p.nchunk, r.buf + slot * r.stage_bytes, r.bars + slot);
         r.issued++;
         r.ck++;
     }
@@ -639,16 +649,32 @@ __device__ __forceinline__ float tile_dispatch(int type, const uint8_t *ra, uint
 // Compute tile t of phase p from its ring slot and apply the epilogue.
 // rope: this position's cos/sin pairs (EPI_QKV); tag: the step's tag for
 // tagged outputs and the residual. MASK: the formats compiled in.
+// Rows in column chunks (p.nchunk > 1): each chunk's sum adds to racc and
+// the epilogue runs after the last chunk.
 template <unsigned MASK>
-__device__ __forceinline__ void run_tile(const Phase &p, int t, const uint8_t *buf, const uint8_t *xq,
+__device__ __forceinline__ void run_tile(const Phase &p, int t, int chunk, const uint8_t *buf, const uint8_t *xq,
                                          const float *xg, const int *step, const float *rope, uint32_t tag, int *err,
-                                         int lane, unsigned long long *cta_amax)
+                                         int lane, unsigned long long *cta_amax, float &racc)
 {
     const MvSeg &s = find_seg(p, t);
     const int r0 = (t - s.tile0) * s.R;
     const int nr = min(s.R, s.rows - r0);
-    const uint8_t *ra = buf + ((reinterpret_cast<uintptr_t>(s.w) + (uintptr_t)r0 * s.rb) & 15);
-    const float va = tile_dispatch<MASK>(s.type, ra, s.rb, nr, p.nunits, p.cols, xq, xg, lane);
+    uintptr_t st = reinterpret_cast<uintptr_t>(s.w) + (uintptr_t)r0 * s.rb;
+    float va;
+    if (p.nchunk > 1) {
+        // the chunk's units (weights relative to the chunk start; x at the same units)
+        const int u0 = chunk * p.cunits, nu = min(p.cunits, p.nunits - u0);
+        const int ccols = min(64 * nu, p.cols - 64 * u0);
+        st += (uintptr_t)chunk * (uintptr_t)p.cbytes;
+        va = tile_dispatch<MASK>(s.type, buf + (st & 15), s.rb, 1, nu, ccols, xq + (size_t)u0 * XQ_UNIT_BYTES,
+                                 xg + (size_t)u0 * XG_UNIT_WORDS, lane);
+        racc += va;
+        if (chunk < p.nchunk - 1) return;
+        va = racc;
+        racc = 0.0f;
+    } else {
+        va = tile_dispatch<MASK>(s.type, buf + (st & 15), s.rb, nr, p.nunits, p.cols, xq, xg, lane);
+    }
     // Epilogue: lane i owns row r0 + i.
     const int r = r0 + lane;
     if (p.epi == EPI_QKV) {

@@ -164,3 +164,30 @@ def test_tinyllama_shape_greedy_128_steps(orc, synth_model):
     assert worst < LOGIT_TOL, worst
     e.close()
     o.close()
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("preset", ["llama2-7b-q4km", "llama3-8b-q5k"])
+def test_7b_8b_shapes_match_oracle(orc, synth_model, preset):
+    """Llama-2-7B and Llama-3-8B shapes (ffn_down rows longer than a ring
+    stage, streamed in column chunks): 4 prompt ids and 4 greedy steps against
+    the oracle, logits within 1e-3."""
+    path = synth_model(preset, seed=1234)
+    e, o = pk_b200.Engine(path, 64), orc.open(path, 64)
+    assert e.launches_per_step() == 2  # the single cooperative step kernel
+    prompt = pk_synth.uniform_ints(43, 4, 3, o.vocab_size)
+    worst = 0.0
+    for pos, t in enumerate(prompt):
+        a = e.forward(int(t), pos)
+        b = o.forward(int(t), pos)
+        worst = max(worst, float(np.abs(a - b).max()))
+    tok = o.greedy(b)
+    dev_tokens, _ = e.generate_greedy(tok, 4, 4)
+    ref_tokens = []
+    for step in range(4):
+        tok = o.greedy(o.forward(tok, 4 + step))
+        ref_tokens.append(tok)
+    assert [int(t) for t in dev_tokens] == ref_tokens
+    assert worst < LOGIT_TOL, worst
+    e.close()
+    o.close()

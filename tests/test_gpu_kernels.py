@@ -151,6 +151,21 @@ def test_matvec_odd_block_count(torch, orc):
         assert rel_l2(gpu_matvec(torch, qtype, wb, rows, cols, x), orc.matvec(qtype, wb, rows, cols, x)) < REL_L2
 
 
+# Rows longer than a ring stage stream in column chunks of whole blocks.
+LONG_ROWS = [(pk_b200.Q6_K, 48, 16384), (pk_b200.Q4_K, 33, 40960), (pk_b200.Q8_0, 40, 8192),
+             (pk_b200.Q4_0, 17, 16384 + 32), (pk_b200.F32, 9, 4096 + 64), (pk_b200.F16, 9, 8192 + 128)]
+
+
+@pytest.mark.parametrize("qtype,rows,cols", LONG_ROWS)
+def test_matvec_long_rows_in_column_chunks(torch, orc, qtype, rows, cols):
+    wb = pk_synth.random_matrix(qtype, rows, cols, seed=rows * 3 + qtype)
+    x = pk_synth.gaussian(cols + 5, cols)
+    y = gpu_matvec(torch, qtype, wb, rows, cols, x)
+    want = orc.matvec(qtype, wb, rows, cols, x)
+    assert rel_l2(y, want) < REL_L2
+    assert normalised_error(orc, qtype, wb, rows, cols, x, y) < NORM_ERR
+
+
 # The isolated sweep shapes (out x in) of the benchmark configuration.
 SWEEP = [(2048, 2048), (256, 2048), (5632, 2048), (2048, 5632), (32000, 2048), (4096, 4096),
          (14336, 4096), (128256, 4096)]
