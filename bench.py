@@ -51,7 +51,7 @@ PUBLISHED_TOKS = 8.03  # reference, TinyLlama-1.1B-Chat Q4_K_M, 8 threads (docum
 # the ncu capture summarised in profiles/phase_kernel_tinyllama_decode.md
 # (dram__bytes_read.sum + dram__bytes_write.sum); None for workloads without
 # a capture.
-NCU_TRAFFIC = {"tinyllama-1.1b-q4km": 635241216 + 3894016}
+NCU_TRAFFIC = {"tinyllama-1.1b-q4km": 637432576 + 10022400}
 FALLBACK_HBM_GBS = 6650.0
 MODEL_SEED = 1234
 

@@ -71,6 +71,7 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
     const int W = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gw = blockIdx.x * W + warp, NW = gridDim.x * W;
     const uint32_t tag = a.step != nullptr ? (uint32_t)a.step[4] : 0u;
+    const int token = a.step != nullptr ? a.step[0] : 0, pos = a.step != nullptr ? a.step[1] : 0;
     const bool tracing = a.trace != nullptr && blockIdx.x == 0;
 
     Ring r;
@@ -96,12 +97,17 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
     if (lane == 0) ring_fill(r, ph, nph, gw, NW);
     if (tracing && threadIdx.x == 0) a.trace[0] = global_ns();
     if (a.rope_cs != nullptr) {
-        const float *row = a.rope_cs + (size_t)a.step[1] * a.rope_dim;
+        const float *row = a.rope_cs + (size_t)pos * a.rope_dim;
         for (int i = threadIdx.x; i < a.rope_dim; i += blockDim.x) rope[i] = row[i];
     }
 
     for (int pi = 0; pi < nph; pi++) {
         const Phase &p = ph[pi];
+        // the next phase's descriptor (global memory) into L1 while this one runs
+        if (a.phases != nullptr && pi + 1 < nph && threadIdx.x < (unsigned)((sizeof(Phase) + 127) / 128)) {
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const char *>(ph + pi + 1) +
+                                                           128 * threadIdx.x));
+        }
         if (p.kind == PH_MV) {
             if (cta_has_tiles(p, blockIdx.x, W, NW)) {
                 __syncthreads();  // every warp is done with the previous phase's x
@@ -116,12 +122,12 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
                     const uint32_t par = (r.consumed / (uint32_t)a.stages) & 1u;
                     // warp-uniform: run_tile's shuffles name every lane
                     const bool ok =
-                        __all_sync(0xFFFFFFFFu, !aborted(a.err) && mbar_wait_bounded(r.bars + slot, par));
+                        __all_sync(0xFFFFFFFFu, mbar_wait_or_abort(r.bars + slot, par, a.err));
                     if (!ok) {
                         if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_MV);
                     } else {
-                        run_tile<MASK>(p, t, k % p.nchunk, r.buf + slot * a.stage_bytes, xq, xg, a.step, rope, tag,
-                                       a.err, lane, cta_amax, racc);
+                        run_tile<MASK>(p, t, k % p.nchunk, r.buf + slot * a.stage_bytes, xq, xg, token, pos, rope,
+                                       tag, a.err, lane, cta_amax, racc);
                     }
                     __syncwarp();
                     r.consumed++;
@@ -162,7 +168,7 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
                 ar_item(p, it, a.step, tag, a.err);
             }
         } else {
-            const int n = a.step[1] + 1, nh = p.n_kv * p.kv_mul;
+            const int n = pos + 1, nh = p.n_kv * p.kv_mul;
             const int span = attn_span(n, p.nsplit_max);
             const int nsplit = (n + span - 1) / span;
             if (tracing && threadIdx.x == 0) a.trace[3 * pi + 1] = global_ns();
@@ -649,11 +655,11 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) na_matvec_kernel(const __gri
         if (t >= p.ntiles) break;
         const uint32_t slot = r.consumed % (uint32_t)a.stages;
         const uint32_t par = (r.consumed / (uint32_t)a.stages) & 1u;
-        const bool ok = __all_sync(0xFFFFFFFFu, !aborted(a.err) && mbar_wait_bounded(r.bars + slot, par));
+        const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait_or_abort(r.bars + slot, par, a.err));
         if (!ok) {
             if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_MV);
         } else {
-            run_tile<FMT_ALL>(p, t, k % p.nchunk, r.buf + slot * a.stage_bytes, xq, xg, nullptr, nullptr, 0u, a.err,
+            run_tile<FMT_ALL>(p, t, k % p.nchunk, r.buf + slot * a.stage_bytes, xq, xg, 0, 0, nullptr, 0u, a.err,
                               lane, nullptr, racc);
         }
         __syncwarp();

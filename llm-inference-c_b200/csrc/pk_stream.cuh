@@ -99,6 +99,17 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     return true;
 }
 
+__device__ __forceinline__ bool aborted(const int *err);
+
+// mbar_wait_bounded that also gives up when another thread has recorded a
+// timeout (checked only while waiting, so a ready stage costs no global load).
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t *bar, uint32_t parity, const int *err)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    if (aborted(err)) return false;
+    return mbar_wait_bounded(bar, parity);
+}
+
 __device__ __forceinline__ unsigned ld_acquire(const unsigned *p)
 {
     unsigned v;
@@ -653,13 +664,19 @@ __device__ __forceinline__ float tile_dispatch(int type, const uint8_t *ra, uint
 // the epilogue runs after the last chunk.
 template <unsigned MASK>
 __device__ __forceinline__ void run_tile(const Phase &p, int t, int chunk, const uint8_t *buf, const uint8_t *xq,
-                                         const float *xg, const int *step, const float *rope, uint32_t tag, int *err,
-                                         int lane, unsigned long long *cta_amax, float &racc)
+                                         const float *xg, int token, int pos, const float *rope, uint32_t tag,
+                                         int *err, int lane, unsigned long long *cta_amax, float &racc)
 {
     const MvSeg &s = find_seg(p, t);
     const int r0 = (t - s.tile0) * s.R;
     const int nr = min(s.R, s.rows - r0);
     uintptr_t st = reinterpret_cast<uintptr_t>(s.w) + (uintptr_t)r0 * s.rb;
+    // the residual word is issued before the dot products so its L2 latency
+    // overlaps them (it was written phases ago; checked after)
+    uint64_t resw = 0;
+    if (p.epi == EPI_ADD && p.res_ll != nullptr && lane < nr && (p.nchunk == 1 || chunk == p.nchunk - 1)) {
+        resw = ld_ll(p.res_ll + r0 + lane);
+    }
     float va;
     if (p.nchunk > 1) {
         // the chunk's units (weights relative to the chunk start; x at the same units)
@@ -681,7 +698,6 @@ __device__ __forceinline__ void run_tile(const Phase &p, int t, int chunk, const
         // RoPE pairs (2i, 2i+1) sit in neighbouring lanes (R and r0 are even).
         const float other = __shfl_xor_sync(0xFFFFFFFFu, va, 1);
         if (lane < nr) {
-            const int pos = step[1];
             float v = va;
             const int d = r % p.hs;
             if (s.kind != KIND_V && (d & ~1) < p.rope_dim) {
@@ -737,8 +753,9 @@ __device__ __forceinline__ void run_tile(const Phase &p, int t, int chunk, const
         if (p.epi == EPI_ADD) {
             // residual stream, src/gguf_forward.c:274-276,297-299 (layer 0's input
             // is the embedding row, decoded again here)
-            const float res = p.res_ll != nullptr ? ll_read(p.res_ll + r, tag, err)
-                                                  : decode_col_call(p.embd_type, p.embd + (size_t)step[0] * p.embd_rb, r);
+            const float res = p.res_ll == nullptr ? decode_col_call(p.embd_type, p.embd + (size_t)token * p.embd_rb, r)
+                              : ll_is(resw, tag)    ? ll_val(resw)
+                                                    : ll_read(p.res_ll + r, tag, err);
             out = __fadd_rn(res, va);
         }
         if (p.y_ll != nullptr) {
