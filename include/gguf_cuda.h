@@ -92,6 +92,42 @@ int gguf_cuda_fp16_table(float *out65536, void *stream);
 int gguf_cuda_matvec_noalloc(const GGUFWeight *weight, const float *x, float *out, void *stream,
                              char *error, size_t error_capacity);
 
+/*
+ * Batched counterpart of gguf_cuda_matvec on the tensor cores: for n
+ * activation vectors (1 <= n <= 64) that share one pass over the packed
+ * weights,
+ *     out[b * rows + r] = sum_c W[r][c] * x[b * cols + c],  b < n, r < rows,
+ * i.e. gguf_matvec (reference include/gguf_model.h:141-145) applied to each
+ * of n vectors. x is n x cols and out is n x rows, row-major, device
+ * pointers; out must not overlap x. Q4_K weights (type 12) only; other
+ * types return 0. Every column agrees with gguf_cuda_matvec / the
+ * reference's kernel to float32 rounding (the products run on fp16
+ * operands that carry x to 22 significant bits, exact products, fp32
+ * accumulation). No counterpart in the reference, whose decode runs one
+ * sequence at a time.
+ *
+ * Scratch (staged x, partial sums) is allocated per device on first use
+ * and grown on demand; make the first call with the largest n and shape
+ * before any stream capture. Calls on one device share the scratch:
+ * serialise calls that may overlap in time (e.g. one stream).
+ */
+int gguf_cuda_matmul(const GGUFWeight *weight, const float *x, int n, float *out, void *stream);
+
+/*
+ * The work split gguf_cuda_matmul uses for `rows` rows of `nsb` 256-column
+ * super-blocks on `sms` SMs: *ctas CTAs (one per SM at most) and *maxp,
+ * the most CTAs that share one 128-row tile. Host-only.
+ */
+void gguf_cuda_matmul_plan(int rows, int nsb, int sms, int *ctas, int *maxp);
+
+/*
+ * The error word of gguf_cuda_matmul on the current device, read and
+ * cleared (synchronises the device): 0 when no wait inside the kernel has
+ * run out of time since the last read, 1 when one has (that call's output
+ * is invalid), -1 when it cannot be read.
+ */
+int gguf_cuda_matmul_error(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -412,7 +412,7 @@ static int stage_need(const Phase &p)
     for (int i = 0; i < p.nseg; i++) {
         const MvSeg &s = p.seg[i];
         const uint64_t bytes = p.nchunk > 1 ? (uint64_t)p.cbytes + 16 : (uint64_t)s.R * s.rb;
-        const int b = (int)((bytes + 32 + 127) / 128 * 128);
+        const int b = (int)((bytes + 32 + 15) / 16 * 16);  // bulk copies need 16-byte granularity
         if (b > need) need = b;
     }
     return need;
@@ -427,7 +427,7 @@ static int stage_cap(int max_units, int attn_floats)
     const int at = (attn_floats * 4 + 127) / 128 * 128;
     if (at > xs) xs = at;
     const int bars = (DK_WARPS * 2 * 8 + 127) / 128 * 128;
-    int cap = (smem_dynamic_max() - bars - xs) / (2 * DK_WARPS) / 128 * 128;
+    int cap = (smem_dynamic_max() - bars - xs) / (2 * DK_WARPS) / 16 * 16;
     if (cap > 8192) cap = 8192;
     return cap;
 }

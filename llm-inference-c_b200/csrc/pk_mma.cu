@@ -1,0 +1,756 @@
+// pk_mma.cu - the batched fused dequant-matmul on the sm_100a tensor cores:
+// Y[b][r] = sum_k W[r][k] * x_b[k] for up to 64 activation vectors x_b that
+// share one pass over the packed Q4_K weights (the matmul form of the
+// matvec, src/gguf_model.c:693-771, for several sequences at once).
+//
+// Operands (fp16 products are exact in the fp32 accumulator):
+//   A (weights): per super-block of 256 columns, the integers sc_j * q
+//       (at most 63 * 15, exact in fp16), one LOP3 and one HFMA2 per two
+//       weights; the super-block scales d and dmin stay out of the product
+//       and are applied in fp32 when the accumulator is read out. A second
+//       operand A2 holds the 6-bit mins m_j.
+//   B (activations): each 256-column piece of every x_b, scaled by a power
+//       of two so that its largest magnitude is below 2^10, split into two
+//       fp16 parts hi = fp16(x) and lo = fp16(x - hi) (22 significant bits
+//       together), at MMA columns 2b and 2b + 1. B2 holds the 32-column
+//       sums of the scaled piece (the Q4_K min term sum_j m_j * xsum_j) the
+//       same way.
+//   D = A x B and D2 = A2 x B2 in TMEM (fp32, M = 128 rows, N = 2n rounded
+//       up to 16), read out once per super-block:
+//       y[b] += (d * (D[2b] + D[2b+1]) - dmin * (D2[2b] + D2[2b+1])) / scale.
+//
+// One CTA per SM, warp-specialised, every hand-off an mbarrier:
+//   warps 0-3  dequantise (thread i = weight row i of the tile = TMEM lane
+//              i) into A, and read the accumulators out;
+//   warp 4     loads the weight super-blocks of the tile (128 rows x 144
+//              bytes, one 2D TMA tensor copy each, plus the 64 scales of
+//              that x piece) into a 4-deep ring;
+//   warp 5     bulk-copies the staged x of each 64-column step into a ring
+//              as deep as shared memory allows (4 steps at n = 64, 32 at
+//              n <= 8);
+//   warp 6     allocates TMEM and issues the MMAs (one thread), committing
+//              to the barriers that free the A and B slots and publish the
+//              accumulators; two accumulator sets let the readout of one
+//              super-block overlap the MMAs of the next.
+// Work units are (row tile, super-block) pairs, split evenly over the CTAs
+// in row-tile-major order. A tile split over several CTAs leaves one partial
+// sum per CTA; for each 32-row group the last CTA to finish it adds the
+// partials up in CTA order (a fixed order: the result does not depend on
+// timing). Two launches per call: the x staging kernel, then this one.
+//
+// Shared-memory operands are fp16, K-major, without swizzle: core matrices
+// of 8 rows x 16 bytes, rows 16 bytes apart. A step tile of 64 columns is
+// [8 column chunks][rows][16 bytes]; element (row, k) sits at
+//     (k / 8) * chunk_bytes + row * 16 + pos(k % 8) * 2,
+// chunk_bytes = 128 * 16 for A, N * 16 for B (the descriptors' leading
+// offset; their stride offset is 128 bytes, the next 8 rows). pos()
+// permutes each run of 8 columns as {0, 2, 1, 3, 4, 6, 5, 7}: the order in
+// which one LOP3 takes the nibbles out of a 32-bit word of packed weights
+// (the sum over k does not depend on the order).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "../../include/gguf_cuda.h"
+#include "pk_quant.cuh"
+#include "pk_stream.cuh"
+
+namespace pk {
+namespace mm {
+
+constexpr int TM = 128;    // weight rows per tile (MMA M)
+constexpr int NMAX = 128;  // MMA N at most: 2 parts x 64 vectors
+constexpr int VMAX = 64;   // activation vectors per call
+constexpr int QK = 256;    // columns per Q4_K super-block
+constexpr int SBB = 144;   // bytes per Q4_K super-block
+constexpr int W_PRODUCER = 4, B_PRODUCER = 5, ISSUER = 6;
+constexpr int DQ_THREADS = 128;  // warps 0-3
+constexpr int THREADS = 224;
+constexpr int SA = 3, SW = 4, SB_MAX = 32;  // ring depths: A steps, weight super-blocks, x steps (at most)
+constexpr int A_BYTES = TM * 128;           // [8 chunks][128 rows][16 B]
+constexpr int A2_BYTES = TM * 32;           // [2 chunks][128 rows][16 B]
+constexpr int W_TILE = TM * SBB;            // 128 rows x one super-block
+constexpr int W_BYTES = W_TILE + VMAX * 4;  // + the inverse scales of the x piece
+// Barriers
+enum {
+    FULL_A = 0,
+    EMPTY_A = FULL_A + SA,
+    FULL_W = EMPTY_A + SA,
+    EMPTY_W = FULL_W + SW,
+    ACC_FULL = EMPTY_W + SW,
+    ACC_EMPTY = ACC_FULL + 2,
+    DRAIN = ACC_EMPTY + 2,
+    FULL_B = DRAIN + 1,
+    EMPTY_B = FULL_B + SB_MAX,
+    NBARS = EMPTY_B + SB_MAX
+};
+// Shared-memory layout (offsets from a 128-byte aligned base)
+constexpr int OFF_BAR = 0;
+constexpr int OFF_INV = 1024;  // 3 x 64 inverse scales (readout)
+constexpr int OFF_A = 2048;
+constexpr int OFF_A2 = OFF_A + SA * A_BYTES;
+constexpr int OFF_W = OFF_A2 + 2 * A2_BYTES;  // 128-byte aligned (TMA tensor destination)
+constexpr int OFF_B = OFF_W + SW * W_BYTES;
+constexpr int B_SLOT_MAX = NMAX * 128 + NMAX * 32;
+static_assert(NBARS * 8 <= OFF_INV, "barriers");
+static_assert(OFF_W % 128 == 0 && W_BYTES % 128 == 0, "TMA destinations");
+static_assert(OFF_B + 4 * B_SLOT_MAX + 128 <= 227 * 1024 - 1024, "at least 4 x steps of N = 128");
+static_assert(OFF_B > 227 * 1024 / 2, "one CTA per SM (it allocates all of TMEM)");
+constexpr int TMEM_COLS = 512;  // 2 accumulator sets x (D: 128 columns, D2: 128 columns)
+
+// Position of column k (mod 8) inside its 16-byte run: 1 <-> 2, 5 <-> 6.
+__host__ __device__ constexpr int perm8(int i)
+{
+    return (i == 1 || i == 2 || i == 5 || i == 6) ? (i ^ 3) : i;
+}
+
+// CTA owning work unit u when U units are split over G CTAs as
+// [c * U / G, (c + 1) * U / G).
+__host__ __device__ inline int unit_owner(long long u, long long U, long long G)
+{
+    return (int)(((u + 1) * G - 1) / U);
+}
+
+// UMMA shared-memory descriptor: K-major, no swizzle, version 1 (sm_100).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo)
+{
+    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    return d;
+}
+
+// Instruction descriptor of kind::f16: fp16 A and B, both K-major, fp32 D.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n)
+{
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accum), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+
+// Arrive on bar once every tcgen05 operation issued so far by this thread
+// has completed.
+__device__ __forceinline__ void mma_commit(uint64_t *bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after()
+{
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before()
+{
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// 2D TMA tensor copy of the box at (x, y) (x in elements of the innermost
+// dimension) into shared memory, completing on bar.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane (warp w reads
+// lanes 32w .. 32w + 31; taddr carries the lane in bits 16-31).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v)
+{
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Two nibbles of w (bits 0-3 and 16-19) as the fp16 pair (sc * q0, sc * q1):
+// 1024 + q by the exponent trick, then (1024 + q) * sc - 1024 * sc in one
+// fma, exact because the result is an integer below 2048.
+__device__ __forceinline__ uint32_t nib2(uint32_t w, __half2 sc2, __half2 nsc2)
+{
+    const uint32_t h = (w & 0x000F000Fu) | 0x64006400u;
+    const __half2 r = __hfma2(*reinterpret_cast<const __half2 *>(&h), sc2, nsc2);
+    return *reinterpret_cast<const uint32_t *>(&r);
+}
+
+// Bounded wait that also gives up once another thread has aborted the CTA;
+// a thread that runs out of time records the timeout and aborts the CTA.
+__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort_flag) return false;
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+            *abort_flag = 1;
+            atomicOr(err, ERR_TIMEOUT_MV);
+            return false;
+        }
+    }
+    return true;
+}
+
+// wait_or_abort with one answer for the whole warp (every lane calls it), so
+// that the warp's later collective instructions stay converged.
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err)
+{
+    const bool got = wait_or_abort(bar, parity, abort_flag, err);
+    return __all_sync(0xFFFFFFFFu, got);
+}
+
+struct MmArgs {
+    int rows, nsb;          // rows, super-blocks per row
+    const uint8_t *xs;      // staged x: [nsb][4 steps][8 chunks][N rows][16 B]
+    const uint8_t *x2s;     // staged x sums: [nsb][2 chunks][N rows][16 B]
+    const float *xinv;      // [nsb][64] inverse scales of the staged pieces
+    int n, N;               // vectors, MMA N
+    int sb, b_slot;         // x ring depth and slot bytes
+    long long U;            // work units (row tiles x super-blocks)
+    int G;                  // CTAs
+    int maxp;               // partial slots per tile
+    float *y;               // [n][rows]
+    float *ypart;           // [tiles][maxp][n][128]
+    unsigned int *arrived;  // [tiles][4 warps] CTAs done with those rows (reset by the last)
+    int *err;
+};
+
+// wmap: the weights as a 2D tensor of bytes [rows][row bytes], box
+// [128 rows][144 bytes] (one super-block of one row tile).
+__global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constant__ CUtensorMap wmap, MmArgs a)
+{
+    extern __shared__ __align__(128) uint8_t sm_raw[];
+    uint8_t *sm = sm_raw + ((128u - (smem_u32(sm_raw) & 127u)) & 127u);
+    __shared__ uint32_t tmem_slot;
+    __shared__ int abort_flag;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + OFF_BAR);
+    float *inv_s = reinterpret_cast<float *>(sm + OFF_INV);
+    const int c = blockIdx.x;
+    const long long u0 = (long long)c * a.U / a.G, u1 = (long long)(c + 1) * a.U / a.G;
+    const int nu = (int)(u1 - u0);
+    const int N = a.N, SB = a.sb;
+
+    if (warp == ISSUER) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                     "r"((uint32_t)TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        for (int i = 0; i < SA; i++) {
+            mbar_init(bars + FULL_A + i, DQ_THREADS);
+            mbar_init(bars + EMPTY_A + i, 1);
+        }
+        for (int i = 0; i < SW; i++) {
+            mbar_init(bars + FULL_W + i, 1);
+            mbar_init(bars + EMPTY_W + i, DQ_THREADS);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(bars + ACC_FULL + i, 1);
+            mbar_init(bars + ACC_EMPTY + i, DQ_THREADS);
+        }
+        mbar_init(bars + DRAIN, 1);
+        for (int i = 0; i < SB; i++) {
+            mbar_init(bars + FULL_B + i, 1);
+            mbar_init(bars + EMPTY_B + i, 1);
+        }
+        fence_mbar_init();
+        abort_flag = 0;
+    }
+    // A2 column chunk 1 (k 8..15) stays zero in both slots
+    for (int i = tid; i < 2 * TM; i += THREADS) {
+        const int slot = i / TM, row = i % TM;
+        *reinterpret_cast<uint4 *>(sm + OFF_A2 + slot * A2_BYTES + TM * 16 + row * 16) = make_uint4(0, 0, 0, 0);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    const uint32_t sbase = smem_u32(sm);
+    volatile int *abrt = &abort_flag;
+
+    if (warp == W_PRODUCER) {
+        if (lane == 0) {
+            // weight super-blocks: one tensor copy of 128 rows x 144 bytes each
+            // (rows past the end of the matrix arrive as zeros), then the 64
+            // inverse scales of the matching x piece
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+            int issued = 0;
+            for (int j = 0; j < nu; j++) {
+                const int slot = j % SW;
+                if (j >= SW && !wait_or_abort(bars + EMPTY_W + slot, ((j / SW) - 1) & 1, abrt, a.err)) break;
+                const long long u = u0 + j;
+                const int T = (int)(u / a.nsb), s = (int)(u % a.nsb);
+                uint8_t *dst = sm + OFF_W + slot * W_BYTES;
+                mbar_expect_tx(bars + FULL_W + slot, (uint32_t)W_BYTES);
+                tma_load_2d(dst, &wmap, s * SBB, T * TM, bars + FULL_W + slot);
+                bulk_g2s(dst + W_TILE, a.xinv + (size_t)s * VMAX, VMAX * 4, bars + FULL_W + slot);
+                issued = j + 1;
+            }
+            // no copy may still be in flight when the CTA exits
+            for (int j = max(0, issued - SW); j < issued; j++)
+                mbar_wait_bounded(bars + FULL_W + j % SW, (j / SW) & 1);
+        }
+    } else if (warp == B_PRODUCER) {
+        if (lane == 0) {
+            int issued = 0;
+            const uint32_t step_bytes = (uint32_t)N * 128, sum_bytes = (uint32_t)N * 32;
+            for (int i = 0; i < 4 * nu; i++) {
+                const int slot = i % SB;
+                if (i >= SB && !wait_or_abort(bars + EMPTY_B + slot, ((i / SB) - 1) & 1, abrt, a.err)) break;
+                const int t = i & 3;
+                const int s = (int)((u0 + i / 4) % a.nsb);
+                uint8_t *dst = sm + OFF_B + slot * a.b_slot;
+                mbar_expect_tx(bars + FULL_B + slot, step_bytes + (t == 3 ? sum_bytes : 0u));
+                bulk_g2s(dst, a.xs + ((size_t)s * 4 + t) * step_bytes, step_bytes, bars + FULL_B + slot);
+                if (t == 3) bulk_g2s(dst + step_bytes, a.x2s + (size_t)s * sum_bytes, sum_bytes, bars + FULL_B + slot);
+                issued = i + 1;
+            }
+            for (int i = max(0, issued - SB); i < issued; i++) mbar_wait_bounded(bars + FULL_B + i % SB, (i / SB) & 1);
+        }
+    } else if (warp == ISSUER) {
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16(TM, N);
+            bool ok = true;
+            int issued = 0;
+            for (int j = 0; j < nu && ok; j++) {
+                const int acc = j & 1;
+                const uint32_t d_col = tmem + (uint32_t)(acc * 256);
+                if (j >= 2 && !wait_or_abort(bars + ACC_EMPTY + acc, ((j / 2) - 1) & 1, abrt, a.err)) break;
+                tc_fence_after();
+                for (int t = 0; t < 4; t++) {
+                    const int i = 4 * j + t, as = i % SA, bs = i % SB;
+                    if (!wait_or_abort(bars + FULL_A + as, (i / SA) & 1, abrt, a.err) ||
+                        !wait_or_abort(bars + FULL_B + bs, (i / SB) & 1, abrt, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = sbase + OFF_A + as * A_BYTES, b0 = sbase + OFF_B + bs * a.b_slot;
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++) {
+                        mma_f16(d_col, sdesc(a0 + kk * 2 * (TM * 16), TM * 16, 128),
+                                sdesc(b0 + kk * 2 * (N * 16), N * 16, 128), idesc, (t | kk) ? 1u : 0u);
+                    }
+                    if (t == 3) {
+                        mma_f16(d_col + 128, sdesc(sbase + OFF_A2 + (j & 1) * A2_BYTES, TM * 16, 128),
+                                sdesc(b0 + N * 128, N * 16, 128), idesc, 0u);
+                    }
+                    issued++;
+                    mma_commit(bars + EMPTY_A + as);
+                    mma_commit(bars + EMPTY_B + bs);
+                }
+                if (!ok) break;
+                mma_commit(bars + ACC_FULL + acc);
+            }
+            // MMAs still running after an abort finish before TMEM is freed
+            if (issued > 0) {
+                mma_commit(bars + DRAIN);
+                mbar_wait_bounded(bars + DRAIN, 0);
+            }
+        }
+    } else {
+        // warps 0-3: dequantise and read out; thread tid owns tile row tid
+        float acc[VMAX];
+#pragma unroll
+        for (int b = 0; b < VMAX; b++) acc[b] = 0.0f;
+        float d_prev = 0.0f, dmin_prev = 0.0f;
+        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        bool ok = true;
+        // Read out super-block jp and, at the end of a tile's piece, store it.
+        // inv_s slot jp % 3 holds its inverse scales: written at the start of
+        // jp, rewritten at the start of jp + 3, which no thread reaches before
+        // every thread has passed this readout (the A ring of depth 3 keeps
+        // the dequantisers within one super-block of each other).
+        auto readout = [&](int jp, float d, float dmin) -> bool {
+            const int accs = jp & 1;
+            if (!warp_wait(bars + ACC_FULL + accs, (jp / 2) & 1, abrt, a.err)) return false;
+            tc_fence_after();
+            __syncwarp();
+            const uint32_t col = lane_base + (uint32_t)(accs * 256);
+            const float *iv = inv_s + (jp % 3) * VMAX;
+#pragma unroll
+            for (int q = 0; q < NMAX / 32; q++) {
+                if (32 * q < N) {
+                    float v[32], v2[32];
+                    tmem_ld32(col + 32 * q, v);
+                    tmem_ld32(col + 128 + 32 * q, v2);
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        const int b = 16 * q + i;
+                        const float t1 = d * (v[2 * i] + v[2 * i + 1]);
+                        acc[b] = fmaf(iv[b], fmaf(-dmin, v2[2 * i] + v2[2 * i + 1], t1), acc[b]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(bars + ACC_EMPTY + accs);
+            const long long u = u0 + jp;
+            const int T = (int)(u / a.nsb);
+            if (jp == nu - 1 || (u + 1) % a.nsb == 0) {
+                const long long t0u = (long long)T * a.nsb;
+                const int r = T * TM + tid;
+                const int c0 = unit_owner(t0u, a.U, a.G), c1 = unit_owner(t0u + a.nsb - 1, a.U, a.G);
+                if (c0 == c1) {
+                    if (r < a.rows) {
+#pragma unroll
+                        for (int b = 0; b < VMAX; b++)
+                            if (b < a.n) a.y[(size_t)b * a.rows + r] = acc[b];
+                    }
+                } else {
+                    // this CTA's piece of the tile. Per warp (32 rows) a
+                    // counter of the CTAs done with those rows: the warp that
+                    // completes it adds the pieces in CTA order (no barrier
+                    // between the warps, so an aborted warp blocks no other)
+                    float *yp = a.ypart + (size_t)T * a.maxp * a.n * TM;
+#pragma unroll
+                    for (int b = 0; b < VMAX; b++)
+                        if (b < a.n) yp[((size_t)(c - c0) * a.n + b) * TM + tid] = acc[b];
+                    __threadfence();
+                    __syncwarp();
+                    unsigned int last = 0;
+                    if (lane == 0) {
+                        const unsigned int seen = atomicAdd(a.arrived + (size_t)T * 4 + warp, 1u);
+                        last = seen == (unsigned int)(c1 - c0);
+                        if (last) a.arrived[(size_t)T * 4 + warp] = 0u;  // ready for the next call
+                    }
+                    last = __shfl_sync(0xFFFFFFFFu, last, 0);
+                    if (last) {
+                        __threadfence();
+                        if (r < a.rows) {
+                            for (int b = 0; b < a.n; b++) {
+                                float sum = 0.0f;
+                                for (int k = 0; k <= c1 - c0; k++) sum += __ldcg(yp + ((size_t)k * a.n + b) * TM + tid);
+                                a.y[(size_t)b * a.rows + r] = sum;
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int b = 0; b < VMAX; b++) acc[b] = 0.0f;
+            }
+            return true;
+        };
+        for (int j = 0; j < nu && ok; j++) {
+            const int ws = j % SW;
+            if (!warp_wait(bars + FULL_W + ws, (j / SW) & 1, abrt, a.err)) {
+                ok = false;
+                break;
+            }
+            const uint8_t *wslot = sm + OFF_W + ws * W_BYTES;
+            const uint8_t *wrow = wslot + tid * SBB;
+            const uint4 hdr = *reinterpret_cast<const uint4 *>(wrow);
+            if (tid < VMAX) inv_s[(j % 3) * VMAX + tid] = reinterpret_cast<const float *>(wslot + W_TILE)[tid];
+            uint32_t scp[4], mnp[4];  // (scale, min) of sub-blocks 2t (low byte) and 2t + 1
+#pragma unroll
+            for (int t = 0; t < 4; t++) scale_min_pair(hdr.y, hdr.z, hdr.w, t, scp[t], mnp[t]);
+            for (int t = 0; t < 4; t++) {
+                const int i = 4 * j + t, as = i % SA;
+                if (i >= SA && !warp_wait(bars + EMPTY_A + as, ((i / SA) - 1) & 1, abrt, a.err)) {
+                    ok = false;
+                    break;
+                }
+                const uint4 qa = *reinterpret_cast<const uint4 *>(wrow + 16 + 32 * t);
+                const uint4 qb = *reinterpret_cast<const uint4 *>(wrow + 32 + 32 * t);
+                if (t == 3) mbar_arrive(bars + EMPTY_W + ws);
+                const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                const __half sl = __ushort2half_rn((unsigned short)(scp[t] & 255u));
+                const __half sh = __ushort2half_rn((unsigned short)(scp[t] >> 8));
+                const __half2 sc_lo = __halves2half2(sl, sl), sc_hi = __halves2half2(sh, sh);
+                const __half2 m1024 = __float2half2_rn(-1024.0f);
+                const __half2 nsc_lo = __hmul2(sc_lo, m1024), nsc_hi = __hmul2(sc_hi, m1024);
+                uint8_t *arow = sm + OFF_A + as * A_BYTES + tid * 16;
+#pragma unroll
+                for (int cc = 0; cc < 4; cc++) {
+                    // columns 8cc .. 8cc+7 of sub-block 2t (low nibbles of bytes 8cc ..) and of
+                    // sub-block 2t + 1 (their high nibbles), chunks cc and 4 + cc
+                    const uint32_t w0 = q[2 * cc], w1 = q[2 * cc + 1];
+                    *reinterpret_cast<uint4 *>(arow + cc * (TM * 16)) =
+                        make_uint4(nib2(w0, sc_lo, nsc_lo), nib2(w0 >> 8, sc_lo, nsc_lo), nib2(w1, sc_lo, nsc_lo),
+                                   nib2(w1 >> 8, sc_lo, nsc_lo));
+                    *reinterpret_cast<uint4 *>(arow + (4 + cc) * (TM * 16)) =
+                        make_uint4(nib2(w0 >> 4, sc_hi, nsc_hi), nib2(w0 >> 12, sc_hi, nsc_hi),
+                                   nib2(w1 >> 4, sc_hi, nsc_hi), nib2(w1 >> 12, sc_hi, nsc_hi));
+                }
+                if (t == 0) {
+                    // A2 row: the 8 mins of this super-block (chunk 0, natural order)
+                    uint32_t m2[4];
+#pragma unroll
+                    for (int p = 0; p < 4; p++) {
+                        const __half2 h = __halves2half2(__ushort2half_rn((unsigned short)(mnp[p] & 255u)),
+                                                         __ushort2half_rn((unsigned short)(mnp[p] >> 8)));
+                        m2[p] = *reinterpret_cast<const uint32_t *>(&h);
+                    }
+                    *reinterpret_cast<uint4 *>(sm + OFF_A2 + (j & 1) * A2_BYTES + tid * 16) =
+                        make_uint4(m2[0], m2[1], m2[2], m2[3]);
+                }
+                // the generic-proxy writes above, seen by the tensor core's async proxy
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive(bars + FULL_A + as);
+            }
+            if (!ok) break;
+            if (j > 0 && !readout(j - 1, d_prev, dmin_prev)) {
+                ok = false;
+                break;
+            }
+            d_prev = hf(hdr.x & 0xFFFFu);
+            dmin_prev = hf(hdr.x >> 16);
+        }
+        if (ok && nu > 0) readout(nu - 1, d_prev, dmin_prev);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == ISSUER) {
+        __syncwarp();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// x into the B operands. Block (s, b) stages super-block s of vector b:
+// scale = a power of two with max |x piece| * scale < 2^10 (1 for a zero or
+// non-finite piece), rows nn = 2b (hi) and 2b + 1 (lo) of the four step
+// tiles, the 32-column sums in B2, and 1 / scale in xinv. Blocks with
+// b >= n write the zero rows up to N. 256 threads, thread t = column
+// 256 s + t.
+__global__ void __launch_bounds__(256) mm_stage_kernel(const float *x, int n, int K, int N, uint8_t *xs, uint8_t *x2s,
+                                                       float *xinv)
+{
+    __shared__ float red[8];
+    const int s = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
+    const float xv = b < n ? x[(size_t)b * K + (size_t)s * QK + t] : 0.0f;
+    float m = fabsf(xv);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    if ((t & 31) == 0) red[t >> 5] = m;
+    __syncthreads();
+    m = red[0];
+#pragma unroll
+    for (int i = 1; i < 8; i++) m = fmaxf(m, red[i]);
+    float scale = 1.0f;
+    if (m > 0.0f && m <= 3.4e38f) {
+        int e = 0;
+        frexpf(m, &e);  // m < 2^e
+        scale = ldexpf(1.0f, max(-100, min(100, 10 - e)));
+    }
+    const float v = xv * scale;
+    const __half hi = __float2half_rn(v);
+    const __half lo = __float2half_rn(v - __half2float(hi));
+    const int step = t >> 6, chunk = (t >> 3) & 7, e = t & 7;
+    uint8_t *run = xs + ((size_t)s * 4 + step) * N * 128 + (size_t)chunk * N * 16 + (size_t)(2 * b) * 16 + perm8(e) * 2;
+    *reinterpret_cast<__half *>(run) = hi;
+    *reinterpret_cast<__half *>(run + 16) = lo;
+    // warp w holds sub-block w: its sum, then split
+    float sum = v;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+    if ((t & 31) == 0) {
+        const int j = t >> 5;
+        const __half shi = __float2half_rn(sum);
+        const __half slo = __float2half_rn(sum - __half2float(shi));
+        uint8_t *row = x2s + (size_t)s * N * 32 + (size_t)(2 * b) * 16 + j * 2;
+        *reinterpret_cast<__half *>(row) = shi;
+        *reinterpret_cast<__half *>(row + 16) = slo;
+        *reinterpret_cast<__half *>(row + (size_t)N * 16) = __half();  // chunk 1: k 8..15
+        *reinterpret_cast<__half *>(row + (size_t)N * 16 + 16) = __half();
+    }
+    if (t == 0) xinv[(size_t)s * VMAX + b] = b < n ? 1.0f / scale : 0.0f;
+}
+
+}  // namespace mm
+}  // namespace pk
+
+using namespace pk;
+
+namespace {
+
+// cuTensorMapEncodeTiled, from the driver through the runtime (no link
+// against libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (fn == nullptr) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// Per-device scratch of gguf_cuda_matmul, grown on demand.
+struct MmScratch {
+    uint8_t *xs = nullptr, *x2s = nullptr;
+    float *xinv = nullptr, *ypart = nullptr;
+    unsigned int *arrived = nullptr;
+    int *err = nullptr;
+    size_t xs_bytes = 0, x2s_bytes = 0, xinv_bytes = 0, ypart_bytes = 0, arrived_bytes = 0;
+    int smem_max = 0;
+};
+
+int grow(void **p, size_t &have, size_t need, bool zero)
+{
+    if (have >= need) return 1;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    have = 0;
+    if (cudaMalloc(p, need) != cudaSuccess) return 0;
+    if (zero && cudaMemset(*p, 0, need) != cudaSuccess) return 0;
+    have = need;
+    return 1;
+}
+
+MmScratch *mm_scratch(int dev, size_t xs_b, size_t x2s_b, size_t xinv_b, size_t yp_b, size_t arr_b)
+{
+    static MmScratch per[64];
+    if (dev < 0 || dev >= 64) return nullptr;
+    MmScratch &s = per[dev];
+    if (!grow((void **)&s.xs, s.xs_bytes, xs_b, false) || !grow((void **)&s.x2s, s.x2s_bytes, x2s_b, false) ||
+        !grow((void **)&s.xinv, s.xinv_bytes, xinv_b, false) || !grow((void **)&s.ypart, s.ypart_bytes, yp_b, false) ||
+        !grow((void **)&s.arrived, s.arrived_bytes, arr_b, true))
+        return nullptr;
+    if (s.err == nullptr) {
+        if (cudaMalloc(&s.err, sizeof(int)) != cudaSuccess) return nullptr;
+        if (cudaMemset(s.err, 0, sizeof(int)) != cudaSuccess) return nullptr;
+    }
+    if (s.smem_max == 0) {
+        int optin = 0;
+        cudaFuncAttributes fa;
+        if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+            cudaFuncGetAttributes(&fa, mm::q4k_mm_kernel) != cudaSuccess)
+            return nullptr;
+        const int avail = optin - (int)fa.sharedSizeBytes;
+        if (avail < mm::OFF_B + 4 * mm::B_SLOT_MAX + 128) return nullptr;
+        if (cudaFuncSetAttribute(mm::q4k_mm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, avail) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        s.smem_max = avail;
+    }
+    return &s;
+}
+
+}  // namespace
+
+// The work split of gguf_cuda_matmul for a matrix of `rows` rows and `nsb`
+// super-blocks per row on `sms` SMs: CTAs, and partial slots per row tile.
+extern "C" void gguf_cuda_matmul_plan(int rows, int nsb, int sms, int *ctas, int *maxp)
+{
+    const int tiles = (rows + mm::TM - 1) / mm::TM;
+    const long long U = (long long)tiles * nsb;
+    const int G = (int)(U < sms ? U : sms);
+    int mp = 1;
+    for (int T = 0; T < tiles; T++) {
+        const int c0 = mm::unit_owner((long long)T * nsb, U, G);
+        const int c1 = mm::unit_owner((long long)T * nsb + nsb - 1, U, G);
+        if (c1 - c0 + 1 > mp) mp = c1 - c0 + 1;
+    }
+    *ctas = G;
+    *maxp = mp;
+}
+
+extern "C" int gguf_cuda_matmul(const GGUFWeight *w, const float *x, int n, float *y, void *stream)
+{
+    if (w == nullptr || w->data == nullptr || x == nullptr || y == nullptr || n < 1 || n > mm::VMAX) return 0;
+    if (w->type != T_Q4_K || w->cols == 0 || w->cols % mm::QK || w->rows == 0) return 0;
+    if (w->rows > 0x7FFFFF00ull || w->cols > 0x7FFFFF00ull) return 0;
+    if (w->row_bytes != w->cols / mm::QK * mm::SBB || ((uintptr_t)w->data & 15) != 0) return 0;
+    const int rows = (int)w->rows, K = (int)w->cols, nsb = K / mm::QK;
+    const int N = (2 * n + 15) / 16 * 16;
+    cudaStream_t st = (cudaStream_t)stream;
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+        return 0;
+    const int tiles = (rows + mm::TM - 1) / mm::TM;
+    int G = 0, maxp = 0;
+    gguf_cuda_matmul_plan(rows, nsb, sms, &G, &maxp);
+    MmScratch *s = mm_scratch(dev, (size_t)nsb * 4 * N * 128, (size_t)nsb * N * 32, (size_t)nsb * mm::VMAX * 4,
+                              (size_t)tiles * maxp * n * mm::TM * sizeof(float), (size_t)tiles * 4 * sizeof(unsigned));
+    if (s == nullptr) return 0;
+    PFN_cuTensorMapEncodeTiled_v12000 enc = encode_tiled();
+    if (enc == nullptr) return 0;
+    CUtensorMap wmap;
+    const cuuint64_t gdim[2] = {(cuuint64_t)w->row_bytes, (cuuint64_t)rows};
+    const cuuint64_t gstride[1] = {(cuuint64_t)w->row_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)mm::SBB, (cuuint32_t)mm::TM};
+    const cuuint32_t estride[2] = {1, 1};
+    if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(w->data), gdim, gstride, box, estride,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return 0;
+    mm::MmArgs a;
+    a.rows = rows;
+    a.nsb = nsb;
+    a.xs = s->xs;
+    a.x2s = s->x2s;
+    a.xinv = s->xinv;
+    a.n = n;
+    a.N = N;
+    a.b_slot = N * 160;
+    a.sb = (s->smem_max - mm::OFF_B - 128) / a.b_slot;
+    if (a.sb > mm::SB_MAX) a.sb = mm::SB_MAX;
+    a.U = (long long)tiles * nsb;
+    a.G = G;
+    a.maxp = maxp;
+    a.y = y;
+    a.ypart = s->ypart;
+    a.arrived = s->arrived;
+    a.err = s->err;
+    const int smem = mm::OFF_B + a.sb * a.b_slot + 128;
+    mm::mm_stage_kernel<<<dim3(nsb, N / 2), 256, 0, st>>>(x, n, K, N, s->xs, s->x2s, s->xinv);
+    mm::q4k_mm_kernel<<<G, mm::THREADS, smem, st>>>(wmap, a);
+    return cudaGetLastError() == cudaSuccess;
+}
+
+// Error word of gguf_cuda_matmul on the current device (0: no wait has run
+// out of time), cleared by the read; -1 when it cannot be read.
+extern "C" int gguf_cuda_matmul_error(void)
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    MmScratch *s = mm_scratch(dev, 0, 0, 0, 0, 0);
+    if (s == nullptr) return -1;
+    int v = 0;
+    if (cudaMemcpy(&v, s->err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (v != 0) {
+        // an aborted call can leave tile counters behind: clear them
+        if (cudaMemset(s->err, 0, sizeof(int)) != cudaSuccess) return -1;
+        if (s->arrived != nullptr && cudaMemset(s->arrived, 0, s->arrived_bytes) != cudaSuccess) return -1;
+    }
+    return v;
+}

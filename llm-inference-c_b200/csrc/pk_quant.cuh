@@ -198,7 +198,7 @@ __device__ __forceinline__ float decode_col(int t, const uint8_t *row, int c)
 // decode_col as a real call: for the cold paths of the decode step (the
 // embedding row of layer 0), where inlining all seven decoders at every
 // use would only bloat the hot kernel's code.
-__device__ __noinline__ float decode_col_call(int t, const uint8_t *row, int c)
+static __device__ __noinline__ float decode_col_call(int t, const uint8_t *row, int c)
 {
     return decode_col(t, row, c);
 }

@@ -677,20 +677,23 @@ __device__ __forceinline__ void run_tile(const Phase &p, int t, int chunk, const
     if (p.epi == EPI_ADD && p.res_ll != nullptr && lane < nr && (p.nchunk == 1 || chunk == p.nchunk - 1)) {
         resw = ld_ll(p.res_ll + r0 + lane);
     }
-    float va;
+    // one call of the unrolled tile loop for both cases: a whole tile, or one
+    // column chunk of a row (weights relative to the chunk start, x at the
+    // chunk's units)
+    int nu = p.nunits, ccols = p.cols, u0 = 0;
     if (p.nchunk > 1) {
-        // the chunk's units (weights relative to the chunk start; x at the same units)
-        const int u0 = chunk * p.cunits, nu = min(p.cunits, p.nunits - u0);
-        const int ccols = min(64 * nu, p.cols - 64 * u0);
+        u0 = chunk * p.cunits;
+        nu = min(p.cunits, p.nunits - u0);
+        ccols = min(64 * nu, p.cols - 64 * u0);
         st += (uintptr_t)chunk * (uintptr_t)p.cbytes;
-        va = tile_dispatch<MASK>(s.type, buf + (st & 15), s.rb, 1, nu, ccols, xq + (size_t)u0 * XQ_UNIT_BYTES,
-                                 xg + (size_t)u0 * XG_UNIT_WORDS, lane);
+    }
+    float va = tile_dispatch<MASK>(s.type, buf + (st & 15), s.rb, nr, nu, ccols, xq + (size_t)u0 * XQ_UNIT_BYTES,
+                                   xg + (size_t)u0 * XG_UNIT_WORDS, lane);
+    if (p.nchunk > 1) {
         racc += va;
         if (chunk < p.nchunk - 1) return;
         va = racc;
         racc = 0.0f;
-    } else {
-        va = tile_dispatch<MASK>(s.type, buf + (st & 15), s.rb, nr, p.nunits, p.cols, xq, xg, lane);
     }
     // Epilogue: lane i owns row r0 + i.
     const int r = r0 + lane;

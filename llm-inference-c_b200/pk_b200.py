@@ -29,6 +29,7 @@ EXPORTS = [
     "engine_weight_bytes", "engine_generate_greedy", "engine_trace", "engine_launches_per_step",
     "engine_tp_plan", "engine_open_tp", "engine_tp_handle", "engine_tp_connect",
     "gguf_cuda_matvec", "gguf_cuda_dequantize_rows", "gguf_cuda_fp16_table", "gguf_cuda_matvec_noalloc",
+    "gguf_cuda_matmul", "gguf_cuda_matmul_plan", "gguf_cuda_matmul_error",
     "tokenizer_free",
 ]
 
@@ -143,6 +144,13 @@ def lib(path=LIB_PATH):
     L.gguf_cuda_matvec_noalloc.restype = ctypes.c_int
     L.gguf_cuda_matvec_noalloc.argtypes = [ctypes.POINTER(GGUFWeight), _P, _P, _P, ctypes.c_char_p,
                                            ctypes.c_size_t]
+    L.gguf_cuda_matmul.restype = ctypes.c_int
+    L.gguf_cuda_matmul.argtypes = [ctypes.POINTER(GGUFWeight), _P, ctypes.c_int, _P, _P]
+    L.gguf_cuda_matmul_plan.restype = None
+    L.gguf_cuda_matmul_plan.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
+                                        ctypes.POINTER(ctypes.c_int)]
+    L.gguf_cuda_matmul_error.restype = ctypes.c_int
+    L.gguf_cuda_matmul_error.argtypes = []
     _lib = L
     return L
 
@@ -288,6 +296,22 @@ def matvec_noalloc(weight, x_ptr, y_ptr, stream=0):
     err = ctypes.create_string_buffer(256)
     rc = lib().gguf_cuda_matvec_noalloc(ctypes.byref(weight), x_ptr, y_ptr, stream, err, 256)
     return rc, err.value.decode()
+
+
+def matmul(weight, x_ptr, n, y_ptr, stream=0):
+    """gguf_cuda_matmul: y (n x rows) = x (n x cols) times W transposed."""
+    return lib().gguf_cuda_matmul(ctypes.byref(weight), x_ptr, n, y_ptr, stream)
+
+
+def matmul_plan(rows, nsb, sms):
+    """gguf_cuda_matmul_plan: (CTAs, most CTAs sharing one 128-row tile)."""
+    g, mp = ctypes.c_int(), ctypes.c_int()
+    lib().gguf_cuda_matmul_plan(rows, nsb, sms, ctypes.byref(g), ctypes.byref(mp))
+    return g.value, mp.value
+
+
+def matmul_error():
+    return lib().gguf_cuda_matmul_error()
 
 
 def dequantize_rows(weight, row0, nrows, out_ptr, stream=0):
