@@ -102,6 +102,29 @@ int engine_tp_connect(LLMModel *model, const void *handles, char *error, size_t 
  * cannot co-schedule the step kernel; 0 for a NULL handle. */
 int engine_launches_per_step(const LLMModel *model);
 
+/* ---- Batched decode (additive; the reference decodes one sequence) --
+ * Up to ENGINE_BATCH_MAX independent sequences decode together, sharing
+ * one pass over the weights per step: Q4_K matrices on the tensor cores,
+ * the other formats on CUDA cores. Each sequence has its own KV cache of
+ * the model's context length, separate from the one engine_forward uses.
+ * Single GPU only (refused on a tensor-parallel rank). */
+#define ENGINE_BATCH_MAX 64
+
+/* Allocate the batched state for max_seqs sequences (1..64), dropping any
+ * previous one. Returns 1, or 0 with a message in error. */
+int engine_batch_open(LLMModel *model, int max_seqs, char *error, size_t error_capacity);
+
+/* One decode step: sequence seq_ids[i] consumes tokens[i] at position
+ * pos[i] (i < n; seq_ids distinct, below max_seqs; tokens in the
+ * vocabulary; positions below the context length), exactly as
+ * engine_forward(tokens[i], pos[i]) would for that sequence alone.
+ * next_tokens[i] receives the greedy token (device argmax, lowest index on
+ * ties; -1 when a logit is not finite); logits, when not NULL, the n x
+ * vocab_size logits (row i for sequence seq_ids[i]). Returns 1, or 0 on
+ * bad arguments or a device error (engine_last_error). */
+int engine_forward_batch(LLMModel *model, const int *tokens, const int *pos, const int *seq_ids, int n,
+                         int *next_tokens, float *logits);
+
 #ifdef __cplusplus
 }
 #endif

@@ -102,9 +102,11 @@ struct LLMModel {
     Tokenizer tokenizer;
     char description[256];
     PkdCtx *dev;
+    PkbCtx *batch;     /* batched decode state (engine_batch_open), or NULL */
     uint64_t weight_bytes;
     int tp_world;      /* tensor-parallel ranks (1: single GPU) */
     int connected;     /* the decode step exists (tensor parallel: after engine_tp_connect) */
+    int batch_seqs;    /* sequences of the batched state */
     char last_error[256];
 };
 
@@ -604,6 +606,7 @@ void engine_close(LLMModel *m)
 {
     if (m == NULL) return;
     tokenizer_free(&m->tokenizer);
+    pkb_destroy(m->batch);
     pkd_destroy(m->dev);
     free(m);
 }
@@ -932,6 +935,48 @@ int engine_generate_greedy(LLMModel *m, int token, int pos, int n, int *out_toke
     }
     if (!pkd_generate_greedy(m->dev, token, pos, n, out_tokens, device_ms)) {
         snprintf(m->last_error, sizeof(m->last_error), "%s", pkd_error(m->dev));
+        return 0;
+    }
+    return 1;
+}
+
+int engine_batch_open(LLMModel *m, int max_seqs, char *err, size_t cap)
+{
+    if (m == NULL || m->dev == NULL || !m->connected) {
+        seterr(err, cap, "No model.");
+        return 0;
+    }
+    if (m->tp_world > 1) {
+        seterr(err, cap, "Batched decode runs on one GPU (not on a tensor-parallel rank).");
+        return 0;
+    }
+    if (max_seqs < 1 || max_seqs > ENGINE_BATCH_MAX) {
+        seterr(err, cap, "Batched decode takes 1 to 64 sequences.");
+        return 0;
+    }
+    pkb_destroy(m->batch);  /* a new open drops the old sequences */
+    m->batch = pkb_create(m->dev, max_seqs, err, cap);
+    if (m->batch == NULL) return 0;
+    m->batch_seqs = max_seqs;
+    if (err && cap) err[0] = '\0';
+    return 1;
+}
+
+int engine_forward_batch(LLMModel *m, const int *tokens, const int *pos, const int *seq_ids, int n,
+                         int *next_tokens, float *logits)
+{
+    if (m == NULL || m->batch == NULL || tokens == NULL || pos == NULL || seq_ids == NULL || next_tokens == NULL ||
+        n < 1 || n > m->batch_seqs)
+        return 0;
+    unsigned long long seen = 0;  /* batch_seqs <= 64: one bit per sequence */
+    for (int i = 0; i < n; i++) {
+        if (tokens[i] < 0 || tokens[i] >= m->config.vocab_size || pos[i] < 0 || pos[i] >= m->config.seq_len ||
+            seq_ids[i] < 0 || seq_ids[i] >= m->batch_seqs || (seen >> seq_ids[i]) & 1ull)
+            return 0;
+        seen |= 1ull << seq_ids[i];
+    }
+    if (!pkb_step(m->batch, tokens, pos, seq_ids, n, next_tokens, logits)) {
+        snprintf(m->last_error, sizeof(m->last_error), "%s", pkb_error(m->batch));
         return 0;
     }
     return 1;

@@ -1,0 +1,536 @@
+// pk_batch.cu - batched decode: one step for up to 64 independent sequences
+// that share one pass over the weights. The reference decodes one sequence
+// at a time (src/engine.c:137-407 over src/gguf_forward.c); per sequence
+// this step computes the same layer loop (gguf_forward.c: RMSNorm, Q/K/V,
+// RoPE, KV-cache append, GQA attention, Wo + residual, RMSNorm, SwiGLU,
+// down + residual, final norm, logits), so each sequence's logits are
+// those of the single-sequence forward up to float rounding.
+//
+// Work per layer, all on the device:
+//   matmuls      Q4_K weights on the tensor cores (pk_mma.cu); every other
+//                format on CUDA cores by mv_tile_kernel, which decodes each
+//                weight once per 64-vector tile into shared memory;
+//   elementwise  embedding rows, RMSNorm, RoPE + cache append, attention
+//                (one CTA per head and sequence), residual adds, SwiGLU,
+//                greedy argmax per sequence.
+// The launches of one step are captured once per batch size n in a CUDA
+// graph (inputs and outputs through fixed pinned buffers).
+//
+// KV caches: [sequence][layer][position][kv_dim] fp32, as the reference's
+// run state (src/transformer.c: key_cache / value_cache) per sequence.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "pk_dev.h"
+#include "pk_mma.h"
+#include "pk_quant.cuh"
+
+namespace pk {
+namespace bt {
+
+constexpr int BMAX = 64;            // sequences per step
+constexpr int TR = 64, TK = 256;    // mv_tile_kernel: rows per CTA, columns per chunk
+constexpr int WS = 68, XS = 66;     // padded row strides of its shared tiles (floats)
+constexpr int MV_SMEM = TK * WS * 4 + TK * XS * 4;
+
+__device__ __forceinline__ float block_sum(float v, float *red)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += red[w];
+    return t;
+}
+
+__device__ __forceinline__ float block_max(float v, float *red)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) t = fmaxf(t, red[w]);
+    return t;
+}
+
+// y[b][r] = sum_c W[r][c] x[b][c] (b < n <= 64) on CUDA cores. Per CTA 64
+// rows; per chunk of 256 columns the weights are decoded once into shared
+// memory (bit-exact decoders, column-major) next to the chunk of every x_b,
+// then thread (rg, vg) accumulates rows 8rg .. 8rg+7 for vectors 2vg, 2vg+1.
+template <int T>
+__global__ void __launch_bounds__(256) mv_tile_kernel(const uint8_t *w, uint64_t rb, int rows, int cols,
+                                                      const float *x, int n, float *y)
+{
+    extern __shared__ float smt[];
+    float *Ws = smt, *Xs = smt + TK * WS;
+    const int tid = threadIdx.x, rg = tid & 7, vg = tid >> 3;
+    const int row0 = blockIdx.x * TR;
+    const bool active = 2 * vg < n;  // warp-uniform (a warp holds vg 4w .. 4w+3)
+    const int npad = (n + 1) & ~1;
+    float acc[8][2];
+#pragma unroll
+    for (int i = 0; i < 8; i++) acc[i][0] = acc[i][1] = 0.0f;
+    for (int k0 = 0; k0 < cols; k0 += TK) {
+        const int kc = min(TK, cols - k0);
+        for (int r = 0; r < TR; r++) {
+            float v = 0.0f;
+            if (tid < kc && row0 + r < rows) v = decode_col(T, w + (size_t)(row0 + r) * rb, k0 + tid);
+            Ws[tid * WS + r] = v;
+        }
+        for (int e = tid; e < npad * TK; e += 256) {
+            const int b = e / TK, k = e % TK;
+            Xs[k * XS + b] = (b < n && k < kc) ? x[(size_t)b * cols + k0 + k] : 0.0f;
+        }
+        __syncthreads();
+        if (active) {
+#pragma unroll 4
+            for (int k = 0; k < kc; k++) {
+                const float4 w0 = *reinterpret_cast<const float4 *>(Ws + k * WS + 8 * rg);
+                const float4 w1 = *reinterpret_cast<const float4 *>(Ws + k * WS + 8 * rg + 4);
+                const float2 xv = *reinterpret_cast<const float2 *>(Xs + k * XS + 2 * vg);
+                const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    acc[i][0] = fmaf(wv[i], xv.x, acc[i][0]);
+                    acc[i][1] = fmaf(wv[i], xv.y, acc[i][1]);
+                }
+            }
+        }
+        __syncthreads();
+    }
+    if (!active) return;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int r = row0 + 8 * rg + i;
+        if (r >= rows) break;
+        y[(size_t)(2 * vg) * rows + r] = acc[i][0];
+        if (2 * vg + 1 < n) y[(size_t)(2 * vg + 1) * rows + r] = acc[i][1];
+    }
+}
+
+// x[b] = embedding row tokens[b] (src/gguf_forward.c: the token's row of
+// token_embd, decoded).
+__global__ void embed_kernel(const uint8_t *embd, uint64_t rb, int type, const int *io, int dim, float *x)
+{
+    const int b = blockIdx.x, tok = io[b];
+    const uint8_t *row = embd + (size_t)tok * rb;
+    for (int c = threadIdx.x; c < dim; c += blockDim.x) x[(size_t)b * dim + c] = decode_col(type, row, c);
+}
+
+// out[b] = w * (x[b] / sqrt(mean(x[b]^2) + eps)), as rmsnorm in
+// src/gguf_forward.c (the same rounding steps as the single-sequence step).
+__global__ void rmsnorm_kernel(const float *x, const float *w, int dim, float eps, float *out)
+{
+    __shared__ float red[32];
+    const float *xb = x + (size_t)blockIdx.x * dim;
+    float ss = 0.0f;
+    for (int c = threadIdx.x; c < dim; c += blockDim.x) ss = fmaf(xb[c], xb[c], ss);
+    const float tot = block_sum(ss, red);
+    const float m = __fadd_rn(__fdiv_rn(tot, (float)dim), eps);
+    const float sc = __fdiv_rn(1.0f, __fsqrt_rn(m));
+    for (int c = threadIdx.x; c < dim; c += blockDim.x)
+        out[(size_t)blockIdx.x * dim + c] = __fmul_rn(w[c], __fmul_rn(sc, xb[c]));
+}
+
+// RoPE on q and k of sequence b at its position (pairs (2i, 2i + 1) of each
+// head, cos/sin from the reference's table), then k and v appended to the
+// sequence's cache (src/gguf_forward.c:50-66 and the cache writes).
+__global__ void rope_cache_kernel(float *q, const float *k, const float *v, const float *rope_cs, int rope_dim,
+                                  int hs, int qd, int kvd, const int *io, int bmax, int layer, int L, int seq_len,
+                                  float *kc, float *vc)
+{
+    const int b = blockIdx.x;
+    const int pos = io[bmax + b], seq = io[2 * bmax + b];
+    const float *rope = rope_cs + (size_t)pos * rope_dim;
+    float *qb = q + (size_t)b * qd;
+    for (int p = threadIdx.x; p < qd / 2; p += blockDim.x) {
+        const int d0 = (2 * p) % hs;
+        if (d0 < rope_dim) {
+            const float c = rope[d0], sn = rope[d0 + 1], v0 = qb[2 * p], v1 = qb[2 * p + 1];
+            qb[2 * p] = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, sn));
+            qb[2 * p + 1] = __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, c));
+        }
+    }
+    const size_t row = (((size_t)seq * L + layer) * seq_len + pos) * kvd;
+    const float *kb = k + (size_t)b * kvd, *vb = v + (size_t)b * kvd;
+    for (int p = threadIdx.x; p < kvd / 2; p += blockDim.x) {
+        const int d0 = (2 * p) % hs;
+        float v0 = kb[2 * p], v1 = kb[2 * p + 1];
+        if (d0 < rope_dim) {
+            const float c = rope[d0], sn = rope[d0 + 1];
+            const float r0 = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, sn));
+            const float r1 = __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, c));
+            v0 = r0;
+            v1 = r1;
+        }
+        kc[row + 2 * p] = v0;
+        kc[row + 2 * p + 1] = v1;
+        vc[row + 2 * p] = vb[2 * p];
+        vc[row + 2 * p + 1] = vb[2 * p + 1];
+    }
+}
+
+// Attention of query head h of sequence b over positions 0 .. pos
+// (grouped-query: KV head h / kv_mul), as in src/gguf_forward.c: scores
+// q . k_t * scale, softmax, weighted sum of v_t. Scores in shared memory.
+__global__ void attention_kernel(const float *q, const float *kc, const float *vc, const int *io, int bmax,
+                                 int layer, int L, int seq_len, int hs, int qd, int kvd, int kv_mul, float scale,
+                                 float *out)
+{
+    extern __shared__ float sc[];  // seq_len scores, then hs query values
+    __shared__ float red[32];
+    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nw = blockDim.x >> 5;
+    const int P = io[bmax + b] + 1, seq = io[2 * bmax + b];
+    float *qs = sc + seq_len;
+    for (int d = tid; d < hs; d += blockDim.x) qs[d] = q[(size_t)b * qd + (size_t)h * hs + d];
+    __syncthreads();
+    const size_t base = ((size_t)seq * L + layer) * seq_len * kvd + (size_t)(h / kv_mul) * hs;
+    for (int t = warp; t < P; t += nw) {
+        const float *kt = kc + base + (size_t)t * kvd;
+        float dot = 0.0f;
+        for (int d = lane; d < hs; d += 32) dot = fmaf(qs[d], kt[d], dot);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xFFFFFFFFu, dot, o);
+        if (lane == 0) sc[t] = dot * scale;
+    }
+    __syncthreads();
+    float m = -INFINITY;
+    for (int t = tid; t < P; t += blockDim.x) m = fmaxf(m, sc[t]);
+    m = block_max(m, red);
+    float s = 0.0f;
+    for (int t = tid; t < P; t += blockDim.x) {
+        const float e = expf(sc[t] - m);
+        sc[t] = e;
+        s += e;
+    }
+    s = block_sum(s, red);
+    const float inv = 1.0f / s;
+    for (int t = tid; t < P; t += blockDim.x) sc[t] *= inv;
+    __syncthreads();
+    for (int d = tid; d < hs; d += blockDim.x) {
+        float o = 0.0f;
+        const float *vt = vc + base + d;
+        for (int t = 0; t < P; t++) o = fmaf(sc[t], vt[(size_t)t * kvd], o);
+        out[(size_t)b * qd + (size_t)h * hs + d] = o;
+    }
+}
+
+__global__ void add_kernel(float *x, const float *y, int count)
+{
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) x[i] += y[i];
+}
+
+// g = silu(g) * u, the reference's rounding steps (src/gguf_forward.c).
+__global__ void swiglu_kernel(float *g, const float *u, int count)
+{
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) {
+        const float v = g[i];
+        g[i] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u[i]);
+    }
+}
+
+// Greedy token of sequence b: the largest logit, the lowest index on ties
+// (src/sampler.c:39-52); -1 when a logit is not finite.
+__global__ void argmax_kernel(const float *logits, int vocab, int *next)
+{
+    __shared__ float bv[32];
+    __shared__ int bi[32], bad[32];
+    const float *l = logits + (size_t)blockIdx.x * vocab;
+    float best = -INFINITY;
+    int idx = 0x7FFFFFFF, nonfinite = 0;
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+        const float v = l[i];
+        if (!isfinite(v)) nonfinite = 1;
+        else if (v > best || (v == best && i < idx)) {
+            best = v;
+            idx = i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+        const int oi = __shfl_xor_sync(0xFFFFFFFFu, idx, o);
+        nonfinite |= __shfl_xor_sync(0xFFFFFFFFu, nonfinite, o);
+        if (ov > best || (ov == best && oi < idx)) {
+            best = ov;
+            idx = oi;
+        }
+    }
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+        bv[warp] = best;
+        bi[warp] = idx;
+        bad[warp] = nonfinite;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) {
+            nonfinite |= bad[w];
+            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) {
+                best = bv[w];
+                idx = bi[w];
+            }
+        }
+        next[blockIdx.x] = nonfinite ? -1 : idx;
+    }
+}
+
+}  // namespace bt
+}  // namespace pk
+
+using namespace pk;
+
+struct PkbCtx {
+    int device, sms, max_seqs;
+    cudaStream_t st;
+    PkdModel m;  // tensor tables owned by the PkdCtx
+    const uint8_t *arena;
+    const float *norms, *rope_cs;
+    float *kc, *vc;                                           // [max_seqs][L][seq_len][kvd]
+    float *x, *xn, *q, *k, *v, *att, *tmp, *g, *u, *logits;  // [64][width]
+    int *io_d, *io_h;  // [tokens 64][pos 64][seq 64][next 64][error word]
+    PkMmScratch mm;
+    cudaGraph_t graph[bt::BMAX + 1];
+    cudaGraphExec_t exec[bt::BMAX + 1];
+    int tile_attr;
+    char msg[256];
+};
+
+static int bfail(PkbCtx *b, cudaError_t e, const char *what)
+{
+    if (e == cudaSuccess) return 0;
+    snprintf(b->msg, sizeof(b->msg), "CUDA %s failed: %s", what, cudaGetErrorString(e));
+    return 1;
+}
+
+// y (n x rows) = x (n x cols) W^T for one weight tensor.
+static int bmatmul(PkbCtx *b, const PkdTensor &t, const float *x, int n, float *y)
+{
+    const uint8_t *w = b->arena + t.offset;
+    const int rows = (int)t.rows, cols = (int)t.cols;
+    if (pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, w)) return pk_mm_run(w, t.row_bytes, rows, cols, x, n, y, &b->mm, b->sms, b->st);
+    const dim3 grid((rows + bt::TR - 1) / bt::TR);
+    switch (t.type) {
+#define PKB_CASE(T)                                                                                           \
+    case T:                                                                                                   \
+        bt::mv_tile_kernel<T><<<grid, 256, bt::MV_SMEM, b->st>>>(w, t.row_bytes, rows, cols, x, n, y);        \
+        break;
+        PKB_CASE(T_F32)
+        PKB_CASE(T_F16)
+        PKB_CASE(T_Q4_0)
+        PKB_CASE(T_Q8_0)
+        PKB_CASE(T_Q4_K)
+        PKB_CASE(T_Q5_K)
+        PKB_CASE(T_Q6_K)
+#undef PKB_CASE
+    default:
+        return 0;
+    }
+    return cudaGetLastError() == cudaSuccess;
+}
+
+// The launches of one step for n sequences (inputs already in io_d).
+static int enqueue_step(PkbCtx *b, int n)
+{
+    const PkdModel &m = b->m;
+    const int dim = m.dim, hs = m.head_size, qd = m.n_heads * hs, kvd = m.n_kv_heads * hs, hid = m.hidden_dim;
+    const int L = m.n_layers, B = bt::BMAX;
+    cudaStream_t st = b->st;
+    const int ew = (n * (hid > dim ? hid : dim) + 255) / 256;
+    bt::embed_kernel<<<n, 256, 0, st>>>(b->arena + m.embd.offset, m.embd.row_bytes, (int)m.embd.type, b->io_d, dim,
+                                        b->x);
+    const size_t att_smem = ((size_t)m.seq_len + hs) * 4;
+    for (int l = 0; l < L; l++) {
+        bt::rmsnorm_kernel<<<n, 256, 0, st>>>(b->x, b->norms + (size_t)(2 * l) * dim, dim, m.rms_eps, b->xn);
+        if (!bmatmul(b, m.wq[l], b->xn, n, b->q) || !bmatmul(b, m.wk[l], b->xn, n, b->k) ||
+            !bmatmul(b, m.wv[l], b->xn, n, b->v))
+            return 0;
+        bt::rope_cache_kernel<<<n, 256, 0, st>>>(b->q, b->k, b->v, b->rope_cs, m.rope_dim, hs, qd, kvd, b->io_d, B, l,
+                                                 L, m.seq_len, b->kc, b->vc);
+        bt::attention_kernel<<<dim3(m.n_heads, n), 128, att_smem, st>>>(b->q, b->kc, b->vc, b->io_d, B, l, L,
+                                                                         m.seq_len, hs, qd, kvd,
+                                                                         m.n_heads / m.n_kv_heads, m.att_scale, b->att);
+        if (!bmatmul(b, m.wo[l], b->att, n, b->tmp)) return 0;
+        bt::add_kernel<<<(n * dim + 255) / 256, 256, 0, st>>>(b->x, b->tmp, n * dim);
+        bt::rmsnorm_kernel<<<n, 256, 0, st>>>(b->x, b->norms + (size_t)(2 * l + 1) * dim, dim, m.rms_eps, b->xn);
+        if (!bmatmul(b, m.gate[l], b->xn, n, b->g) || !bmatmul(b, m.up[l], b->xn, n, b->u)) return 0;
+        bt::swiglu_kernel<<<ew, 256, 0, st>>>(b->g, b->u, n * hid);
+        if (!bmatmul(b, m.down[l], b->g, n, b->tmp)) return 0;
+        bt::add_kernel<<<(n * dim + 255) / 256, 256, 0, st>>>(b->x, b->tmp, n * dim);
+    }
+    bt::rmsnorm_kernel<<<n, 256, 0, st>>>(b->x, b->norms + (size_t)(2 * L) * dim, dim, m.rms_eps, b->xn);
+    if (!bmatmul(b, m.output, b->xn, n, b->logits)) return 0;
+    bt::argmax_kernel<<<n, 256, 0, st>>>(b->logits, m.vocab_size, b->io_d + 3 * B);
+    // the greedy tokens and the matmul error word come back with the step
+    cudaMemcpyAsync(b->io_d + 4 * B, b->mm.err, sizeof(int), cudaMemcpyDeviceToDevice, st);
+    cudaMemcpyAsync(b->io_h + 3 * B, b->io_d + 3 * B, (B + 1) * sizeof(int), cudaMemcpyDeviceToHost, st);
+    return cudaGetLastError() == cudaSuccess;
+}
+
+extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
+{
+    PkdView v;
+    if (!pkd_view(ctx, &v)) {
+        if (err && cap) snprintf(err, cap, "Batched decode needs a built single-GPU model.");
+        return NULL;
+    }
+    if (max_seqs < 1 || max_seqs > bt::BMAX) {
+        if (err && cap) snprintf(err, cap, "Batched decode takes 1 to %d sequences.", bt::BMAX);
+        return NULL;
+    }
+    const PkdModel &m = *v.model;
+    if ((m.head_size & 1) || m.rope_dim > m.head_size || (m.rope_dim & 1)) {
+        if (err && cap) snprintf(err, cap, "Unsupported model shape for batched decode.");
+        return NULL;
+    }
+    PkbCtx *b = (PkbCtx *)calloc(1, sizeof(PkbCtx));
+    if (b == NULL) {
+        if (err && cap) snprintf(err, cap, "Out of memory.");
+        return NULL;
+    }
+    b->device = v.device;
+    b->st = (cudaStream_t)v.stream;
+    b->m = m;
+    b->arena = v.arena;
+    b->norms = v.norms;
+    b->rope_cs = v.rope_cs;
+    b->max_seqs = max_seqs;
+    cudaSetDevice(b->device);
+    cudaDeviceGetAttribute(&b->sms, cudaDevAttrMultiProcessorCount, b->device);
+    const int B = bt::BMAX, dim = m.dim, hs = m.head_size, qd = m.n_heads * hs, kvd = m.n_kv_heads * hs;
+    const size_t cache = (size_t)max_seqs * m.n_layers * m.seq_len * kvd;
+    // matmul scratch: the largest need over the model's Q4_K weights at n = 64
+    PkMmNeed mx = {0, 0, 0, 0, 0};
+    const PkdTensor *lists[7] = {m.wq, m.wk, m.wv, m.wo, m.gate, m.up, m.down};
+    for (int j = 0; j <= 7 * m.n_layers; j++) {
+        const PkdTensor &t = j == 7 * m.n_layers ? m.output : lists[j / m.n_layers][j % m.n_layers];
+        if (!pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, v.arena + t.offset)) continue;
+        PkMmNeed nd;
+        pk_mm_need((int)t.rows, (int)t.cols, B, b->sms, &nd);
+        if (nd.xs > mx.xs) mx.xs = nd.xs;
+        if (nd.x2s > mx.x2s) mx.x2s = nd.x2s;
+        if (nd.xinv > mx.xinv) mx.xinv = nd.xinv;
+        if (nd.ypart > mx.ypart) mx.ypart = nd.ypart;
+        if (nd.arrived > mx.arrived) mx.arrived = nd.arrived;
+    }
+    b->mm.smem_max = pk_mm_smem_max(b->device);
+    int ok = b->mm.smem_max > 0 || mx.xs == 0;
+    if (!ok) snprintf(b->msg, sizeof(b->msg), "The tensor-core matmul cannot run on this device.");
+    ok = ok && !bfail(b, cudaMalloc(&b->kc, cache * 4), "cudaMalloc(batched KV cache)") &&
+         !bfail(b, cudaMalloc(&b->vc, cache * 4), "cudaMalloc(batched KV cache)") &&
+         !bfail(b, cudaMalloc(&b->x, (size_t)B * dim * 4), "cudaMalloc") &&
+         !bfail(b, cudaMalloc(&b->xn, (size_t)B * dim * 4), "cudaMalloc") &&
+         !bfail(b, cudaMalloc(&b->tmp, (size_t)B * dim * 4), "cudaMalloc") &&
+         !bfail(b, cudaMalloc(&b->q, (size_t)B * qd * 4), "cudaMalloc") &&
+         !bfail(b, cudaMalloc(&b->att, (size_t)B * qd * 4), "cudaMalloc") &&
+         !bfail(b, cudaMalloc(&b->k, (size_t)B * kvd * 4), "cudaMalloc") &&
+         !bfail(b, cudaMalloc(&b->v, (size_t)B * kvd * 4), "cudaMalloc") &&
+         !bfail(b, cudaMalloc(&b->g, (size_t)B * m.hidden_dim * 4), "cudaMalloc") &&
+         !bfail(b, cudaMalloc(&b->u, (size_t)B * m.hidden_dim * 4), "cudaMalloc") &&
+         !bfail(b, cudaMalloc(&b->logits, (size_t)B * m.vocab_size * 4), "cudaMalloc") &&
+         !bfail(b, cudaMalloc(&b->io_d, (size_t)(5 * B) * 4), "cudaMalloc") &&
+         !bfail(b, cudaMallocHost(&b->io_h, (size_t)(5 * B) * 4), "cudaMallocHost") &&
+         !bfail(b, cudaMalloc(&b->mm.xs, mx.xs + 16), "cudaMalloc") &&
+         !bfail(b, cudaMalloc(&b->mm.x2s, mx.x2s + 16), "cudaMalloc") &&
+         !bfail(b, cudaMalloc(&b->mm.xinv, mx.xinv + 16), "cudaMalloc") &&
+         !bfail(b, cudaMalloc(&b->mm.ypart, mx.ypart + 16), "cudaMalloc") &&
+         !bfail(b, cudaMalloc(&b->mm.arrived, mx.arrived + 16), "cudaMalloc") &&
+         !bfail(b, cudaMalloc(&b->mm.err, 16), "cudaMalloc") &&
+         !bfail(b, cudaMemsetAsync(b->mm.arrived, 0, mx.arrived + 16, b->st), "cudaMemset") &&
+         !bfail(b, cudaMemsetAsync(b->mm.err, 0, 16, b->st), "cudaMemset") &&
+         !bfail(b, cudaMemsetAsync(b->kc, 0, cache * 4, b->st), "cudaMemset") &&
+         !bfail(b, cudaMemsetAsync(b->vc, 0, cache * 4, b->st), "cudaMemset");
+#define PKB_ATTR(T)                                                                                           \
+    ok = ok && !bfail(b, cudaFuncSetAttribute(bt::mv_tile_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                              bt::MV_SMEM),                                                   \
+                      "cudaFuncSetAttribute");
+    PKB_ATTR(T_F32)
+    PKB_ATTR(T_F16)
+    PKB_ATTR(T_Q4_0)
+    PKB_ATTR(T_Q8_0)
+    PKB_ATTR(T_Q4_K)
+    PKB_ATTR(T_Q5_K)
+    PKB_ATTR(T_Q6_K)
+#undef PKB_ATTR
+    const size_t att_smem = ((size_t)m.seq_len + hs) * 4;
+    if (ok && att_smem > 48 * 1024)
+        ok = !bfail(b, cudaFuncSetAttribute(bt::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)att_smem),
+                    "cudaFuncSetAttribute");
+    ok = ok && !bfail(b, cudaStreamSynchronize(b->st), "batched setup");
+    if (!ok) {
+        if (err && cap) snprintf(err, cap, "%s", b->msg[0] ? b->msg : "Batched decode setup failed.");
+        pkb_destroy(b);
+        return NULL;
+    }
+    return b;
+}
+
+extern "C" int pkb_step(PkbCtx *b, const int *tokens, const int *pos, const int *seq_ids, int n, int *next,
+                        float *logits)
+{
+    const int B = bt::BMAX;
+    cudaSetDevice(b->device);
+    memcpy(b->io_h, tokens, (size_t)n * 4);
+    memcpy(b->io_h + B, pos, (size_t)n * 4);
+    memcpy(b->io_h + 2 * B, seq_ids, (size_t)n * 4);
+    if (b->exec[n] == NULL) {
+        // capture the step for this batch size: input copy, kernels, outputs
+        cudaGetLastError();
+        if (bfail(b, cudaStreamBeginCapture(b->st, cudaStreamCaptureModeThreadLocal), "capture")) return 0;
+        cudaMemcpyAsync(b->io_d, b->io_h, (size_t)(3 * B) * 4, cudaMemcpyHostToDevice, b->st);
+        const int ok = enqueue_step(b, n);
+        cudaGraph_t g = NULL;
+        const cudaError_t e = cudaStreamEndCapture(b->st, &g);
+        if (!ok || bfail(b, e, "capture") || bfail(b, cudaGraphInstantiate(&b->exec[n], g, 0), "graph instantiate")) {
+            if (!b->msg[0]) snprintf(b->msg, sizeof(b->msg), "Could not build the batched step.");
+            if (g) cudaGraphDestroy(g);
+            b->exec[n] = NULL;
+            return 0;
+        }
+        b->graph[n] = g;
+    }
+    if (bfail(b, cudaGraphLaunch(b->exec[n], b->st), "graph launch") ||
+        bfail(b, cudaStreamSynchronize(b->st), "batched step"))
+        return 0;
+    if (b->io_h[4 * B] != 0) {
+        snprintf(b->msg, sizeof(b->msg), "A tensor-core matmul wait ran out of time (error word %d).", b->io_h[4 * B]);
+        return 0;
+    }
+    memcpy(next, b->io_h + 3 * B, (size_t)n * 4);
+    if (logits != NULL &&
+        bfail(b, cudaMemcpy(logits, b->logits, (size_t)n * b->m.vocab_size * 4, cudaMemcpyDeviceToHost),
+              "logits copy"))
+        return 0;
+    return 1;
+}
+
+extern "C" const char *pkb_error(const PkbCtx *b)
+{
+    return b ? b->msg : "";
+}
+
+extern "C" void pkb_destroy(PkbCtx *b)
+{
+    if (b == NULL) return;
+    cudaSetDevice(b->device);
+    for (int i = 0; i <= bt::BMAX; i++) {
+        if (b->exec[i]) cudaGraphExecDestroy(b->exec[i]);
+        if (b->graph[i]) cudaGraphDestroy(b->graph[i]);
+    }
+    void *dev[] = {b->kc, b->vc, b->x, b->xn, b->tmp, b->q, b->att, b->k, b->v, b->g, b->u, b->logits, b->io_d,
+                   b->mm.xs, b->mm.x2s, b->mm.xinv, b->mm.ypart, b->mm.arrived, b->mm.err};
+    for (void *p : dev)
+        if (p) cudaFree(p);
+    if (b->io_h) cudaFreeHost(b->io_h);
+    free(b);
+}

@@ -101,6 +101,39 @@ const char *pkd_error(const PkdCtx *ctx);
  * phases + 1 otherwise). */
 int pkd_launches_per_step(const PkdCtx *ctx);
 
+/* What the batched step (pk_batch.cu) reads from a built single-GPU
+ * context: the stream, the weight arena, the decoded norms
+ * ([2 * n_layers + 1][dim]: attention and FFN norm of each layer, then the
+ * output norm), the RoPE table on the device ([seq_len][rope_dim]) and the
+ * model (tensor tables owned by the context). */
+typedef struct {
+    int device;
+    void *stream;
+    const uint8_t *arena;
+    const float *norms;
+    const float *rope_cs;
+    const PkdModel *model;
+} PkdView;
+
+/* 0 for a tensor-parallel rank or an unbuilt context. */
+int pkd_view(PkdCtx *ctx, PkdView *out);
+
+/* Batched decode: one step for up to 64 independent sequences that share
+ * one pass over the weights (pk_batch.cu). */
+typedef struct PkbCtx PkbCtx;
+
+/* Run state for max_seqs sequences (each a KV cache of the model's
+ * seq_len) on ctx's device and stream. NULL + message on failure. */
+PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap);
+void pkb_destroy(PkbCtx *b);
+
+/* Sequence seq_ids[i] takes tokens[i] at position pos[i], i < n. next[i]
+ * receives the greedy token (-1 when a logit is not finite); logits (n x
+ * vocab floats, host) when not NULL. Arguments are checked by the caller.
+ * Returns 1, or 0 on a device error (message in pkb_error). */
+int pkb_step(PkbCtx *b, const int *tokens, const int *pos, const int *seq_ids, int n, int *next, float *logits);
+const char *pkb_error(const PkbCtx *b);
+
 #ifdef __cplusplus
 }
 #endif

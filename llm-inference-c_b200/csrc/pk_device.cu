@@ -1432,6 +1432,18 @@ extern "C" const char *pkd_error(const PkdCtx *c)
     return c ? c->msg : "";
 }
 
+extern "C" int pkd_view(PkdCtx *c, PkdView *out)
+{
+    if (c == NULL || out == NULL || c->tensors == NULL || c->tp.world > 1 || c->norms == NULL) return 0;
+    out->device = c->device;
+    out->stream = (void *)c->stream;
+    out->arena = c->arena;
+    out->norms = c->norms;
+    out->rope_cs = c->rope_cs;
+    out->model = &c->model;
+    return 1;
+}
+
 extern "C" int pkd_launches_per_step(const PkdCtx *c)
 {
     if (c == NULL) return 0;

@@ -20,22 +20,25 @@
 //       y[b] += (d * (D[2b] + D[2b+1]) - dmin * (D2[2b] + D2[2b+1])) / scale.
 //
 // One CTA per SM, warp-specialised, every hand-off an mbarrier:
-//   warps 0-3  dequantise (thread i = weight row i of the tile = TMEM lane
-//              i) into A, and read the accumulators out;
-//   warp 4     loads the weight super-blocks of the tile (128 rows x 144
+//   warps 0-7  dequantise into A and read the accumulators out: thread t
+//              owns weight row t % 128 of the tile (= TMEM lane t % 128);
+//              warps 0-3 take the low-nibble sub-block of each 64-column
+//              step and vectors 0-31, warps 4-7 the high-nibble sub-block
+//              and vectors 32-63;
+//   warp 8     loads the weight super-blocks of the tile (128 rows x 144
 //              bytes, one 2D TMA tensor copy each, plus the 64 scales of
-//              that x piece) into a 4-deep ring;
-//   warp 5     bulk-copies the staged x of each 64-column step into a ring
-//              as deep as shared memory allows (4 steps at n = 64, 32 at
+//              that x piece) into a 3-deep ring;
+//   warp 9     bulk-copies the staged x of each 64-column step into a ring
+//              as deep as shared memory allows (3 steps at n = 64, 24 at
 //              n <= 8);
-//   warp 6     allocates TMEM and issues the MMAs (one thread), committing
+//   warp 10    allocates TMEM and issues the MMAs (one elected lane), committing
 //              to the barriers that free the A and B slots and publish the
 //              accumulators; two accumulator sets let the readout of one
 //              super-block overlap the MMAs of the next.
 // Work units are (row tile, super-block) pairs, split evenly over the CTAs
 // in row-tile-major order. A tile split over several CTAs leaves one partial
-// sum per CTA; for each 32-row group the last CTA to finish it adds the
-// partials up in CTA order (a fixed order: the result does not depend on
+// sum per CTA; for each block of 32 rows x 32 vectors the last CTA to
+// finish it adds the partials up in CTA order (a fixed order: the result does not depend on
 // timing). Two launches per call: the x staging kernel, then this one.
 //
 // Shared-memory operands are fp16, K-major, without swizzle: core matrices
@@ -56,6 +59,7 @@
 #include <string.h>
 
 #include "../../include/gguf_cuda.h"
+#include "pk_mma.h"
 #include "pk_quant.cuh"
 #include "pk_stream.cuh"
 
@@ -67,10 +71,11 @@ constexpr int NMAX = 128;  // MMA N at most: 2 parts x 64 vectors
 constexpr int VMAX = 64;   // activation vectors per call
 constexpr int QK = 256;    // columns per Q4_K super-block
 constexpr int SBB = 144;   // bytes per Q4_K super-block
-constexpr int W_PRODUCER = 4, B_PRODUCER = 5, ISSUER = 6;
-constexpr int DQ_THREADS = 128;  // warps 0-3
-constexpr int THREADS = 224;
-constexpr int SA = 3, SW = 4, SB_MAX = 32;  // ring depths: A steps, weight super-blocks, x steps (at most)
+constexpr int DQ_WARPS = 8, DQ_THREADS = 256;  // warps 0-7: two per row group of 32
+constexpr int W_PRODUCER = 8, B_PRODUCER = 9, ISSUER = 10;
+constexpr int THREADS = 352;
+constexpr int SA = 6, SW = 3, SB_MAX = 32;  // ring depths: A steps, weight super-blocks, x steps (at most)
+constexpr int SA2 = 3, SINV = 4;            // A2 slots, inverse-scale slots (see the dequantisers)
 constexpr int A_BYTES = TM * 128;           // [8 chunks][128 rows][16 B]
 constexpr int A2_BYTES = TM * 32;           // [2 chunks][128 rows][16 B]
 constexpr int W_TILE = TM * SBB;            // 128 rows x one super-block
@@ -90,15 +95,15 @@ enum {
 };
 // Shared-memory layout (offsets from a 128-byte aligned base)
 constexpr int OFF_BAR = 0;
-constexpr int OFF_INV = 1024;  // 3 x 64 inverse scales (readout)
+constexpr int OFF_INV = 1024;  // SINV x 64 inverse scales (readout)
 constexpr int OFF_A = 2048;
 constexpr int OFF_A2 = OFF_A + SA * A_BYTES;
-constexpr int OFF_W = OFF_A2 + 2 * A2_BYTES;  // 128-byte aligned (TMA tensor destination)
+constexpr int OFF_W = OFF_A2 + SA2 * A2_BYTES;  // 128-byte aligned (TMA tensor destination)
 constexpr int OFF_B = OFF_W + SW * W_BYTES;
 constexpr int B_SLOT_MAX = NMAX * 128 + NMAX * 32;
-static_assert(NBARS * 8 <= OFF_INV, "barriers");
+static_assert(NBARS * 8 <= OFF_INV && OFF_INV + SINV * VMAX * 4 <= OFF_A, "barriers, scales");
 static_assert(OFF_W % 128 == 0 && W_BYTES % 128 == 0, "TMA destinations");
-static_assert(OFF_B + 4 * B_SLOT_MAX + 128 <= 227 * 1024 - 1024, "at least 4 x steps of N = 128");
+static_assert(OFF_B + 3 * B_SLOT_MAX + 128 <= 227 * 1024 - 1024, "at least 3 x steps of N = 128");
 static_assert(OFF_B > 227 * 1024 / 2, "one CTA per SM (it allocates all of TMEM)");
 constexpr int TMEM_COLS = 512;  // 2 accumulator sets x (D: 128 columns, D2: 128 columns)
 
@@ -204,13 +209,40 @@ __device__ __forceinline__ uint32_t nib2(uint32_t w, __half2 sc2, __half2 nsc2)
     return *reinterpret_cast<const uint32_t *>(&r);
 }
 
-// Bounded wait that also gives up once another thread has aborted the CTA;
-// a thread that runs out of time records the timeout and aborts the CTA.
-__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err)
+// mbarrier.try_wait with a suspend-time hint: the thread sleeps until the
+// phase completes (or about a millisecond passes) instead of spinning, so
+// waiting warps take no issue slots from the working ones.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity)
 {
-    if (mbar_try_wait(bar, parity)) return true;
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+        : "memory");
+    return ok != 0;
+}
+
+// One lane of a converged warp (the same lane every time).
+__device__ __forceinline__ bool elect_one()
+{
+    uint32_t pred;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "elect.sync _|P, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, P;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
+}
+
+// The slow path of wait_or_abort, out of line: the kernel's code stays
+// small enough for the instruction caches that its eleven warps share.
+__device__ __noinline__ bool wait_or_abort_slow(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err)
+{
     const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_sleep(bar, parity)) {
         if (*abort_flag) return false;
         if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
             *abort_flag = 1;
@@ -219,6 +251,13 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, vo
         }
     }
     return true;
+}
+
+// Bounded wait that also gives up once another thread has aborted the CTA;
+// a thread that runs out of time records the timeout and aborts the CTA.
+__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err)
+{
+    return mbar_try_wait_sleep(bar, parity) || wait_or_abort_slow(bar, parity, abort_flag, err);
 }
 
 // wait_or_abort with one answer for the whole warp (every lane calls it), so
@@ -236,14 +275,55 @@ struct MmArgs {
     const float *xinv;      // [nsb][64] inverse scales of the staged pieces
     int n, N;               // vectors, MMA N
     int sb, b_slot;         // x ring depth and slot bytes
-    long long U;            // work units (row tiles x super-blocks)
+    int U;                  // work units (row tiles x super-blocks)
     int G;                  // CTAs
     int maxp;               // partial slots per tile
     float *y;               // [n][rows]
     float *ypart;           // [tiles][maxp][n][128]
-    unsigned int *arrived;  // [tiles][4 warps] CTAs done with those rows (reset by the last)
+    unsigned int *arrived;  // [tiles][8 warps] CTAs done with that block (reset by the last)
     int *err;
 };
+
+// Store the sums of one tile piece: acc[b] = vector b0 + b of tile row
+// row. A tile owned by one CTA goes straight to y. Otherwise the piece goes
+// to the CTA's partial slot; per warp (32 rows x 32 vectors) a counter of
+// the CTAs done with that block names the last one, which adds the pieces
+// in CTA order (no barrier between warps: an aborted warp blocks none).
+// Out of line and rare (once per tile piece): it keeps the kernel small.
+__device__ __noinline__ void flush_piece(const float *acc, float *y, float *ypart, unsigned int *arrived, int rows,
+                                         int n, int nsb, int U, int G, int maxp, int T, int c, int row, int b0)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = T * TM + row;
+    const int c0 = unit_owner((long long)T * nsb, U, G), c1 = unit_owner((long long)T * nsb + nsb - 1, U, G);
+    const int nb = min(32, n - b0);
+    if (c0 == c1) {
+        if (r < rows)
+            for (int b = 0; b < nb; b++) y[(size_t)(b0 + b) * rows + r] = acc[b];
+        return;
+    }
+    float *yp = ypart + (size_t)T * maxp * n * TM;
+    for (int b = 0; b < nb; b++) yp[((size_t)(c - c0) * n + b0 + b) * TM + row] = acc[b];
+    __threadfence();
+    __syncwarp();
+    unsigned int last = 0;
+    if (lane == 0) {
+        const unsigned int seen = atomicAdd(arrived + (size_t)T * DQ_WARPS + warp, 1u);
+        last = seen == (unsigned int)(c1 - c0);
+        if (last) arrived[(size_t)T * DQ_WARPS + warp] = 0u;  // ready for the next call
+    }
+    last = __shfl_sync(0xFFFFFFFFu, last, 0);
+    if (last) {
+        __threadfence();
+        if (r < rows) {
+            for (int b = b0; b < b0 + nb; b++) {
+                float sum = 0.0f;
+                for (int k = 0; k <= c1 - c0; k++) sum += __ldcg(yp + ((size_t)k * n + b) * TM + row);
+                y[(size_t)b * rows + r] = sum;
+            }
+        }
+    }
+}
 
 // wmap: the weights as a 2D tensor of bytes [rows][row bytes], box
 // [128 rows][144 bytes] (one super-block of one row tile).
@@ -257,8 +337,10 @@ __global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constan
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + OFF_BAR);
     float *inv_s = reinterpret_cast<float *>(sm + OFF_INV);
     const int c = blockIdx.x;
-    const long long u0 = (long long)c * a.U / a.G, u1 = (long long)(c + 1) * a.U / a.G;
-    const int nu = (int)(u1 - u0);
+    // this CTA's units [u0, u0 + nu): tile T0, super-block s0 first
+    const int u0 = (int)((long long)c * a.U / a.G);
+    const int nu = (int)((long long)(c + 1) * a.U / a.G) - u0;
+    const int T0 = u0 / a.nsb, s0 = u0 - T0 * a.nsb;
     const int N = a.N, SB = a.sb;
 
     if (warp == ISSUER) {
@@ -288,8 +370,8 @@ __global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constan
         fence_mbar_init();
         abort_flag = 0;
     }
-    // A2 column chunk 1 (k 8..15) stays zero in both slots
-    for (int i = tid; i < 2 * TM; i += THREADS) {
+    // A2 column chunk 1 (k 8..15) stays zero in every slot
+    for (int i = tid; i < SA2 * TM; i += THREADS) {
         const int slot = i / TM, row = i % TM;
         *reinterpret_cast<uint4 *>(sm + OFF_A2 + slot * A2_BYTES + TM * 16 + row * 16) = make_uint4(0, 0, 0, 0);
     }
@@ -301,108 +383,146 @@ __global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constan
     volatile int *abrt = &abort_flag;
 
     if (warp == W_PRODUCER) {
-        if (lane == 0) {
-            // weight super-blocks: one tensor copy of 128 rows x 144 bytes each
-            // (rows past the end of the matrix arrive as zeros), then the 64
-            // inverse scales of the matching x piece
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
-            int issued = 0;
-            for (int j = 0; j < nu; j++) {
-                const int slot = j % SW;
-                if (j >= SW && !wait_or_abort(bars + EMPTY_W + slot, ((j / SW) - 1) & 1, abrt, a.err)) break;
-                const long long u = u0 + j;
-                const int T = (int)(u / a.nsb), s = (int)(u % a.nsb);
+        // weight super-blocks: one tensor copy of 128 rows x 144 bytes each
+        // (rows past the end of the matrix arrive as zeros), then the 64
+        // inverse scales of the matching x piece
+        const bool leader = elect_one();
+        if (leader) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+        int issued = 0, T = T0, s = s0;
+        for (int j = 0; j < nu; j++) {
+            const int slot = j % SW;
+            if (j >= SW && !warp_wait(bars + EMPTY_W + slot, ((j / SW) - 1) & 1, abrt, a.err)) break;
+            if (leader) {
                 uint8_t *dst = sm + OFF_W + slot * W_BYTES;
                 mbar_expect_tx(bars + FULL_W + slot, (uint32_t)W_BYTES);
                 tma_load_2d(dst, &wmap, s * SBB, T * TM, bars + FULL_W + slot);
                 bulk_g2s(dst + W_TILE, a.xinv + (size_t)s * VMAX, VMAX * 4, bars + FULL_W + slot);
-                issued = j + 1;
             }
-            // no copy may still be in flight when the CTA exits
-            for (int j = max(0, issued - SW); j < issued; j++)
-                mbar_wait_bounded(bars + FULL_W + j % SW, (j / SW) & 1);
+            __syncwarp();
+            issued = j + 1;
+            if (++s == a.nsb) {
+                s = 0;
+                T++;
+            }
         }
+        // no copy may still be in flight when the CTA exits
+        for (int j = max(0, issued - SW); j < issued; j++) mbar_wait_bounded(bars + FULL_W + j % SW, (j / SW) & 1);
     } else if (warp == B_PRODUCER) {
-        if (lane == 0) {
-            int issued = 0;
-            const uint32_t step_bytes = (uint32_t)N * 128, sum_bytes = (uint32_t)N * 32;
-            for (int i = 0; i < 4 * nu; i++) {
-                const int slot = i % SB;
-                if (i >= SB && !wait_or_abort(bars + EMPTY_B + slot, ((i / SB) - 1) & 1, abrt, a.err)) break;
-                const int t = i & 3;
-                const int s = (int)((u0 + i / 4) % a.nsb);
+        const bool leader = elect_one();
+        const uint32_t step_bytes = (uint32_t)N * 128, sum_bytes = (uint32_t)N * 32;
+        int issued = 0, slot = 0, s = s0;
+        uint32_t phase = 0;  // parity of the slot's next EMPTY_B completion
+        for (int i = 0; i < 4 * nu; i++) {
+            if (i >= SB && !warp_wait(bars + EMPTY_B + slot, phase, abrt, a.err)) break;
+            const int t = i & 3;
+            if (leader) {
                 uint8_t *dst = sm + OFF_B + slot * a.b_slot;
                 mbar_expect_tx(bars + FULL_B + slot, step_bytes + (t == 3 ? sum_bytes : 0u));
                 bulk_g2s(dst, a.xs + ((size_t)s * 4 + t) * step_bytes, step_bytes, bars + FULL_B + slot);
                 if (t == 3) bulk_g2s(dst + step_bytes, a.x2s + (size_t)s * sum_bytes, sum_bytes, bars + FULL_B + slot);
-                issued = i + 1;
             }
-            for (int i = max(0, issued - SB); i < issued; i++) mbar_wait_bounded(bars + FULL_B + i % SB, (i / SB) & 1);
+            __syncwarp();
+            issued = i + 1;
+            if (t == 3 && ++s == a.nsb) s = 0;
+            if (++slot == SB) {
+                slot = 0;
+                if (i >= SB) phase ^= 1u;
+            }
         }
+        for (int i = max(0, issued - SB); i < issued; i++) mbar_wait_bounded(bars + FULL_B + i % SB, (i / SB) & 1);
     } else if (warp == ISSUER) {
-        if (lane == 0) {
-            const uint32_t idesc = idesc_f16(TM, N);
-            bool ok = true;
-            int issued = 0;
-            for (int j = 0; j < nu && ok; j++) {
-                const int acc = j & 1;
-                const uint32_t d_col = tmem + (uint32_t)(acc * 256);
-                if (j >= 2 && !wait_or_abort(bars + ACC_EMPTY + acc, ((j / 2) - 1) & 1, abrt, a.err)) break;
+        // the whole warp follows the loop; one elected lane issues
+        const bool leader = elect_one();
+        const uint32_t idesc = idesc_f16(TM, N);
+        // descriptors of slot 0 / chunk pair 0; later ones add (offset >> 4)
+        const uint64_t a_desc0 = sdesc(sbase + OFF_A, TM * 16, 128);
+        const uint64_t b_desc0 = sdesc(sbase + OFF_B, N * 16, 128);
+        const uint64_t a2_desc0 = sdesc(sbase + OFF_A2, TM * 16, 128);
+        const uint32_t b_kstep = (uint32_t)(2 * N * 16) >> 4, b_slot16 = (uint32_t)a.b_slot >> 4;
+        bool ok = true;
+        int issued = 0, as = 0, bs = 0;
+        uint32_t a_ph = 0, b_ph = 0;  // parity of the slots' next FULL completion
+        for (int j = 0; j < nu && ok; j++) {
+            const int acc = j & 1;
+            const uint32_t d_col = tmem + (uint32_t)(acc * 256);
+            if (j >= 2 && !warp_wait(bars + ACC_EMPTY + acc, ((j / 2) - 1) & 1, abrt, a.err)) break;
+            tc_fence_after();
+#pragma unroll 1
+            for (int t = 0; t < 4; t++) {
+                if (!warp_wait(bars + FULL_A + as, a_ph, abrt, a.err) ||
+                    !warp_wait(bars + FULL_B + bs, b_ph, abrt, a.err)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
-                for (int t = 0; t < 4; t++) {
-                    const int i = 4 * j + t, as = i % SA, bs = i % SB;
-                    if (!wait_or_abort(bars + FULL_A + as, (i / SA) & 1, abrt, a.err) ||
-                        !wait_or_abort(bars + FULL_B + bs, (i / SB) & 1, abrt, a.err)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t a0 = sbase + OFF_A + as * A_BYTES, b0 = sbase + OFF_B + bs * a.b_slot;
+                if (leader) {
+                    const uint64_t ad = a_desc0 + (uint64_t)(as * (A_BYTES >> 4));
+                    const uint64_t bd = b_desc0 + (uint64_t)(bs * b_slot16);
 #pragma unroll
                     for (int kk = 0; kk < 4; kk++) {
-                        mma_f16(d_col, sdesc(a0 + kk * 2 * (TM * 16), TM * 16, 128),
-                                sdesc(b0 + kk * 2 * (N * 16), N * 16, 128), idesc, (t | kk) ? 1u : 0u);
+                        mma_f16(d_col, ad + (uint64_t)(kk * ((2 * TM * 16) >> 4)), bd + (uint64_t)(kk * b_kstep), idesc,
+                                (t | kk) ? 1u : 0u);
                     }
                     if (t == 3) {
-                        mma_f16(d_col + 128, sdesc(sbase + OFF_A2 + (j & 1) * A2_BYTES, TM * 16, 128),
-                                sdesc(b0 + N * 128, N * 16, 128), idesc, 0u);
+                        mma_f16(d_col + 128, a2_desc0 + (uint64_t)((j % SA2) * (A2_BYTES >> 4)),
+                                bd + (uint64_t)(4 * b_kstep), idesc, 0u);
                     }
-                    issued++;
                     mma_commit(bars + EMPTY_A + as);
                     mma_commit(bars + EMPTY_B + bs);
                 }
-                if (!ok) break;
-                mma_commit(bars + ACC_FULL + acc);
+                __syncwarp();
+                issued++;
+                if (++as == SA) {
+                    as = 0;
+                    a_ph ^= 1u;
+                }
+                if (++bs == SB) {
+                    bs = 0;
+                    b_ph ^= 1u;
+                }
             }
-            // MMAs still running after an abort finish before TMEM is freed
-            if (issued > 0) {
-                mma_commit(bars + DRAIN);
-                mbar_wait_bounded(bars + DRAIN, 0);
-            }
+            if (!ok) break;
+            if (leader) mma_commit(bars + ACC_FULL + acc);
+            __syncwarp();
+        }
+        // MMAs still running after an abort finish before TMEM is freed
+        if (issued > 0) {
+            if (leader) mma_commit(bars + DRAIN);
+            __syncwarp();
+            mbar_wait_bounded(bars + DRAIN, 0);
         }
     } else {
-        // warps 0-3: dequantise and read out; thread tid owns tile row tid
-        float acc[VMAX];
+        // warps 0-7: dequantise and read out. Thread tid owns tile row
+        // row = tid % 128 (TMEM lane row); half = tid / 128 picks the
+        // sub-block of each step (low or high nibbles) and the vectors
+        // 32 half .. 32 half + 31 of the readout.
+        const int row = tid & (TM - 1), half = tid >> 7;
+        const int b0 = 32 * half;
+        float acc[32];
 #pragma unroll
-        for (int b = 0; b < VMAX; b++) acc[b] = 0.0f;
+        for (int b = 0; b < 32; b++) acc[b] = 0.0f;
         float d_prev = 0.0f, dmin_prev = 0.0f;
-        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        int rT = T0, rs = s0;  // tile and super-block of the next readout
+        const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         bool ok = true;
         // Read out super-block jp and, at the end of a tile's piece, store it.
-        // inv_s slot jp % 3 holds its inverse scales: written at the start of
-        // jp, rewritten at the start of jp + 3, which no thread reaches before
-        // every thread has passed this readout (the A ring of depth 3 keeps
-        // the dequantisers within one super-block of each other).
+        // Slot lifetimes, from the A ring (depth SA = 6): a thread starts step
+        // i only after the MMAs of step i - 6 completed, which needed every
+        // thread's A of that step. So the thread that rewrites inv_s slot
+        // jp % 4 (start of jp + 4: after step 4 jp + 15, i.e. after every
+        // thread wrote step 4 jp + 9, which follows readout jp) cannot run
+        // ahead of this readout; and A2 slot j % 3, written at step 4j after
+        // the MMAs of step 4j - 6, was last read by the MMA of step 4j - 9.
         auto readout = [&](int jp, float d, float dmin) -> bool {
             const int accs = jp & 1;
             if (!warp_wait(bars + ACC_FULL + accs, (jp / 2) & 1, abrt, a.err)) return false;
             tc_fence_after();
             __syncwarp();
-            const uint32_t col = lane_base + (uint32_t)(accs * 256);
-            const float *iv = inv_s + (jp % 3) * VMAX;
+            const uint32_t col = lane_base + (uint32_t)(accs * 256 + 2 * b0);
+            const float *iv = inv_s + (jp % SINV) * VMAX + b0;
 #pragma unroll
-            for (int q = 0; q < NMAX / 32; q++) {
-                if (32 * q < N) {
+            for (int q = 0; q < 2; q++) {
+                if (2 * b0 + 32 * q < N) {
                     float v[32], v2[32];
                     tmem_ld32(col + 32 * q, v);
                     tmem_ld32(col + 128 + 32 * q, v2);
@@ -416,68 +536,44 @@ __global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constan
             }
             tc_fence_before();
             mbar_arrive(bars + ACC_EMPTY + accs);
-            const long long u = u0 + jp;
-            const int T = (int)(u / a.nsb);
-            if (jp == nu - 1 || (u + 1) % a.nsb == 0) {
-                const long long t0u = (long long)T * a.nsb;
-                const int r = T * TM + tid;
-                const int c0 = unit_owner(t0u, a.U, a.G), c1 = unit_owner(t0u + a.nsb - 1, a.U, a.G);
-                if (c0 == c1) {
-                    if (r < a.rows) {
+            const bool piece_end = jp == nu - 1 || rs == a.nsb - 1;
+            if (piece_end && b0 < a.n) {
+                float out[32];
 #pragma unroll
-                        for (int b = 0; b < VMAX; b++)
-                            if (b < a.n) a.y[(size_t)b * a.rows + r] = acc[b];
-                    }
-                } else {
-                    // this CTA's piece of the tile. Per warp (32 rows) a
-                    // counter of the CTAs done with those rows: the warp that
-                    // completes it adds the pieces in CTA order (no barrier
-                    // between the warps, so an aborted warp blocks no other)
-                    float *yp = a.ypart + (size_t)T * a.maxp * a.n * TM;
+                for (int b = 0; b < 32; b++) out[b] = acc[b];
+                flush_piece(out, a.y, a.ypart, a.arrived, a.rows, a.n, a.nsb, a.U, a.G, a.maxp, rT, c, row, b0);
+            }
+            if (++rs == a.nsb) {
+                rs = 0;
+                rT++;
+            }
+            if (piece_end) {
 #pragma unroll
-                    for (int b = 0; b < VMAX; b++)
-                        if (b < a.n) yp[((size_t)(c - c0) * a.n + b) * TM + tid] = acc[b];
-                    __threadfence();
-                    __syncwarp();
-                    unsigned int last = 0;
-                    if (lane == 0) {
-                        const unsigned int seen = atomicAdd(a.arrived + (size_t)T * 4 + warp, 1u);
-                        last = seen == (unsigned int)(c1 - c0);
-                        if (last) a.arrived[(size_t)T * 4 + warp] = 0u;  // ready for the next call
-                    }
-                    last = __shfl_sync(0xFFFFFFFFu, last, 0);
-                    if (last) {
-                        __threadfence();
-                        if (r < a.rows) {
-                            for (int b = 0; b < a.n; b++) {
-                                float sum = 0.0f;
-                                for (int k = 0; k <= c1 - c0; k++) sum += __ldcg(yp + ((size_t)k * a.n + b) * TM + tid);
-                                a.y[(size_t)b * a.rows + r] = sum;
-                            }
-                        }
-                    }
-                }
-#pragma unroll
-                for (int b = 0; b < VMAX; b++) acc[b] = 0.0f;
+                for (int b = 0; b < 32; b++) acc[b] = 0.0f;
             }
             return true;
         };
-        for (int j = 0; j < nu && ok; j++) {
+        int as = 0;
+        uint32_t ea_ph = 0;  // parity of the A slot's next EMPTY completion
+        // iteration j dequantises super-block j (j < nu), then reads out j - 1
+        for (int j = 0; j <= nu && ok; j++) {
+          if (j < nu) {
             const int ws = j % SW;
             if (!warp_wait(bars + FULL_W + ws, (j / SW) & 1, abrt, a.err)) {
                 ok = false;
                 break;
             }
             const uint8_t *wslot = sm + OFF_W + ws * W_BYTES;
-            const uint8_t *wrow = wslot + tid * SBB;
+            const uint8_t *wrow = wslot + row * SBB;
             const uint4 hdr = *reinterpret_cast<const uint4 *>(wrow);
-            if (tid < VMAX) inv_s[(j % 3) * VMAX + tid] = reinterpret_cast<const float *>(wslot + W_TILE)[tid];
+            if (tid < VMAX) inv_s[(j % SINV) * VMAX + tid] = reinterpret_cast<const float *>(wslot + W_TILE)[tid];
             uint32_t scp[4], mnp[4];  // (scale, min) of sub-blocks 2t (low byte) and 2t + 1
 #pragma unroll
             for (int t = 0; t < 4; t++) scale_min_pair(hdr.y, hdr.z, hdr.w, t, scp[t], mnp[t]);
+#pragma unroll 1
             for (int t = 0; t < 4; t++) {
-                const int i = 4 * j + t, as = i % SA;
-                if (i >= SA && !warp_wait(bars + EMPTY_A + as, ((i / SA) - 1) & 1, abrt, a.err)) {
+                const int i = 4 * j + t;
+                if (i >= SA && !warp_wait(bars + EMPTY_A + as, ea_ph, abrt, a.err)) {
                     ok = false;
                     break;
                 }
@@ -485,25 +581,21 @@ __global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constan
                 const uint4 qb = *reinterpret_cast<const uint4 *>(wrow + 32 + 32 * t);
                 if (t == 3) mbar_arrive(bars + EMPTY_W + ws);
                 const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-                const __half sl = __ushort2half_rn((unsigned short)(scp[t] & 255u));
-                const __half sh = __ushort2half_rn((unsigned short)(scp[t] >> 8));
-                const __half2 sc_lo = __halves2half2(sl, sl), sc_hi = __halves2half2(sh, sh);
-                const __half2 m1024 = __float2half2_rn(-1024.0f);
-                const __half2 nsc_lo = __hmul2(sc_lo, m1024), nsc_hi = __hmul2(sc_hi, m1024);
-                uint8_t *arow = sm + OFF_A + as * A_BYTES + tid * 16;
+                // this half's sub-block: 2t (low nibbles, low scale byte) or 2t + 1
+                const __half sc = __ushort2half_rn((unsigned short)((scp[t] >> (8 * half)) & 255u));
+                const __half2 sc2 = __halves2half2(sc, sc);
+                const __half2 nsc2 = __hmul2(sc2, __float2half2_rn(-1024.0f));
+                const int sh = 4 * half;
+                uint8_t *arow = sm + OFF_A + as * A_BYTES + row * 16 + half * 4 * (TM * 16);
 #pragma unroll
                 for (int cc = 0; cc < 4; cc++) {
-                    // columns 8cc .. 8cc+7 of sub-block 2t (low nibbles of bytes 8cc ..) and of
-                    // sub-block 2t + 1 (their high nibbles), chunks cc and 4 + cc
-                    const uint32_t w0 = q[2 * cc], w1 = q[2 * cc + 1];
+                    // columns 8cc .. 8cc+7 of the sub-block: nibbles of bytes 8cc .. 8cc+7
+                    const uint32_t w0 = q[2 * cc] >> sh, w1 = q[2 * cc + 1] >> sh;
                     *reinterpret_cast<uint4 *>(arow + cc * (TM * 16)) =
-                        make_uint4(nib2(w0, sc_lo, nsc_lo), nib2(w0 >> 8, sc_lo, nsc_lo), nib2(w1, sc_lo, nsc_lo),
-                                   nib2(w1 >> 8, sc_lo, nsc_lo));
-                    *reinterpret_cast<uint4 *>(arow + (4 + cc) * (TM * 16)) =
-                        make_uint4(nib2(w0 >> 4, sc_hi, nsc_hi), nib2(w0 >> 12, sc_hi, nsc_hi),
-                                   nib2(w1 >> 4, sc_hi, nsc_hi), nib2(w1 >> 12, sc_hi, nsc_hi));
+                        make_uint4(nib2(w0, sc2, nsc2), nib2(w0 >> 8, sc2, nsc2), nib2(w1, sc2, nsc2),
+                                   nib2(w1 >> 8, sc2, nsc2));
                 }
-                if (t == 0) {
+                if (t == 0 && half == 0) {
                     // A2 row: the 8 mins of this super-block (chunk 0, natural order)
                     uint32_t m2[4];
 #pragma unroll
@@ -512,22 +604,29 @@ __global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constan
                                                          __ushort2half_rn((unsigned short)(mnp[p] >> 8)));
                         m2[p] = *reinterpret_cast<const uint32_t *>(&h);
                     }
-                    *reinterpret_cast<uint4 *>(sm + OFF_A2 + (j & 1) * A2_BYTES + tid * 16) =
+                    *reinterpret_cast<uint4 *>(sm + OFF_A2 + (j % SA2) * A2_BYTES + row * 16) =
                         make_uint4(m2[0], m2[1], m2[2], m2[3]);
                 }
                 // the generic-proxy writes above, seen by the tensor core's async proxy
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 mbar_arrive(bars + FULL_A + as);
+                if (++as == SA) {
+                    as = 0;
+                    if (i >= SA) ea_ph ^= 1u;
+                }
             }
             if (!ok) break;
+            const float d_cur = hf(hdr.x & 0xFFFFu), dmin_cur = hf(hdr.x >> 16);
             if (j > 0 && !readout(j - 1, d_prev, dmin_prev)) {
                 ok = false;
                 break;
             }
-            d_prev = hf(hdr.x & 0xFFFFu);
-            dmin_prev = hf(hdr.x >> 16);
+            d_prev = d_cur;
+            dmin_prev = dmin_cur;
+          } else if (!readout(j - 1, d_prev, dmin_prev)) {
+            ok = false;
+          }
         }
-        if (ok && nu > 0) readout(nu - 1, d_prev, dmin_prev);
     }
     tc_fence_before();
     __syncthreads();
@@ -646,21 +745,8 @@ MmScratch *mm_scratch(int dev, size_t xs_b, size_t x2s_b, size_t xinv_b, size_t 
         if (cudaMalloc(&s.err, sizeof(int)) != cudaSuccess) return nullptr;
         if (cudaMemset(s.err, 0, sizeof(int)) != cudaSuccess) return nullptr;
     }
-    if (s.smem_max == 0) {
-        int optin = 0;
-        cudaFuncAttributes fa;
-        if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
-            cudaFuncGetAttributes(&fa, mm::q4k_mm_kernel) != cudaSuccess)
-            return nullptr;
-        const int avail = optin - (int)fa.sharedSizeBytes;
-        if (avail < mm::OFF_B + 4 * mm::B_SLOT_MAX + 128) return nullptr;
-        if (cudaFuncSetAttribute(mm::q4k_mm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, avail) !=
-            cudaSuccess) {
-            cudaGetLastError();
-            return nullptr;
-        }
-        s.smem_max = avail;
-    }
+    if (s.smem_max == 0) s.smem_max = pk_mm_smem_max(dev);
+    if (s.smem_max == 0) return nullptr;
     return &s;
 }
 
@@ -683,33 +769,65 @@ extern "C" void gguf_cuda_matmul_plan(int rows, int nsb, int sms, int *ctas, int
     *maxp = mp;
 }
 
-extern "C" int gguf_cuda_matmul(const GGUFWeight *w, const float *x, int n, float *y, void *stream)
+int pk_mm_shape_ok(uint32_t type, uint64_t rows, uint64_t cols, uint64_t row_bytes, const void *data)
 {
-    if (w == nullptr || w->data == nullptr || x == nullptr || y == nullptr || n < 1 || n > mm::VMAX) return 0;
-    if (w->type != T_Q4_K || w->cols == 0 || w->cols % mm::QK || w->rows == 0) return 0;
-    if (w->rows > 0x7FFFFF00ull || w->cols > 0x7FFFFF00ull) return 0;
-    if (w->row_bytes != w->cols / mm::QK * mm::SBB || ((uintptr_t)w->data & 15) != 0) return 0;
-    const int rows = (int)w->rows, K = (int)w->cols, nsb = K / mm::QK;
+    if (type != T_Q4_K || cols == 0 || cols % mm::QK || rows == 0) return 0;
+    if (rows > 0x7FFFFF00ull || cols > 0x7FFFFF00ull) return 0;
+    if ((rows + 127) / 128 * (cols / mm::QK) > 0x7FFFFFFFull / 256) return 0;  // units and their products fit int
+    return row_bytes == cols / mm::QK * mm::SBB && ((uintptr_t)data & 15) == 0;
+}
+
+void pk_mm_need(int rows, int cols, int n, int sms, PkMmNeed *need)
+{
+    const int nsb = cols / mm::QK, N = (2 * n + 15) / 16 * 16, tiles = (rows + mm::TM - 1) / mm::TM;
+    int G = 0, maxp = 0;
+    gguf_cuda_matmul_plan(rows, nsb, sms, &G, &maxp);
+    need->xs = (size_t)nsb * 4 * N * 128;
+    need->x2s = (size_t)nsb * N * 32;
+    need->xinv = (size_t)nsb * mm::VMAX * 4;
+    need->ypart = (size_t)tiles * maxp * n * mm::TM * sizeof(float);
+    need->arrived = (size_t)tiles * mm::DQ_WARPS * sizeof(unsigned);
+}
+
+int pk_mm_smem_max(int dev)
+{
+    static int per[64] = {0};
+    if (dev < 0 || dev >= 64) return 0;
+    if (per[dev] == 0) {
+        int optin = 0;
+        cudaFuncAttributes fa;
+        if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+            cudaFuncGetAttributes(&fa, mm::q4k_mm_kernel) != cudaSuccess)
+            return 0;
+        const int avail = optin - (int)fa.sharedSizeBytes;
+        if (avail < mm::OFF_B + 3 * mm::B_SLOT_MAX + 128) return 0;
+        if (cudaFuncSetAttribute(mm::q4k_mm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, avail) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        per[dev] = avail;
+    }
+    return per[dev];
+}
+
+int pk_mm_run(const uint8_t *w, uint64_t row_bytes, int rows, int cols, const float *x, int n, float *y,
+              const PkMmScratch *s, int sms, cudaStream_t st)
+{
+    if (n < 1 || n > mm::VMAX || s == nullptr || s->smem_max <= 0) return 0;
+    const int K = cols, nsb = K / mm::QK;
     const int N = (2 * n + 15) / 16 * 16;
-    cudaStream_t st = (cudaStream_t)stream;
-    int dev = 0, sms = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
-        return 0;
     const int tiles = (rows + mm::TM - 1) / mm::TM;
     int G = 0, maxp = 0;
     gguf_cuda_matmul_plan(rows, nsb, sms, &G, &maxp);
-    MmScratch *s = mm_scratch(dev, (size_t)nsb * 4 * N * 128, (size_t)nsb * N * 32, (size_t)nsb * mm::VMAX * 4,
-                              (size_t)tiles * maxp * n * mm::TM * sizeof(float), (size_t)tiles * 4 * sizeof(unsigned));
-    if (s == nullptr) return 0;
     PFN_cuTensorMapEncodeTiled_v12000 enc = encode_tiled();
     if (enc == nullptr) return 0;
     CUtensorMap wmap;
-    const cuuint64_t gdim[2] = {(cuuint64_t)w->row_bytes, (cuuint64_t)rows};
-    const cuuint64_t gstride[1] = {(cuuint64_t)w->row_bytes};
+    const cuuint64_t gdim[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    const cuuint64_t gstride[1] = {(cuuint64_t)row_bytes};
     const cuuint32_t box[2] = {(cuuint32_t)mm::SBB, (cuuint32_t)mm::TM};
     const cuuint32_t estride[2] = {1, 1};
-    if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(w->data), gdim, gstride, box, estride,
+    if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(w), gdim, gstride, box, estride,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return 0;
@@ -724,7 +842,7 @@ extern "C" int gguf_cuda_matmul(const GGUFWeight *w, const float *x, int n, floa
     a.b_slot = N * 160;
     a.sb = (s->smem_max - mm::OFF_B - 128) / a.b_slot;
     if (a.sb > mm::SB_MAX) a.sb = mm::SB_MAX;
-    a.U = (long long)tiles * nsb;
+    a.U = tiles * nsb;
     a.G = G;
     a.maxp = maxp;
     a.y = y;
@@ -735,6 +853,30 @@ extern "C" int gguf_cuda_matmul(const GGUFWeight *w, const float *x, int n, floa
     mm::mm_stage_kernel<<<dim3(nsb, N / 2), 256, 0, st>>>(x, n, K, N, s->xs, s->x2s, s->xinv);
     mm::q4k_mm_kernel<<<G, mm::THREADS, smem, st>>>(wmap, a);
     return cudaGetLastError() == cudaSuccess;
+}
+
+extern "C" int gguf_cuda_matmul(const GGUFWeight *w, const float *x, int n, float *y, void *stream)
+{
+    if (w == nullptr || w->data == nullptr || x == nullptr || y == nullptr || n < 1 || n > mm::VMAX) return 0;
+    if (!pk_mm_shape_ok(w->type, w->rows, w->cols, w->row_bytes, w->data)) return 0;
+    const int rows = (int)w->rows, K = (int)w->cols;
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+        return 0;
+    PkMmNeed need;
+    pk_mm_need(rows, K, n, sms, &need);
+    MmScratch *s = mm_scratch(dev, need.xs, need.x2s, need.xinv, need.ypart, need.arrived);
+    if (s == nullptr) return 0;
+    PkMmScratch sc;
+    sc.xs = s->xs;
+    sc.x2s = s->x2s;
+    sc.xinv = s->xinv;
+    sc.ypart = s->ypart;
+    sc.arrived = s->arrived;
+    sc.err = s->err;
+    sc.smem_max = s->smem_max;
+    return pk_mm_run((const uint8_t *)w->data, w->row_bytes, rows, K, x, n, y, &sc, sms, (cudaStream_t)stream);
 }
 
 // Error word of gguf_cuda_matmul on the current device (0: no wait has run

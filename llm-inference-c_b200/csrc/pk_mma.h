@@ -1,0 +1,37 @@
+// pk_mma.h - the tcgen05 batched Q4_K matmul (pk_mma.cu) for other device
+// code of this library: the same launch as gguf_cuda_matmul, with scratch
+// owned by the caller (so that the launch can be captured in a CUDA graph).
+#ifndef PK_MMA_H
+#define PK_MMA_H
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+// Device scratch of one launch sequence (sized by pk_mm_need; `arrived`
+// zeroed once; launches on one stream may share it).
+struct PkMmScratch {
+    uint8_t *xs, *x2s;
+    float *xinv, *ypart;
+    unsigned *arrived;
+    int *err;        // error word: a wait that ran out of time sets bit 0
+    int smem_max;    // from pk_mm_smem_max
+};
+
+struct PkMmNeed {
+    size_t xs, x2s, xinv, ypart, arrived;  // bytes
+};
+
+// 1 if gguf_cuda_matmul takes this weight (Q4_K, 16-byte aligned rows).
+int pk_mm_shape_ok(uint32_t type, uint64_t rows, uint64_t cols, uint64_t row_bytes, const void *data);
+// Scratch bytes for rows x cols and n vectors on `sms` SMs.
+void pk_mm_need(int rows, int cols, int n, int sms, PkMmNeed *need);
+// Dynamic shared memory the kernel may use on `dev` (sets the attribute
+// once; 0 when the device cannot run the kernel). Call outside capture.
+int pk_mm_smem_max(int dev);
+// y (n x rows) = x (n x cols) W^T: the staging kernel and the matmul kernel
+// on `st`. Returns 1 when both were enqueued.
+int pk_mm_run(const uint8_t *w, uint64_t row_bytes, int rows, int cols, const float *x, int n, float *y,
+              const PkMmScratch *s, int sms, cudaStream_t st);
+
+#endif

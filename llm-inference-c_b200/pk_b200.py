@@ -28,6 +28,7 @@ EXPORTS = [
     "engine_is_stop_token", "engine_open_device", "engine_forward_greedy", "engine_last_error",
     "engine_weight_bytes", "engine_generate_greedy", "engine_trace", "engine_launches_per_step",
     "engine_tp_plan", "engine_open_tp", "engine_tp_handle", "engine_tp_connect",
+    "engine_batch_open", "engine_forward_batch",
     "gguf_cuda_matvec", "gguf_cuda_dequantize_rows", "gguf_cuda_fp16_table", "gguf_cuda_matvec_noalloc",
     "gguf_cuda_matmul", "gguf_cuda_matmul_plan", "gguf_cuda_matmul_error",
     "tokenizer_free",
@@ -134,6 +135,10 @@ def lib(path=LIB_PATH):
     L.engine_tp_handle.argtypes = [_P, _P]
     L.engine_tp_connect.restype = ctypes.c_int
     L.engine_tp_connect.argtypes = [_P, _P, ctypes.c_char_p, ctypes.c_size_t]
+    L.engine_batch_open.restype = ctypes.c_int
+    L.engine_batch_open.argtypes = [_P, ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t]
+    L.engine_forward_batch.restype = ctypes.c_int
+    L.engine_forward_batch.argtypes = [_P, _P, _P, _P, ctypes.c_int, _P, _P]
     L.gguf_cuda_matvec.restype = ctypes.c_int
     L.gguf_cuda_matvec.argtypes = [ctypes.POINTER(GGUFWeight), _P, _P, _P]
     L.gguf_cuda_dequantize_rows.restype = ctypes.c_int
@@ -203,6 +208,27 @@ class Engine:
 
     def forward_greedy(self, token, pos):
         return lib().engine_forward_greedy(self.h, token, pos)
+
+    def batch_open(self, max_seqs):
+        """engine_batch_open: batched state for max_seqs sequences."""
+        err = ctypes.create_string_buffer(512)
+        if lib().engine_batch_open(self.h, max_seqs, err, 512) != 1:
+            raise RuntimeError("engine_batch_open failed: " + err.value.decode())
+
+    def forward_batch(self, tokens, pos, seq_ids, logits=False):
+        """engine_forward_batch: (greedy tokens, n x vocab logits or None);
+        None when the call returns 0."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        p = np.ascontiguousarray(pos, dtype=np.int32)
+        q = np.ascontiguousarray(seq_ids, dtype=np.int32)
+        n = t.size
+        nxt = np.zeros(max(n, 1), dtype=np.int32)
+        lg = np.zeros((n, self.vocab_size), dtype=np.float32) if logits else None
+        ok = lib().engine_forward_batch(self.h, t.ctypes.data, p.ctypes.data, q.ctypes.data, n, nxt.ctypes.data,
+                                        lg.ctypes.data if logits else None)
+        if ok != 1:
+            return None
+        return nxt[:n], lg
 
     def generate_greedy(self, token, pos, n):
         """n device-side greedy steps: (tokens, device milliseconds)."""
