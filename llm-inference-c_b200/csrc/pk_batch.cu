@@ -8,8 +8,9 @@
 //
 // Work per layer, all on the device:
 //   matmuls      Q4_K weights on the tensor cores (pk_mma.cu); every other
-//                format on CUDA cores by mv_tile_kernel, which decodes each
-//                weight once per 64-vector tile into shared memory;
+//                format on CUDA cores by mv_tile_kernel, which stages the
+//                packed rows in shared memory and decodes each weight once
+//                per 64-vector tile;
 //   elementwise  embedding rows, RMSNorm, RoPE + cache append, attention
 //                (one CTA per head and sequence), residual adds, SwiGLU,
 //                greedy argmax per sequence.
@@ -34,8 +35,9 @@ namespace bt {
 
 constexpr int BMAX = 64;            // sequences per step
 constexpr int TR = 64, TK = 256;    // mv_tile_kernel: rows per CTA, columns per chunk
-constexpr int WS = 68, XS = 66;     // padded row strides of its shared tiles (floats)
-constexpr int MV_SMEM = TK * WS * 4 + TK * XS * 4;
+constexpr int WS = 68;              // padded row stride of the decoded weight tile Ws[k][row] (floats)
+constexpr int XP = TK + 4;          // padded row stride of the x tile Xs[b][k] (floats)
+constexpr int MV_SMEM = TK * WS * 4 + BMAX * XP * 4;
 
 __device__ __forceinline__ float block_sum(float v, float *red)
 {
@@ -61,33 +63,85 @@ __device__ __forceinline__ float block_max(float v, float *red)
     return t;
 }
 
+// Bytes of 256 columns of a row of type T (one K-quant super-block, eight
+// Q4_0 / Q8_0 blocks, 256 F16 / F32 values).
+template <int T>
+__host__ __device__ constexpr int chunk_bytes()
+{
+    return T == T_Q4_K ? 144 : T == T_Q5_K ? 176 : T == T_Q6_K ? 210 : T == T_Q4_0 ? 144 : T == T_Q8_0 ? 272
+         : T == T_F16 ? 512 : 1024;
+}
+
+template <int T>
+__host__ __device__ constexpr int mv_smem()
+{
+    return TR * chunk_bytes<T>() + MV_SMEM;
+}
+
 // y[b][r] = sum_c W[r][c] x[b][c] (b < n <= 64) on CUDA cores. Per CTA 64
-// rows; per chunk of 256 columns the weights are decoded once into shared
-// memory (bit-exact decoders, column-major) next to the chunk of every x_b,
-// then thread (rg, vg) accumulates rows 8rg .. 8rg+7 for vectors 2vg, 2vg+1.
+// rows and a range of 256-column chunks (split-K over blockIdx.y when the
+// row tiles alone are too few for the SMs). Per chunk the packed bytes of
+// the 64 rows are staged in shared memory with independent 2-byte loads,
+// decoded there once (bit-exact decoders, column-major floats), and thread
+// (rg, vg) accumulates rows 8rg .. 8rg+7 for vectors 2vg, 2vg+1 against the
+// chunk of every x_b. One split writes y; several write partial sums that
+// mv_reduce_kernel adds in split order.
 template <int T>
 __global__ void __launch_bounds__(256) mv_tile_kernel(const uint8_t *w, uint64_t rb, int rows, int cols,
-                                                      const float *x, int n, float *y)
+                                                      const float *x, int n, float *y, float *part, int cps)
 {
-    extern __shared__ float smt[];
+    constexpr int CB = chunk_bytes<T>();
+    extern __shared__ __align__(16) float smt[];
     float *Ws = smt, *Xs = smt + TK * WS;
+    uint16_t *Wraw = reinterpret_cast<uint16_t *>(smt + TK * WS + BMAX * XP);
     const int tid = threadIdx.x, rg = tid & 7, vg = tid >> 3;
     const int row0 = blockIdx.x * TR;
+    const int nchunks = (cols + TK - 1) / TK;
+    const int c0 = blockIdx.y * cps, c1 = min(nchunks, c0 + cps);
     const bool active = 2 * vg < n;  // warp-uniform (a warp holds vg 4w .. 4w+3)
     const int npad = (n + 1) & ~1;
     float acc[8][2];
 #pragma unroll
     for (int i = 0; i < 8; i++) acc[i][0] = acc[i][1] = 0.0f;
-    for (int k0 = 0; k0 < cols; k0 += TK) {
-        const int kc = min(TK, cols - k0);
-        for (int r = 0; r < TR; r++) {
-            float v = 0.0f;
-            if (tid < kc && row0 + r < rows) v = decode_col(T, w + (size_t)(row0 + r) * rb, k0 + tid);
-            Ws[tid * WS + r] = v;
+    for (int ch = c0; ch < c1; ch++) {
+        const int k0 = ch * TK, kc = min(TK, cols - k0);
+        const uint64_t boff = (uint64_t)ch * CB;
+        const int have = (int)min((uint64_t)CB, rb - boff) / 2;  // halfwords of this chunk in a row
+        // x chunk of every vector: 16-byte async copies into Xs[b][k]
+        // (cols and kc are multiples of 4; columns past kc are never read)
+        for (int e = tid; e < npad * (TK / 4); e += 256) {
+            const int b = e / (TK / 4), k4 = 4 * (e % (TK / 4));
+            float *dst = Xs + b * XP + k4;
+            if (b < n && k4 < kc) {
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                                 (uint32_t)__cvta_generic_to_shared(dst)),
+                             "l"(x + (size_t)b * cols + k0 + k4)
+                             : "memory");
+            } else {
+                *reinterpret_cast<float4 *>(dst) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
         }
-        for (int e = tid; e < npad * TK; e += 256) {
-            const int b = e / TK, k = e % TK;
-            Xs[k * XS + b] = (b < n && k < kc) ? x[(size_t)b * cols + k0 + k] : 0.0f;
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        // packed rows: batches of independent 2-byte loads, then the stores
+        constexpr int PER = (TR * (CB / 2) + 255) / 256;
+        uint16_t raw[PER];
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            const int e = tid + 256 * j, r = e / (CB / 2), hw = e - r * (CB / 2);
+            raw[j] = (e < TR * (CB / 2) && row0 + r < rows && hw < have)
+                         ? ld_u16(w + (size_t)(row0 + r) * rb + boff + 2 * hw)
+                         : (uint16_t)0;
+        }
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            const int e = tid + 256 * j;
+            if (e < TR * (CB / 2)) Wraw[e] = raw[j];
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();
+        for (int r = 0; r < TR; r++) {
+            const uint8_t *rowp = reinterpret_cast<const uint8_t *>(Wraw + r * (CB / 2));
+            Ws[tid * WS + r] = tid < kc ? decode_col(T, rowp, tid) : 0.0f;
         }
         __syncthreads();
         if (active) {
@@ -95,7 +149,7 @@ __global__ void __launch_bounds__(256) mv_tile_kernel(const uint8_t *w, uint64_t
             for (int k = 0; k < kc; k++) {
                 const float4 w0 = *reinterpret_cast<const float4 *>(Ws + k * WS + 8 * rg);
                 const float4 w1 = *reinterpret_cast<const float4 *>(Ws + k * WS + 8 * rg + 4);
-                const float2 xv = *reinterpret_cast<const float2 *>(Xs + k * XS + 2 * vg);
+                const float2 xv = make_float2(Xs[(2 * vg) * XP + k], Xs[(2 * vg + 1) * XP + k]);
                 const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
@@ -107,13 +161,34 @@ __global__ void __launch_bounds__(256) mv_tile_kernel(const uint8_t *w, uint64_t
         __syncthreads();
     }
     if (!active) return;
+    float *out = gridDim.y == 1 ? y : part + (size_t)blockIdx.y * n * rows;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const int r = row0 + 8 * rg + i;
         if (r >= rows) break;
-        y[(size_t)(2 * vg) * rows + r] = acc[i][0];
-        if (2 * vg + 1 < n) y[(size_t)(2 * vg + 1) * rows + r] = acc[i][1];
+        out[(size_t)(2 * vg) * rows + r] = acc[i][0];
+        if (2 * vg + 1 < n) out[(size_t)(2 * vg + 1) * rows + r] = acc[i][1];
     }
+}
+
+// y = the splits' partial sums, added in split order.
+__global__ void mv_reduce_kernel(const float *part, int splits, int count, float *y)
+{
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) {
+        float s = 0.0f;
+        for (int k = 0; k < splits; k++) s += part[(size_t)k * count + i];
+        y[i] = s;
+    }
+}
+
+// Split-K of mv_tile_kernel for `rows` x `cols`: chunks per split.
+__host__ inline int mv_cps(int rows, int cols, int sms)
+{
+    const int tiles = (rows + TR - 1) / TR, nchunks = (cols + TK - 1) / TK;
+    int splits = (2 * sms + tiles - 1) / tiles;
+    if (splits > nchunks) splits = nchunks;
+    if (splits < 1) splits = 1;
+    return (nchunks + splits - 1) / splits;
 }
 
 // x[b] = embedding row tokens[b] (src/gguf_forward.c: the token's row of
@@ -297,6 +372,7 @@ struct PkbCtx {
     const float *norms, *rope_cs;
     float *kc, *vc;                                           // [max_seqs][L][seq_len][kvd]
     float *x, *xn, *q, *k, *v, *att, *tmp, *g, *u, *logits;  // [64][width]
+    float *part;                                              // split-K partial sums of mv_tile_kernel
     int *io_d, *io_h;  // [tokens 64][pos 64][seq 64][next 64][error word]
     PkMmScratch mm;
     cudaGraph_t graph[bt::BMAX + 1];
@@ -318,11 +394,14 @@ static int bmatmul(PkbCtx *b, const PkdTensor &t, const float *x, int n, float *
     const uint8_t *w = b->arena + t.offset;
     const int rows = (int)t.rows, cols = (int)t.cols;
     if (pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, w)) return pk_mm_run(w, t.row_bytes, rows, cols, x, n, y, &b->mm, b->sms, b->st);
-    const dim3 grid((rows + bt::TR - 1) / bt::TR);
+    const int cps = bt::mv_cps(rows, cols, b->sms), nchunks = (cols + bt::TK - 1) / bt::TK;
+    const int splits = (nchunks + cps - 1) / cps;
+    const dim3 grid((rows + bt::TR - 1) / bt::TR, splits);
     switch (t.type) {
 #define PKB_CASE(T)                                                                                           \
     case T:                                                                                                   \
-        bt::mv_tile_kernel<T><<<grid, 256, bt::MV_SMEM, b->st>>>(w, t.row_bytes, rows, cols, x, n, y);        \
+        bt::mv_tile_kernel<T><<<grid, 256, bt::mv_smem<T>(), b->st>>>(w, t.row_bytes, rows, cols, x, n, y,    \
+                                                                      b->part, cps);                          \
         break;
         PKB_CASE(T_F32)
         PKB_CASE(T_F16)
@@ -334,6 +413,10 @@ static int bmatmul(PkbCtx *b, const PkdTensor &t, const float *x, int n, float *
 #undef PKB_CASE
     default:
         return 0;
+    }
+    if (splits > 1) {
+        const int count = n * rows;
+        bt::mv_reduce_kernel<<<(count + 255) / 256, 256, 0, b->st>>>(b->part, splits, count, y);
     }
     return cudaGetLastError() == cudaSuccess;
 }
@@ -422,6 +505,13 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
         if (nd.ypart > mx.ypart) mx.ypart = nd.ypart;
         if (nd.arrived > mx.arrived) mx.arrived = nd.arrived;
     }
+    size_t part_max = 16;
+    for (int j = 0; j <= 7 * m.n_layers; j++) {
+        const PkdTensor &t = j == 7 * m.n_layers ? m.output : lists[j / m.n_layers][j % m.n_layers];
+        const int cps = bt::mv_cps((int)t.rows, (int)t.cols, b->sms);
+        const int splits = ((int)((t.cols + bt::TK - 1) / bt::TK) + cps - 1) / cps;
+        if (splits > 1 && (size_t)splits * B * t.rows * 4 > part_max) part_max = (size_t)splits * B * t.rows * 4;
+    }
     b->mm.smem_max = pk_mm_smem_max(b->device);
     int ok = b->mm.smem_max > 0 || mx.xs == 0;
     if (!ok) snprintf(b->msg, sizeof(b->msg), "The tensor-core matmul cannot run on this device.");
@@ -437,6 +527,7 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
          !bfail(b, cudaMalloc(&b->g, (size_t)B * m.hidden_dim * 4), "cudaMalloc") &&
          !bfail(b, cudaMalloc(&b->u, (size_t)B * m.hidden_dim * 4), "cudaMalloc") &&
          !bfail(b, cudaMalloc(&b->logits, (size_t)B * m.vocab_size * 4), "cudaMalloc") &&
+         !bfail(b, cudaMalloc(&b->part, part_max), "cudaMalloc") &&
          !bfail(b, cudaMalloc(&b->io_d, (size_t)(5 * B) * 4), "cudaMalloc") &&
          !bfail(b, cudaMallocHost(&b->io_h, (size_t)(5 * B) * 4), "cudaMallocHost") &&
          !bfail(b, cudaMalloc(&b->mm.xs, mx.xs + 16), "cudaMalloc") &&
@@ -451,7 +542,7 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
          !bfail(b, cudaMemsetAsync(b->vc, 0, cache * 4, b->st), "cudaMemset");
 #define PKB_ATTR(T)                                                                                           \
     ok = ok && !bfail(b, cudaFuncSetAttribute(bt::mv_tile_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                              bt::MV_SMEM),                                                   \
+                                              bt::mv_smem<T>()),                                              \
                       "cudaFuncSetAttribute");
     PKB_ATTR(T_F32)
     PKB_ATTR(T_F16)
@@ -527,7 +618,7 @@ extern "C" void pkb_destroy(PkbCtx *b)
         if (b->exec[i]) cudaGraphExecDestroy(b->exec[i]);
         if (b->graph[i]) cudaGraphDestroy(b->graph[i]);
     }
-    void *dev[] = {b->kc, b->vc, b->x, b->xn, b->tmp, b->q, b->att, b->k, b->v, b->g, b->u, b->logits, b->io_d,
+    void *dev[] = {b->kc, b->vc, b->x, b->xn, b->tmp, b->q, b->att, b->k, b->v, b->g, b->u, b->logits, b->part, b->io_d,
                    b->mm.xs, b->mm.x2s, b->mm.xinv, b->mm.ypart, b->mm.arrived, b->mm.err};
     for (void *p : dev)
         if (p) cudaFree(p);

@@ -316,11 +316,19 @@ __device__ __noinline__ void flush_piece(const float *acc, float *y, float *ypar
     if (last) {
         __threadfence();
         if (r < rows) {
-            for (int b = b0; b < b0 + nb; b++) {
-                float sum = 0.0f;
-                for (int k = 0; k <= c1 - c0; k++) sum += __ldcg(yp + ((size_t)k * n + b) * TM + row);
-                y[(size_t)b * rows + r] = sum;
+            // piece by piece, the 32 vectors' loads of a piece in flight together
+            float sum[32];
+#pragma unroll
+            for (int b = 0; b < 32; b++) sum[b] = 0.0f;
+            for (int k = 0; k <= c1 - c0; k++) {
+                const float *pk = yp + ((size_t)k * n + b0) * TM + row;
+#pragma unroll
+                for (int b = 0; b < 32; b++)
+                    if (b < nb) sum[b] += __ldcg(pk + (size_t)b * TM);
             }
+#pragma unroll
+            for (int b = 0; b < 32; b++)
+                if (b < nb) y[(size_t)(b0 + b) * rows + r] = sum[b];
         }
     }
 }
@@ -754,18 +762,24 @@ MmScratch *mm_scratch(int dev, size_t xs_b, size_t x2s_b, size_t xinv_b, size_t 
 
 // The work split of gguf_cuda_matmul for a matrix of `rows` rows and `nsb`
 // super-blocks per row on `sms` SMs: CTAs, and partial slots per row tile.
+// At most one CTA per SM, and no more CTAs than split each row tile in
+// about two pieces: the last CTA of a tile adds the pieces up after all
+// others, so many pieces per tile leave one straggler per tile.
 extern "C" void gguf_cuda_matmul_plan(int rows, int nsb, int sms, int *ctas, int *maxp)
 {
     const int tiles = (rows + mm::TM - 1) / mm::TM;
     const long long U = (long long)tiles * nsb;
-    const int G = (int)(U < sms ? U : sms);
+    long long G = (2 * U + nsb - 1) / nsb;  // about two pieces per tile
+    if (G < tiles) G = tiles;
+    if (G > sms) G = sms;
+    if (G > U) G = U;
     int mp = 1;
     for (int T = 0; T < tiles; T++) {
         const int c0 = mm::unit_owner((long long)T * nsb, U, G);
         const int c1 = mm::unit_owner((long long)T * nsb + nsb - 1, U, G);
         if (c1 - c0 + 1 > mp) mp = c1 - c0 + 1;
     }
-    *ctas = G;
+    *ctas = (int)G;
     *maxp = mp;
 }
 
