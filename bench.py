@@ -233,20 +233,142 @@ def run_matvec_sweep(args):
     return 0
 
 
+def run_matmul_sweep(args):
+    """The batched Q4_K matmul (gguf_cuda_matmul) alone: n activation
+    vectors against one weight matrix, graph-replayed, inputs resident; one
+    JSON line per (shape, n) with the time, the weight-stream GB/s and the
+    tensor FLOP/s (2 * rows * cols * N, N = 2n rounded up to 16: the hi and
+    lo fp16 halves of every vector)."""
+    import torch
+    import pk_b200
+    torch.cuda.set_device(0)
+    hbm, _ = peaks()
+    shapes = [(2048, 2048), (5632, 2048), (2048, 5632), (4096, 4096), (11008, 4096), (32000, 4096)]
+    ns = (1, 8, 16, 32, 64)
+    only = None
+    if args.only:  # e.g. "32000x4096:64"
+        shp, n = args.only.split(":")
+        only = (tuple(int(v) for v in shp.split("x")), int(n))
+    for rows, cols in shapes:
+        if only is not None and (rows, cols) != only[0]:
+            continue
+        wb = pk_synth.random_matrix(pk_b200.Q4_K, rows, cols, seed=rows + cols)
+        nbytes = wb.size
+        copies = max(1, min(8, (512 << 20) // nbytes))  # rotate > 2x L2 of weight copies
+        ws = [torch.from_numpy(wb).cuda() for _ in range(copies)]
+        wts = [pk_b200.make_weight(w.data_ptr(), pk_b200.Q4_K, rows, cols) for w in ws]
+        for n in ns:
+            if only is not None and n != only[1]:
+                continue
+            x = torch.from_numpy(np.stack([pk_synth.gaussian(7 + b, cols) for b in range(n)])).cuda()
+            y = torch.empty(n, rows, device="cuda")
+            st = torch.cuda.Stream()
+            with torch.cuda.stream(st):
+                for i in range(3):
+                    assert pk_b200.matmul(wts[i % copies], x.data_ptr(), n, y.data_ptr(), st.cuda_stream) == 1
+                st.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=st):
+                    for i in range(copies):
+                        pk_b200.matmul(wts[i], x.data_ptr(), n, y.data_ptr(), st.cuda_stream)
+                reps = max(1, max(args.steps, 20) // copies)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                g.replay()
+                st.synchronize()
+                e0.record(st)
+                for i in range(reps):
+                    g.replay()
+                e1.record(st)
+                st.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
+            N = (2 * n + 15) // 16 * 16
+            print(json.dumps({"matmul": "Q4_K", "rows": rows, "cols": cols, "n": n, "bytes": nbytes, "us": us,
+                              "GB/s": nbytes / (us * 1e-6) / 1e9, "frac_of_hbm": nbytes / (us * 1e-6) / 1e9 / hbm,
+                              "tensor_TFLOP/s": 2.0 * rows * cols * N / (us * 1e-6) / 1e12,
+                              "matmul_error": pk_b200.matmul_error()}))
+            del g
+        del ws
+    return 0
+
+
+def run_b64(path, args, cfg):
+    """Batched decode of 64 independent sequences (engine_forward_batch):
+    each sequence first decodes a seeded random context (512 tokens by
+    default, --b64-context) into its KV cache, then W warm-up and K timed
+    greedy steps of all 64 together.
+    Every step carries its token ids to the device and the greedy tokens
+    back (synchronous), so the wall time per step is end to end."""
+    import pk_b200
+    B, W, K, C = 64, args.warmup, args.b64_steps, args.b64_context
+    e = pk_b200.Engine(path, C + W + K + 8, device=0)
+    e.batch_open(B)
+    rng = np.random.default_rng(MODEL_SEED + 64)
+    ctx = rng.integers(0, e.vocab_size, size=(B, C))
+    seq = np.arange(B, dtype=np.int32)
+    t0 = time.perf_counter()
+    nxt = None
+    for p in range(C):
+        nxt, _ = e.forward_batch(ctx[:, p], np.full(B, p), seq)
+    fill_s = time.perf_counter() - t0
+    pos = C
+    for i in range(W):
+        nxt, _ = e.forward_batch(nxt, np.full(B, pos), seq)
+        pos += 1
+    t0 = time.perf_counter()
+    for i in range(K):
+        nxt, _ = e.forward_batch(nxt, np.full(B, pos), seq)
+        pos += 1
+    dt = time.perf_counter() - t0
+    e.close()
+    wbytes = pk_synth.weight_bytes_per_token(WORKLOADS["tinyllama"]["preset"])
+    kvb = kv_bytes_per_step(cfg, list(range(C + W, C + W + K))) * B
+    step_s = dt / K
+    hbm, peak_kind = peaks()
+    achieved = (wbytes + kvb) / step_s / 1e9
+    return {"metric": "decode tok/s (B=64)", "value": B * K / dt, "unit": "tok/s", "steps": K, "warmup": W,
+            "ms_per_step": step_s * 1e3,
+            "config": {"workload": "TinyLlama-1.1B-arch Q4_K_M, 64 independent sequences, greedy decode",
+                       "context_per_sequence": [C + W, C + W + K - 1],
+                       "context_fill": f"{C} seeded random tokens per sequence decoded through "
+                                       f"engine_forward_batch ({fill_s:.1f} s, untimed)"},
+            "path": "engine_forward_batch: Q4_K matrices on the tcgen05 tensor-core matmul, Q6_K on the "
+                    "CUDA-core tile kernel, one CUDA graph per step; token ids in and greedy tokens out every "
+                    "step (h2d 768 B, d2h 260 B), timed on the host around synchronous steps",
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "algorithmic_bytes_per_step": wbytes + kvb, "weight_bytes_per_step": wbytes,
+                         "kv_bytes_per_step": kvb,
+                         "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs" if peak_kind == "measured"
+                         else "fallback 6.65 TB/s"}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="tinyllama", choices=list(WORKLOADS) + ["matvec"])
+    ap.add_argument("--workload", default="tinyllama", choices=list(WORKLOADS) + ["matvec", "matmul", "b64"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", default=None, help="matvec workload: one TYPE:ROWSxCOLS case")
+    ap.add_argument("--b64-steps", type=int, default=32, help="timed steps of the B=64 batched decode (0: skip)")
+    ap.add_argument("--b64-context", type=int, default=512, help="tokens decoded into each sequence's KV cache first")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     if args.workload == "matvec":
         return run_matvec_sweep(args)
+    if args.workload == "matmul":
+        return run_matmul_sweep(args)
+    if args.workload == "b64":
+        import torch
+        import pk_b200
+        torch.cuda.set_device(0)
+        path = ensure_model(WORKLOADS["tinyllama"]["preset"], 0, lambda: None)
+        e = pk_b200.Engine(path, 64, device=0)
+        cfg = e.config
+        e.close()
+        print(json.dumps(run_b64(path, args, cfg)))
+        return 0
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         return run_reference_arm(args, wl)
@@ -334,6 +456,10 @@ def main():
     else:
         kernel = f"phase_kernel x{launches_per_step - 1} (one per phase) + finish_kernel"
 
+    b64 = None
+    if world == 1 and args.b64_steps > 0 and args.workload == "tinyllama":
+        b64 = run_b64(path, args, cfg)
+
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         base = reference_decode(path, wl["prompt"], 64, 2, budget_s=15.0)
@@ -368,6 +494,7 @@ def main():
                          "peak_source": (f"{peak_kind} MEASURED_PEAKS.json hbm_gbs" if peak_kind == "measured"
                                          else "fallback 6.65 TB/s") + (f" x {world} GPUs" if world > 1 else "")},
             "cpu_baseline": base,
+            "b64": b64,
             "clocks": clocks.summary(),
             "gpu_launches": launches_per_step * args.steps,
         }
