@@ -255,31 +255,41 @@ __global__ void rope_cache_kernel(float *q, const float *k, const float *v, cons
 
 // Attention of query head h of sequence b over positions 0 .. pos
 // (grouped-query: KV head h / kv_mul), as in src/gguf_forward.c: scores
-// q . k_t * scale, softmax, weighted sum of v_t. Scores in shared memory.
-__global__ void attention_kernel(const float *q, const float *kc, const float *vc, const int *io, int bmax,
-                                 int layer, int L, int seq_len, int hs, int qd, int kvd, int kv_mul, float scale,
-                                 float *out)
+// q . k_t * scale, softmax, weighted sum of v_t. One thread per position
+// for the scores (16-byte loads of its key row, q from shared memory);
+// for the weighted sum thread (g, d4) adds float4 d4 of the values of the
+// positions t = g mod G, and the G partial sums are added in order.
+// 128 threads; hs a multiple of 4, at most 256.
+__global__ void __launch_bounds__(128) attention_kernel(const float *q, const float *kc, const float *vc,
+                                                        const int *io, int bmax, int layer, int L, int seq_len,
+                                                        int hs, int qd, int kvd, int kv_mul, float scale, float *out)
 {
-    extern __shared__ float sc[];  // seq_len scores, then hs query values
+    extern __shared__ __align__(16) float sc[];  // seq_len scores, then hs query values, then 128 x 4 partials
     __shared__ float red[32];
-    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nw = blockDim.x >> 5;
+    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
     const int P = io[bmax + b] + 1, seq = io[2 * bmax + b];
-    float *qs = sc + seq_len;
+    float *qs = sc + ((seq_len + 3) & ~3);
+    float4 *part = reinterpret_cast<float4 *>(qs + hs);
     for (int d = tid; d < hs; d += blockDim.x) qs[d] = q[(size_t)b * qd + (size_t)h * hs + d];
     __syncthreads();
     const size_t base = ((size_t)seq * L + layer) * seq_len * kvd + (size_t)(h / kv_mul) * hs;
-    for (int t = warp; t < P; t += nw) {
-        const float *kt = kc + base + (size_t)t * kvd;
-        float dot = 0.0f;
-        for (int d = lane; d < hs; d += 32) dot = fmaf(qs[d], kt[d], dot);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xFFFFFFFFu, dot, o);
-        if (lane == 0) sc[t] = dot * scale;
-    }
-    __syncthreads();
+    const int F4 = hs >> 2;
+    const float4 *q4 = reinterpret_cast<const float4 *>(qs);
     float m = -INFINITY;
-    for (int t = tid; t < P; t += blockDim.x) m = fmaxf(m, sc[t]);
+    for (int t = tid; t < P; t += blockDim.x) {
+        const float4 *kt = reinterpret_cast<const float4 *>(kc + base + (size_t)t * kvd);
+        float dot = 0.0f;
+        for (int i = 0; i < F4; i++) {
+            const float4 kv = kt[i], qv = q4[i];
+            dot = fmaf(qv.x, kv.x, dot);
+            dot = fmaf(qv.y, kv.y, dot);
+            dot = fmaf(qv.z, kv.z, dot);
+            dot = fmaf(qv.w, kv.w, dot);
+        }
+        const float v = dot * scale;
+        sc[t] = v;
+        m = fmaxf(m, v);
+    }
     m = block_max(m, red);
     float s = 0.0f;
     for (int t = tid; t < P; t += blockDim.x) {
@@ -291,11 +301,33 @@ __global__ void attention_kernel(const float *q, const float *kc, const float *v
     const float inv = 1.0f / s;
     for (int t = tid; t < P; t += blockDim.x) sc[t] *= inv;
     __syncthreads();
-    for (int d = tid; d < hs; d += blockDim.x) {
-        float o = 0.0f;
-        const float *vt = vc + base + d;
-        for (int t = 0; t < P; t++) o = fmaf(sc[t], vt[(size_t)t * kvd], o);
-        out[(size_t)b * qd + (size_t)h * hs + d] = o;
+    const int G = blockDim.x / F4, g = tid / F4, d4 = tid - g * F4;
+    float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (g < G) {
+        const float4 *vb = reinterpret_cast<const float4 *>(vc + base) + d4;
+        const size_t stride = (size_t)(kvd >> 2);
+#pragma unroll 4
+        for (int t = g; t < P; t += G) {
+            const float4 vv = vb[(size_t)t * stride];
+            const float pt = sc[t];
+            o.x = fmaf(pt, vv.x, o.x);
+            o.y = fmaf(pt, vv.y, o.y);
+            o.z = fmaf(pt, vv.z, o.z);
+            o.w = fmaf(pt, vv.w, o.w);
+        }
+        part[g * F4 + d4] = o;
+    }
+    __syncthreads();
+    if (tid < F4) {
+        float4 r = part[tid];
+        for (int k = 1; k < G; k++) {
+            const float4 pk = part[k * F4 + tid];
+            r.x += pk.x;
+            r.y += pk.y;
+            r.z += pk.z;
+            r.w += pk.w;
+        }
+        reinterpret_cast<float4 *>(out + (size_t)b * qd + (size_t)h * hs)[tid] = r;
     }
 }
 
@@ -431,7 +463,7 @@ static int enqueue_step(PkbCtx *b, int n)
     const int ew = (n * (hid > dim ? hid : dim) + 255) / 256;
     bt::embed_kernel<<<n, 256, 0, st>>>(b->arena + m.embd.offset, m.embd.row_bytes, (int)m.embd.type, b->io_d, dim,
                                         b->x);
-    const size_t att_smem = ((size_t)m.seq_len + hs) * 4;
+    const size_t att_smem = (((size_t)m.seq_len + 3) / 4 * 4 + hs + 128 * 4) * 4;
     for (int l = 0; l < L; l++) {
         bt::rmsnorm_kernel<<<n, 256, 0, st>>>(b->x, b->norms + (size_t)(2 * l) * dim, dim, m.rms_eps, b->xn);
         if (!bmatmul(b, m.wq[l], b->xn, n, b->q) || !bmatmul(b, m.wk[l], b->xn, n, b->k) ||
@@ -471,7 +503,7 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
         return NULL;
     }
     const PkdModel &m = *v.model;
-    if ((m.head_size & 1) || m.rope_dim > m.head_size || (m.rope_dim & 1)) {
+    if ((m.head_size & 3) || m.head_size > 256 || m.rope_dim > m.head_size || (m.rope_dim & 1)) {
         if (err && cap) snprintf(err, cap, "Unsupported model shape for batched decode.");
         return NULL;
     }
@@ -552,7 +584,7 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
     PKB_ATTR(T_Q5_K)
     PKB_ATTR(T_Q6_K)
 #undef PKB_ATTR
-    const size_t att_smem = ((size_t)m.seq_len + hs) * 4;
+    const size_t att_smem = (((size_t)m.seq_len + 3) / 4 * 4 + hs + 128 * 4) * 4;
     if (ok && att_smem > 48 * 1024)
         ok = !bfail(b, cudaFuncSetAttribute(bt::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             (int)att_smem),
