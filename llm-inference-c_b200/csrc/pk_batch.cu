@@ -34,10 +34,19 @@ namespace pk {
 namespace bt {
 
 constexpr int BMAX = 64;            // sequences per step
-constexpr int TR = 64, TK = 256;    // mv_tile_kernel: rows per CTA, columns per chunk
-constexpr int WS = 68;              // padded row stride of the decoded weight tile Ws[k][row] (floats)
-constexpr int XP = TK + 4;          // padded row stride of the x tile Xs[b][k] (floats)
-constexpr int MV_SMEM = TK * WS * 4 + BMAX * XP * 4;
+constexpr int TR = 64, TK = 256;    // mv_tile_kernel: rows per CTA, columns per staged chunk
+constexpr int TH = 128;             // columns per decoded half chunk
+constexpr int WS = 68;              // row stride of the decoded tile Ws[k][row'] (floats)
+constexpr int XP = TH + 4;          // row stride of the x tile Xs[b][k] (floats)
+constexpr int MV_SMEM = TH * WS * 4 + BMAX * XP * 4;
+
+// Position of tile row r inside a row of Ws: rows 32..63 shifted by 4 words
+// so that the eight 8-row groups read by one warp start on eight different
+// 4-bank groups (conflict-free 16-byte loads).
+__host__ __device__ constexpr int wpos(int r)
+{
+    return r + 4 * (r >> 5);
+}
 
 __device__ __forceinline__ float block_sum(float v, float *red)
 {
@@ -81,84 +90,94 @@ __host__ __device__ constexpr int mv_smem()
 // y[b][r] = sum_c W[r][c] x[b][c] (b < n <= 64) on CUDA cores. Per CTA 64
 // rows and a range of 256-column chunks (split-K over blockIdx.y when the
 // row tiles alone are too few for the SMs). Per chunk the packed bytes of
-// the 64 rows are staged in shared memory with independent 2-byte loads,
-// decoded there once (bit-exact decoders, column-major floats), and thread
-// (rg, vg) accumulates rows 8rg .. 8rg+7 for vectors 2vg, 2vg+1 against the
-// chunk of every x_b. One split writes y; several write partial sums that
-// mv_reduce_kernel adds in split order.
+// the 64 rows are staged in shared memory with batched 2-byte loads; then,
+// per half of 128 columns, the x columns of every vector arrive by 16-byte
+// async copies, each weight is decoded once from shared memory (bit-exact
+// decoders, column-major floats), and thread (rg, vg) accumulates rows
+// 8rg .. 8rg+7 for vectors 2vg, 2vg+1. One split writes y; several write
+// partial sums that mv_reduce_kernel adds in split order. Two CTAs per SM
+// (about 82 KB of shared memory for the K-quants).
 template <int T>
-__global__ void __launch_bounds__(256) mv_tile_kernel(const uint8_t *w, uint64_t rb, int rows, int cols,
-                                                      const float *x, int n, float *y, float *part, int cps)
+__global__ void __launch_bounds__(256, 2) mv_tile_kernel(const uint8_t *w, uint64_t rb, int rows, int cols,
+                                                         const float *x, int n, float *y, float *part, int cps)
 {
     constexpr int CB = chunk_bytes<T>();
+    constexpr int HW = TR * (CB / 2);       // halfwords of a staged chunk
+    constexpr int PER = (HW + 255) / 256;   // per thread
+    constexpr int BATCH = PER < 8 ? PER : 8;
     extern __shared__ __align__(16) float smt[];
-    float *Ws = smt, *Xs = smt + TK * WS;
-    uint16_t *Wraw = reinterpret_cast<uint16_t *>(smt + TK * WS + BMAX * XP);
+    float *Ws = smt, *Xs = smt + TH * WS;
+    uint16_t *Wraw = reinterpret_cast<uint16_t *>(smt + TH * WS + BMAX * XP);
     const int tid = threadIdx.x, rg = tid & 7, vg = tid >> 3;
     const int row0 = blockIdx.x * TR;
     const int nchunks = (cols + TK - 1) / TK;
     const int c0 = blockIdx.y * cps, c1 = min(nchunks, c0 + cps);
     const bool active = 2 * vg < n;  // warp-uniform (a warp holds vg 4w .. 4w+3)
     const int npad = (n + 1) & ~1;
+    const int dc = tid & (TH - 1), dr0 = (tid >> 7) * 32;  // decode: column dc, rows dr0 .. dr0+31
     float acc[8][2];
 #pragma unroll
     for (int i = 0; i < 8; i++) acc[i][0] = acc[i][1] = 0.0f;
     for (int ch = c0; ch < c1; ch++) {
-        const int k0 = ch * TK, kc = min(TK, cols - k0);
         const uint64_t boff = (uint64_t)ch * CB;
         const int have = (int)min((uint64_t)CB, rb - boff) / 2;  // halfwords of this chunk in a row
-        // x chunk of every vector: 16-byte async copies into Xs[b][k]
-        // (cols and kc are multiples of 4; columns past kc are never read)
-        for (int e = tid; e < npad * (TK / 4); e += 256) {
-            const int b = e / (TK / 4), k4 = 4 * (e % (TK / 4));
-            float *dst = Xs + b * XP + k4;
-            if (b < n && k4 < kc) {
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                                 (uint32_t)__cvta_generic_to_shared(dst)),
-                             "l"(x + (size_t)b * cols + k0 + k4)
-                             : "memory");
-            } else {
-                *reinterpret_cast<float4 *>(dst) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int j0 = 0; j0 < PER; j0 += BATCH) {
+            uint16_t raw[BATCH];
+#pragma unroll
+            for (int j = 0; j < BATCH; j++) {
+                const int e = tid + 256 * (j0 + j), r = e / (CB / 2), hw = e - r * (CB / 2);
+                raw[j] = (j0 + j < PER && e < HW && row0 + r < rows && hw < have)
+                             ? ld_u16(w + (size_t)(row0 + r) * rb + boff + 2 * hw)
+                             : (uint16_t)0;
+            }
+#pragma unroll
+            for (int j = 0; j < BATCH; j++) {
+                const int e = tid + 256 * (j0 + j);
+                if (j0 + j < PER && e < HW) Wraw[e] = raw[j];
             }
         }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-        // packed rows: batches of independent 2-byte loads, then the stores
-        constexpr int PER = (TR * (CB / 2) + 255) / 256;
-        uint16_t raw[PER];
-#pragma unroll
-        for (int j = 0; j < PER; j++) {
-            const int e = tid + 256 * j, r = e / (CB / 2), hw = e - r * (CB / 2);
-            raw[j] = (e < TR * (CB / 2) && row0 + r < rows && hw < have)
-                         ? ld_u16(w + (size_t)(row0 + r) * rb + boff + 2 * hw)
-                         : (uint16_t)0;
-        }
-#pragma unroll
-        for (int j = 0; j < PER; j++) {
-            const int e = tid + 256 * j;
-            if (e < TR * (CB / 2)) Wraw[e] = raw[j];
-        }
-        asm volatile("cp.async.wait_all;" ::: "memory");
-        __syncthreads();
-        for (int r = 0; r < TR; r++) {
-            const uint8_t *rowp = reinterpret_cast<const uint8_t *>(Wraw + r * (CB / 2));
-            Ws[tid * WS + r] = tid < kc ? decode_col(T, rowp, tid) : 0.0f;
-        }
-        __syncthreads();
-        if (active) {
-#pragma unroll 4
-            for (int k = 0; k < kc; k++) {
-                const float4 w0 = *reinterpret_cast<const float4 *>(Ws + k * WS + 8 * rg);
-                const float4 w1 = *reinterpret_cast<const float4 *>(Ws + k * WS + 8 * rg + 4);
-                const float2 xv = make_float2(Xs[(2 * vg) * XP + k], Xs[(2 * vg + 1) * XP + k]);
-                const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    acc[i][0] = fmaf(wv[i], xv.x, acc[i][0]);
-                    acc[i][1] = fmaf(wv[i], xv.y, acc[i][1]);
+        for (int hf = 0; hf < TK / TH; hf++) {
+            const int k0 = ch * TK + hf * TH, kc = min(TH, cols - k0);
+            if (kc <= 0) break;
+            // x columns k0 .. k0+kc of every vector (cols and kc are multiples of 4)
+            for (int e = tid; e < npad * (TH / 4); e += 256) {
+                const int b = e / (TH / 4), k4 = 4 * (e % (TH / 4));
+                float *dst = Xs + b * XP + k4;
+                if (b < n && k4 < kc) {
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                                     (uint32_t)__cvta_generic_to_shared(dst)),
+                                 "l"(x + (size_t)b * cols + k0 + k4)
+                                 : "memory");
+                } else {
+                    *reinterpret_cast<float4 *>(dst) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 }
             }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+            __syncthreads();  // the chunk's packed rows are staged; Ws is free
+#pragma unroll 4
+            for (int r = dr0; r < dr0 + 32; r++) {
+                const uint8_t *rowp = reinterpret_cast<const uint8_t *>(Wraw + r * (CB / 2));
+                Ws[dc * WS + wpos(r)] = dc < kc ? decode_col(T, rowp, hf * TH + dc) : 0.0f;
+            }
+            asm volatile("cp.async.wait_all;" ::: "memory");
+            __syncthreads();
+            if (active) {
+                const float *wk = Ws + wpos(8 * rg);
+#pragma unroll 4
+                for (int k = 0; k < kc; k++) {
+                    const float4 w0 = *reinterpret_cast<const float4 *>(wk + k * WS);
+                    const float4 w1 = *reinterpret_cast<const float4 *>(wk + k * WS + 4);
+                    const float2 xv = make_float2(Xs[(2 * vg) * XP + k], Xs[(2 * vg + 1) * XP + k]);
+                    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        acc[i][0] = fmaf(wv[i], xv.x, acc[i][0]);
+                        acc[i][1] = fmaf(wv[i], xv.y, acc[i][1]);
+                    }
+                }
+            }
+            __syncthreads();
         }
-        __syncthreads();
     }
     if (!active) return;
     float *out = gridDim.y == 1 ? y : part + (size_t)blockIdx.y * n * rows;
@@ -185,7 +204,7 @@ __global__ void mv_reduce_kernel(const float *part, int splits, int count, float
 __host__ inline int mv_cps(int rows, int cols, int sms)
 {
     const int tiles = (rows + TR - 1) / TR, nchunks = (cols + TK - 1) / TK;
-    int splits = (2 * sms + tiles - 1) / tiles;
+    int splits = (4 * sms + tiles - 1) / tiles;  // two CTAs per SM, two waves
     if (splits > nchunks) splits = nchunks;
     if (splits < 1) splits = 1;
     return (nchunks + splits - 1) / splits;
