@@ -472,6 +472,30 @@ static int bmatmul(PkbCtx *b, const PkdTensor &t, const float *x, int n, float *
     return cudaGetLastError() == cudaSuccess;
 }
 
+// y_i = x W_i^T for weights that multiply the same x: the Q4_K ones in one
+// tensor-core launch (x staged once), the others on the tile kernel.
+static int bmatmul_group(PkbCtx *b, const PkdTensor *const *ts, float *const *ys, int cnt, const float *x, int n)
+{
+    PkMmSeg seg[3];
+    int ns = 0;
+    for (int i = 0; i < cnt; i++) {
+        const PkdTensor &t = *ts[i];
+        const uint8_t *w = b->arena + t.offset;
+        if (pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, w)) {
+            seg[ns].w = w;
+            seg[ns].row_bytes = t.row_bytes;
+            seg[ns].rows = (int)t.rows;
+            seg[ns].y = ys[i];
+            ns++;
+        } else if (!bmatmul(b, t, x, n, ys[i])) {
+            return 0;
+        }
+    }
+    if (ns == 0) return 1;
+    const int cols = (int)ts[0]->cols;
+    return pk_mm_stage(x, n, cols, &b->mm, b->st) && pk_mm_run_staged(seg, ns, cols, n, &b->mm, b->sms, b->st);
+}
+
 // The launches of one step for n sequences (inputs already in io_d).
 static int enqueue_step(PkbCtx *b, int n)
 {
@@ -485,9 +509,9 @@ static int enqueue_step(PkbCtx *b, int n)
     const size_t att_smem = (((size_t)m.seq_len + 3) / 4 * 4 + hs + 128 * 4) * 4;
     for (int l = 0; l < L; l++) {
         bt::rmsnorm_kernel<<<n, 256, 0, st>>>(b->x, b->norms + (size_t)(2 * l) * dim, dim, m.rms_eps, b->xn);
-        if (!bmatmul(b, m.wq[l], b->xn, n, b->q) || !bmatmul(b, m.wk[l], b->xn, n, b->k) ||
-            !bmatmul(b, m.wv[l], b->xn, n, b->v))
-            return 0;
+        const PkdTensor *qkv[3] = {&m.wq[l], &m.wk[l], &m.wv[l]};
+        float *const qkv_y[3] = {b->q, b->k, b->v};
+        if (!bmatmul_group(b, qkv, qkv_y, 3, b->xn, n)) return 0;
         bt::rope_cache_kernel<<<n, 256, 0, st>>>(b->q, b->k, b->v, b->rope_cs, m.rope_dim, hs, qd, kvd, b->io_d, B, l,
                                                  L, m.seq_len, b->kc, b->vc);
         bt::attention_kernel<<<dim3(m.n_heads, n), 128, att_smem, st>>>(b->q, b->kc, b->vc, b->io_d, B, l, L,
@@ -496,7 +520,9 @@ static int enqueue_step(PkbCtx *b, int n)
         if (!bmatmul(b, m.wo[l], b->att, n, b->tmp)) return 0;
         bt::add_kernel<<<(n * dim + 255) / 256, 256, 0, st>>>(b->x, b->tmp, n * dim);
         bt::rmsnorm_kernel<<<n, 256, 0, st>>>(b->x, b->norms + (size_t)(2 * l + 1) * dim, dim, m.rms_eps, b->xn);
-        if (!bmatmul(b, m.gate[l], b->xn, n, b->g) || !bmatmul(b, m.up[l], b->xn, n, b->u)) return 0;
+        const PkdTensor *gu[2] = {&m.gate[l], &m.up[l]};
+        float *const gu_y[2] = {b->g, b->u};
+        if (!bmatmul_group(b, gu, gu_y, 2, b->xn, n)) return 0;
         bt::swiglu_kernel<<<ew, 256, 0, st>>>(b->g, b->u, n * hid);
         if (!bmatmul(b, m.down[l], b->g, n, b->tmp)) return 0;
         bt::add_kernel<<<(n * dim + 255) / 256, 256, 0, st>>>(b->x, b->tmp, n * dim);
@@ -542,20 +568,30 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
     cudaDeviceGetAttribute(&b->sms, cudaDevAttrMultiProcessorCount, b->device);
     const int B = bt::BMAX, dim = m.dim, hs = m.head_size, qd = m.n_heads * hs, kvd = m.n_kv_heads * hs;
     const size_t cache = (size_t)max_seqs * m.n_layers * m.seq_len * kvd;
-    // matmul scratch: the largest need over the model's Q4_K weights at n = 64
+    // matmul scratch: the largest need over the model's Q4_K launches at
+    // n = 64 (Q/K/V and gate/up each one launch of their Q4_K matrices)
     PkMmNeed mx = {0, 0, 0, 0, 0};
     const PkdTensor *lists[7] = {m.wq, m.wk, m.wv, m.wo, m.gate, m.up, m.down};
-    for (int j = 0; j <= 7 * m.n_layers; j++) {
-        const PkdTensor &t = j == 7 * m.n_layers ? m.output : lists[j / m.n_layers][j % m.n_layers];
-        if (!pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, v.arena + t.offset)) continue;
+    auto consider = [&](int rows, int cols) {
+        if (rows == 0) return;
         PkMmNeed nd;
-        pk_mm_need((int)t.rows, (int)t.cols, B, b->sms, &nd);
+        pk_mm_need(rows, cols, B, b->sms, &nd);
         if (nd.xs > mx.xs) mx.xs = nd.xs;
         if (nd.x2s > mx.x2s) mx.x2s = nd.x2s;
         if (nd.xinv > mx.xinv) mx.xinv = nd.xinv;
         if (nd.ypart > mx.ypart) mx.ypart = nd.ypart;
         if (nd.arrived > mx.arrived) mx.arrived = nd.arrived;
+    };
+    auto q4k_rows = [&](const PkdTensor &t) -> int {
+        return pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, v.arena + t.offset) ? (int)t.rows : 0;
+    };
+    for (int l = 0; l < m.n_layers; l++) {
+        consider(q4k_rows(m.wq[l]) + q4k_rows(m.wk[l]) + q4k_rows(m.wv[l]), m.dim);
+        consider(q4k_rows(m.wo[l]), (int)m.wo[l].cols);
+        consider(q4k_rows(m.gate[l]) + q4k_rows(m.up[l]), m.dim);
+        consider(q4k_rows(m.down[l]), (int)m.down[l].cols);
     }
+    consider(q4k_rows(m.output), m.dim);
     size_t part_max = 16;
     for (int j = 0; j <= 7 * m.n_layers; j++) {
         const PkdTensor &t = j == 7 * m.n_layers ? m.output : lists[j / m.n_layers][j % m.n_layers];

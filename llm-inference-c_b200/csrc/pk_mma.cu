@@ -268,8 +268,20 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volati
     return __all_sync(0xFFFFFFFFu, got);
 }
 
+constexpr int MSEG = 3;  // weight matrices (segments) of one launch, all with the same columns
+
+// The weight matrices of one launch as 2D tensors of bytes [rows][row
+// bytes], box [128 rows][144 bytes] (one super-block of one row tile).
+struct MmMaps {
+    CUtensorMap m[MSEG];
+};
+
 struct MmArgs {
-    int rows, nsb;          // rows, super-blocks per row
+    int nseg;               // segments: row tiles [tile0[s], tile0[s + 1]) are matrix s
+    int tile0[MSEG + 1];
+    int seg_rows[MSEG];
+    float *seg_y[MSEG];     // [n][rows of the segment]
+    int nsb;                // super-blocks per row
     const uint8_t *xs;      // staged x: [nsb][4 steps][8 chunks][N rows][16 B]
     const uint8_t *x2s;     // staged x sums: [nsb][2 chunks][N rows][16 B]
     const float *xinv;      // [nsb][64] inverse scales of the staged pieces
@@ -278,7 +290,6 @@ struct MmArgs {
     int U;                  // work units (row tiles x super-blocks)
     int G;                  // CTAs
     int maxp;               // partial slots per tile
-    float *y;               // [n][rows]
     float *ypart;           // [tiles][maxp][n][128]
     unsigned int *arrived;  // [tiles][8 warps] CTAs done with that block (reset by the last)
     int *err;
@@ -290,11 +301,14 @@ struct MmArgs {
 // the CTAs done with that block names the last one, which adds the pieces
 // in CTA order (no barrier between warps: an aborted warp blocks none).
 // Out of line and rare (once per tile piece): it keeps the kernel small.
+// T: the tile's index over all segments (partial slots, owners); lt: its
+// index inside its matrix, whose rows and output are rows / y.
 __device__ __noinline__ void flush_piece(const float *acc, float *y, float *ypart, unsigned int *arrived, int rows,
-                                         int n, int nsb, int U, int G, int maxp, int T, int c, int row, int b0)
+                                         int n, int nsb, int U, int G, int maxp, int T, int lt, int c, int row,
+                                         int b0)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int r = T * TM + row;
+    const int r = lt * TM + row;
     const int c0 = unit_owner((long long)T * nsb, U, G), c1 = unit_owner((long long)T * nsb + nsb - 1, U, G);
     const int nb = min(32, n - b0);
     if (c0 == c1) {
@@ -333,15 +347,20 @@ __device__ __noinline__ void flush_piece(const float *acc, float *y, float *ypar
     }
 }
 
-// wmap: the weights as a 2D tensor of bytes [rows][row bytes], box
-// [128 rows][144 bytes] (one super-block of one row tile).
-__global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constant__ CUtensorMap wmap, MmArgs a)
+__device__ __forceinline__ int seg_of(const MmArgs &a, int T)
+{
+    int sg = 0;
+    while (sg + 1 < a.nseg && T >= a.tile0[sg + 1]) sg++;
+    return sg;
+}
+
+__global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constant__ MmMaps maps, MmArgs a)
 {
     extern __shared__ __align__(128) uint8_t sm_raw[];
     uint8_t *sm = sm_raw + ((128u - (smem_u32(sm_raw) & 127u)) & 127u);
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tid = threadIdx.x, warp = tid >> 5;
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + OFF_BAR);
     float *inv_s = reinterpret_cast<float *>(sm + OFF_INV);
     const int c = blockIdx.x;
@@ -395,7 +414,10 @@ __global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constan
         // (rows past the end of the matrix arrive as zeros), then the 64
         // inverse scales of the matching x piece
         const bool leader = elect_one();
-        if (leader) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+        if (leader) {
+            for (int sg = 0; sg < a.nseg; sg++)
+                asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.m[sg])) : "memory");
+        }
         int issued = 0, T = T0, s = s0;
         for (int j = 0; j < nu; j++) {
             const int slot = j % SW;
@@ -403,7 +425,8 @@ __global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constan
             if (leader) {
                 uint8_t *dst = sm + OFF_W + slot * W_BYTES;
                 mbar_expect_tx(bars + FULL_W + slot, (uint32_t)W_BYTES);
-                tma_load_2d(dst, &wmap, s * SBB, T * TM, bars + FULL_W + slot);
+                const int sg = seg_of(a, T);
+                tma_load_2d(dst, &maps.m[sg], s * SBB, (T - a.tile0[sg]) * TM, bars + FULL_W + slot);
                 bulk_g2s(dst + W_TILE, a.xinv + (size_t)s * VMAX, VMAX * 4, bars + FULL_W + slot);
             }
             __syncwarp();
@@ -549,7 +572,9 @@ __global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constan
                 float out[32];
 #pragma unroll
                 for (int b = 0; b < 32; b++) out[b] = acc[b];
-                flush_piece(out, a.y, a.ypart, a.arrived, a.rows, a.n, a.nsb, a.U, a.G, a.maxp, rT, c, row, b0);
+                const int sg = seg_of(a, rT);
+                flush_piece(out, a.seg_y[sg], a.ypart, a.arrived, a.seg_rows[sg], a.n, a.nsb, a.U, a.G, a.maxp, rT,
+                            rT - a.tile0[sg], c, row, b0);
             }
             if (++rs == a.nsb) {
                 rs = 0;
@@ -765,9 +790,8 @@ MmScratch *mm_scratch(int dev, size_t xs_b, size_t x2s_b, size_t xinv_b, size_t 
 // At most one CTA per SM, and no more CTAs than split each row tile in
 // about two pieces: the last CTA of a tile adds the pieces up after all
 // others, so many pieces per tile leave one straggler per tile.
-extern "C" void gguf_cuda_matmul_plan(int rows, int nsb, int sms, int *ctas, int *maxp)
+static void plan_tiles(int tiles, int nsb, int sms, int *ctas, int *maxp)
 {
-    const int tiles = (rows + mm::TM - 1) / mm::TM;
     const long long U = (long long)tiles * nsb;
     long long G = (2 * U + nsb - 1) / nsb;  // about two pieces per tile
     if (G < tiles) G = tiles;
@@ -783,6 +807,11 @@ extern "C" void gguf_cuda_matmul_plan(int rows, int nsb, int sms, int *ctas, int
     *maxp = mp;
 }
 
+extern "C" void gguf_cuda_matmul_plan(int rows, int nsb, int sms, int *ctas, int *maxp)
+{
+    plan_tiles((rows + mm::TM - 1) / mm::TM, nsb, sms, ctas, maxp);
+}
+
 int pk_mm_shape_ok(uint32_t type, uint64_t rows, uint64_t cols, uint64_t row_bytes, const void *data)
 {
     if (type != T_Q4_K || cols == 0 || cols % mm::QK || rows == 0) return 0;
@@ -795,7 +824,7 @@ void pk_mm_need(int rows, int cols, int n, int sms, PkMmNeed *need)
 {
     const int nsb = cols / mm::QK, N = (2 * n + 15) / 16 * 16, tiles = (rows + mm::TM - 1) / mm::TM;
     int G = 0, maxp = 0;
-    gguf_cuda_matmul_plan(rows, nsb, sms, &G, &maxp);
+    plan_tiles(tiles, nsb, sms, &G, &maxp);
     need->xs = (size_t)nsb * 4 * N * 128;
     need->x2s = (size_t)nsb * N * 32;
     need->xinv = (size_t)nsb * mm::VMAX * 4;
@@ -825,28 +854,43 @@ int pk_mm_smem_max(int dev)
     return per[dev];
 }
 
-int pk_mm_run(const uint8_t *w, uint64_t row_bytes, int rows, int cols, const float *x, int n, float *y,
-              const PkMmScratch *s, int sms, cudaStream_t st)
+int pk_mm_stage(const float *x, int n, int cols, const PkMmScratch *s, cudaStream_t st)
 {
-    if (n < 1 || n > mm::VMAX || s == nullptr || s->smem_max <= 0) return 0;
-    const int K = cols, nsb = K / mm::QK;
+    if (n < 1 || n > mm::VMAX || s == nullptr) return 0;
     const int N = (2 * n + 15) / 16 * 16;
-    const int tiles = (rows + mm::TM - 1) / mm::TM;
-    int G = 0, maxp = 0;
-    gguf_cuda_matmul_plan(rows, nsb, sms, &G, &maxp);
+    mm::mm_stage_kernel<<<dim3(cols / mm::QK, N / 2), 256, 0, st>>>(x, n, cols, N, s->xs, s->x2s, s->xinv);
+    return cudaGetLastError() == cudaSuccess;
+}
+
+int pk_mm_run_staged(const PkMmSeg *seg, int nseg, int cols, int n, const PkMmScratch *s, int sms, cudaStream_t st)
+{
+    if (n < 1 || n > mm::VMAX || s == nullptr || s->smem_max <= 0 || nseg < 1 || nseg > mm::MSEG) return 0;
+    const int nsb = cols / mm::QK;
+    const int N = (2 * n + 15) / 16 * 16;
     PFN_cuTensorMapEncodeTiled_v12000 enc = encode_tiled();
     if (enc == nullptr) return 0;
-    CUtensorMap wmap;
-    const cuuint64_t gdim[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
-    const cuuint64_t gstride[1] = {(cuuint64_t)row_bytes};
-    const cuuint32_t box[2] = {(cuuint32_t)mm::SBB, (cuuint32_t)mm::TM};
-    const cuuint32_t estride[2] = {1, 1};
-    if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(w), gdim, gstride, box, estride,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return 0;
+    mm::MmMaps maps;
+    memset(&maps, 0, sizeof(maps));
     mm::MmArgs a;
-    a.rows = rows;
+    a.nseg = nseg;
+    int tiles = 0;
+    for (int i = 0; i < nseg; i++) {
+        const cuuint64_t gdim[2] = {(cuuint64_t)seg[i].row_bytes, (cuuint64_t)seg[i].rows};
+        const cuuint64_t gstride[1] = {(cuuint64_t)seg[i].row_bytes};
+        const cuuint32_t box[2] = {(cuuint32_t)mm::SBB, (cuuint32_t)mm::TM};
+        const cuuint32_t estride[2] = {1, 1};
+        if (enc(&maps.m[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(seg[i].w), gdim, gstride, box,
+                estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return 0;
+        a.tile0[i] = tiles;
+        a.seg_rows[i] = seg[i].rows;
+        a.seg_y[i] = seg[i].y;
+        tiles += (seg[i].rows + mm::TM - 1) / mm::TM;
+    }
+    for (int i = nseg; i <= mm::MSEG; i++) a.tile0[i] = tiles;
+    int G = 0, maxp = 0;
+    plan_tiles(tiles, nsb, sms, &G, &maxp);
     a.nsb = nsb;
     a.xs = s->xs;
     a.x2s = s->x2s;
@@ -859,14 +903,23 @@ int pk_mm_run(const uint8_t *w, uint64_t row_bytes, int rows, int cols, const fl
     a.U = tiles * nsb;
     a.G = G;
     a.maxp = maxp;
-    a.y = y;
     a.ypart = s->ypart;
     a.arrived = s->arrived;
     a.err = s->err;
     const int smem = mm::OFF_B + a.sb * a.b_slot + 128;
-    mm::mm_stage_kernel<<<dim3(nsb, N / 2), 256, 0, st>>>(x, n, K, N, s->xs, s->x2s, s->xinv);
-    mm::q4k_mm_kernel<<<G, mm::THREADS, smem, st>>>(wmap, a);
+    mm::q4k_mm_kernel<<<G, mm::THREADS, smem, st>>>(maps, a);
     return cudaGetLastError() == cudaSuccess;
+}
+
+int pk_mm_run(const uint8_t *w, uint64_t row_bytes, int rows, int cols, const float *x, int n, float *y,
+              const PkMmScratch *s, int sms, cudaStream_t st)
+{
+    PkMmSeg seg;
+    seg.w = w;
+    seg.row_bytes = row_bytes;
+    seg.rows = rows;
+    seg.y = y;
+    return pk_mm_stage(x, n, cols, s, st) && pk_mm_run_staged(&seg, 1, cols, n, s, sms, st);
 }
 
 extern "C" int gguf_cuda_matmul(const GGUFWeight *w, const float *x, int n, float *y, void *stream)

@@ -34,4 +34,17 @@ int pk_mm_smem_max(int dev);
 int pk_mm_run(const uint8_t *w, uint64_t row_bytes, int rows, int cols, const float *x, int n, float *y,
               const PkMmScratch *s, int sms, cudaStream_t st);
 
+// The same in two parts, for several matrices that multiply one x: stage x
+// once (pk_mm_stage), then one launch over up to 3 matrices of `cols`
+// columns (pk_mm_run_staged; scratch sized by pk_mm_need for their summed
+// rows), each with its own output.
+struct PkMmSeg {
+    const uint8_t *w;
+    uint64_t row_bytes;
+    int rows;
+    float *y;  // n x rows
+};
+int pk_mm_stage(const float *x, int n, int cols, const PkMmScratch *s, cudaStream_t st);
+int pk_mm_run_staged(const PkMmSeg *seg, int nseg, int cols, int n, const PkMmScratch *s, int sms, cudaStream_t st);
+
 #endif
