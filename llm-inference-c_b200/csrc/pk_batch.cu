@@ -350,6 +350,101 @@ __global__ void __launch_bounds__(128) attention_kernel(const float *q, const fl
     }
 }
 
+// Attention of all H = kv_mul query heads of KV head g for sequence b in
+// one CTA, so every key and value row is read once per group rather than
+// once per query head. Scores: one thread per position computes the H dot
+// products from its key row (16-byte loads); softmax: warp w takes heads
+// w, w + 16, ...; weighted sum: thread (tg, h, d4) adds float4 d4 of the
+// value rows t = tg mod G times p_h, and the G partials are added in order.
+// 512 threads; H * hs / 4 <= 128.
+__global__ void __launch_bounds__(512) attention_gqa_kernel(const float *q, const float *kc, const float *vc,
+                                                            const int *io, int bmax, int layer, int L, int seq_len,
+                                                            int hs, int qd, int kvd, int H, float scale, float *out)
+{
+    extern __shared__ __align__(16) float sg[];  // H * hs queries, H rows of seq_len scores, G x 128 float4 partials
+    const int g = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int P = io[bmax + b] + 1, seq = io[2 * bmax + b];
+    const int sl = (seq_len + 3) & ~3, F4 = hs >> 2;
+    float *qs = sg, *sc = sg + H * hs;
+    for (int i = tid; i < H * hs; i += blockDim.x) qs[i] = q[(size_t)b * qd + (size_t)g * H * hs + i];
+    __syncthreads();
+    const size_t base = ((size_t)seq * L + layer) * seq_len * kvd + (size_t)g * hs;
+    const float4 *q4 = reinterpret_cast<const float4 *>(qs);
+    for (int t = tid; t < P; t += blockDim.x) {
+        const float4 *kt = reinterpret_cast<const float4 *>(kc + base + (size_t)t * kvd);
+        float dot[8];
+#pragma unroll
+        for (int h = 0; h < 8; h++) dot[h] = 0.0f;
+        for (int i = 0; i < F4; i++) {
+            const float4 kv = kt[i];
+#pragma unroll
+            for (int h = 0; h < 8; h++) {
+                if (h < H) {
+                    const float4 qv = q4[h * F4 + i];
+                    dot[h] = fmaf(qv.x, kv.x, dot[h]);
+                    dot[h] = fmaf(qv.y, kv.y, dot[h]);
+                    dot[h] = fmaf(qv.z, kv.z, dot[h]);
+                    dot[h] = fmaf(qv.w, kv.w, dot[h]);
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 8; h++)
+            if (h < H) sc[h * sl + t] = dot[h] * scale;
+    }
+    __syncthreads();
+    for (int h = warp; h < H; h += blockDim.x >> 5) {
+        float *sh = sc + h * sl;
+        float m = -INFINITY;
+        for (int t = lane; t < P; t += 32) m = fmaxf(m, sh[t]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+        float sum = 0.0f;
+        for (int t = lane; t < P; t += 32) {
+            const float e = expf(sh[t] - m);
+            sh[t] = e;
+            sum += e;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+        const float inv = 1.0f / sum;
+        for (int t = lane; t < P; t += 32) sh[t] *= inv;
+    }
+    __syncthreads();
+    const int HF = H * F4, G = blockDim.x / HF;
+    const int tg = tid / HF, hd = tid - tg * HF, h = hd / F4, d4 = hd - h * F4;
+    float4 *part = reinterpret_cast<float4 *>(sc + H * sl);
+    if (tg < G) {
+        const float4 *vb = reinterpret_cast<const float4 *>(vc + base) + d4;
+        const float *ph = sc + h * sl;
+        const size_t stride = (size_t)(kvd >> 2);
+        float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 4
+        for (int t = tg; t < P; t += G) {
+            const float4 vv = vb[(size_t)t * stride];
+            const float pt = ph[t];
+            o.x = fmaf(pt, vv.x, o.x);
+            o.y = fmaf(pt, vv.y, o.y);
+            o.z = fmaf(pt, vv.z, o.z);
+            o.w = fmaf(pt, vv.w, o.w);
+        }
+        part[tg * HF + hd] = o;
+    }
+    __syncthreads();
+    if (tid < HF) {
+        float4 r = part[tid];
+        for (int k = 1; k < G; k++) {
+            const float4 pk = part[k * HF + tid];
+            r.x += pk.x;
+            r.y += pk.y;
+            r.z += pk.z;
+            r.w += pk.w;
+        }
+        const int hh = tid / F4, dd = tid - hh * F4;
+        reinterpret_cast<float4 *>(out + (size_t)b * qd + ((size_t)g * H + hh) * hs)[dd] = r;
+    }
+}
+
 __global__ void add_kernel(float *x, const float *y, int count)
 {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) x[i] += y[i];
@@ -428,7 +523,7 @@ struct PkbCtx {
     PkMmScratch mm;
     cudaGraph_t graph[bt::BMAX + 1];
     cudaGraphExec_t exec[bt::BMAX + 1];
-    int tile_attr;
+    int gqa_smem;  // dynamic shared memory of attention_gqa_kernel (0: per-head attention instead)
     char msg[256];
 };
 
@@ -514,9 +609,16 @@ static int enqueue_step(PkbCtx *b, int n)
         if (!bmatmul_group(b, qkv, qkv_y, 3, b->xn, n)) return 0;
         bt::rope_cache_kernel<<<n, 256, 0, st>>>(b->q, b->k, b->v, b->rope_cs, m.rope_dim, hs, qd, kvd, b->io_d, B, l,
                                                  L, m.seq_len, b->kc, b->vc);
-        bt::attention_kernel<<<dim3(m.n_heads, n), 128, att_smem, st>>>(b->q, b->kc, b->vc, b->io_d, B, l, L,
-                                                                         m.seq_len, hs, qd, kvd,
-                                                                         m.n_heads / m.n_kv_heads, m.att_scale, b->att);
+        if (b->gqa_smem > 0) {
+            bt::attention_gqa_kernel<<<dim3(m.n_kv_heads, n), 512, b->gqa_smem, st>>>(
+                b->q, b->kc, b->vc, b->io_d, B, l, L, m.seq_len, hs, qd, kvd, m.n_heads / m.n_kv_heads, m.att_scale,
+                b->att);
+        } else {
+            bt::attention_kernel<<<dim3(m.n_heads, n), 128, att_smem, st>>>(b->q, b->kc, b->vc, b->io_d, B, l, L,
+                                                                             m.seq_len, hs, qd, kvd,
+                                                                             m.n_heads / m.n_kv_heads, m.att_scale,
+                                                                             b->att);
+        }
         if (!bmatmul(b, m.wo[l], b->att, n, b->tmp)) return 0;
         bt::add_kernel<<<(n * dim + 255) / 256, 256, 0, st>>>(b->x, b->tmp, n * dim);
         bt::rmsnorm_kernel<<<n, 256, 0, st>>>(b->x, b->norms + (size_t)(2 * l + 1) * dim, dim, m.rms_eps, b->xn);
@@ -644,6 +746,18 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
         ok = !bfail(b, cudaFuncSetAttribute(bt::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             (int)att_smem),
                     "cudaFuncSetAttribute");
+    // grouped attention when a CTA can hold the group's queries and scores
+    // and the group fills at least half of its threads
+    {
+        const int H = m.n_heads / m.n_kv_heads;
+        const size_t gs = ((size_t)H * hs + (size_t)H * ((m.seq_len + 3) / 4 * 4)) * 4 + 512 * 16;
+        if (ok && H >= 2 && H <= 8 && H * (hs / 4) >= 64 && H * (hs / 4) <= 128 && gs <= 200 * 1024) {
+            ok = !bfail(b, cudaFuncSetAttribute(bt::attention_gqa_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                (int)gs),
+                        "cudaFuncSetAttribute");
+            b->gqa_smem = (int)gs;
+        }
+    }
     ok = ok && !bfail(b, cudaStreamSynchronize(b->st), "batched setup");
     if (!ok) {
         if (err && cap) snprintf(err, cap, "%s", b->msg[0] ? b->msg : "Batched decode setup failed.");
