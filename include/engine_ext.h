@@ -114,14 +114,17 @@ int engine_launches_per_step(const LLMModel *model);
  * previous one. Returns 1, or 0 with a message in error. */
 int engine_batch_open(LLMModel *model, int max_seqs, char *error, size_t error_capacity);
 
-/* One decode step: sequence seq_ids[i] consumes tokens[i] at position
- * pos[i] (i < n; seq_ids distinct, below max_seqs; tokens in the
- * vocabulary; positions below the context length), exactly as
- * engine_forward(tokens[i], pos[i]) would for that sequence alone.
- * next_tokens[i] receives the greedy token (device argmax, lowest index on
- * ties; -1 when a logit is not finite); logits, when not NULL, the n x
- * vocab_size logits (row i for sequence seq_ids[i]). Returns 1, or 0 on
- * bad arguments or a device error (engine_last_error). */
+/* One step over n <= 64 rows: sequence seq_ids[i] consumes tokens[i] at
+ * position pos[i] (seq_ids below max_seqs; tokens in the vocabulary;
+ * positions below the context length; each (sequence, position) at most
+ * once per call), exactly as engine_forward(tokens[i], pos[i]) would for
+ * that sequence alone. Rows of one sequence at consecutive positions form a
+ * prompt chunk (prefill): every row's keys and values are appended before
+ * any row attends, so row i sees the sequence's positions 0 .. pos[i].
+ * next_tokens[i] receives the greedy token of row i (device argmax, lowest
+ * index on ties; -1 when a logit is not finite); logits, when not NULL, the
+ * n x vocab_size logits. Returns 1, or 0 on bad arguments or a device error
+ * (engine_last_error). */
 int engine_forward_batch(LLMModel *model, const int *tokens, const int *pos, const int *seq_ids, int n,
                          int *next_tokens, float *logits);
 

@@ -966,14 +966,14 @@ int engine_forward_batch(LLMModel *m, const int *tokens, const int *pos, const i
                          int *next_tokens, float *logits)
 {
     if (m == NULL || m->batch == NULL || tokens == NULL || pos == NULL || seq_ids == NULL || next_tokens == NULL ||
-        n < 1 || n > m->batch_seqs)
+        n < 1 || n > ENGINE_BATCH_MAX)
         return 0;
-    unsigned long long seen = 0;  /* batch_seqs <= 64: one bit per sequence */
     for (int i = 0; i < n; i++) {
         if (tokens[i] < 0 || tokens[i] >= m->config.vocab_size || pos[i] < 0 || pos[i] >= m->config.seq_len ||
-            seq_ids[i] < 0 || seq_ids[i] >= m->batch_seqs || (seen >> seq_ids[i]) & 1ull)
+            seq_ids[i] < 0 || seq_ids[i] >= m->batch_seqs)
             return 0;
-        seen |= 1ull << seq_ids[i];
+        for (int j = 0; j < i; j++)  /* each (sequence, position) once per step */
+            if (seq_ids[j] == seq_ids[i] && pos[j] == pos[i]) return 0;
     }
     if (!pkb_step(m->batch, tokens, pos, seq_ids, n, next_tokens, logits)) {
         snprintf(m->last_error, sizeof(m->last_error), "%s", pkb_error(m->batch));

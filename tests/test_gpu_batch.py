@@ -77,16 +77,53 @@ def test_batch_legacy_formats(orc, synth_model):
     assert worst <= LOGIT_TOL, worst
 
 
+def test_batch_prefill_chunks_match_oracle(orc, synth_model):
+    # one call carries a whole prompt of sequence 0 (positions 0..39), a
+    # chunk of sequence 2's prompt and a decode row of sequence 1
+    path = synth_model("tiny-q4km")
+    e = pk_b200.Engine(path, 128, device=0)
+    e.batch_open(3)
+    rng = np.random.default_rng(21)
+    p0 = list(rng.integers(0, e.vocab_size, size=40))
+    p1 = list(rng.integers(0, e.vocab_size, size=3))
+    p2 = list(rng.integers(0, e.vocab_size, size=20))
+    refs = [orc.open(path, 128) for _ in range(3)]
+    worst = 0.0
+    # sequence 1 first decodes its first two tokens alone
+    for pos, t in enumerate(p1[:2]):
+        nxt, lg = e.forward_batch([t], [pos], [1], logits=True)
+        want = refs[1].forward(int(t), pos)
+        worst = max(worst, float(np.max(np.abs(lg[0] - want))))
+    toks = p0 + p2[:10] + [p1[2]]
+    poss = list(range(40)) + list(range(10)) + [2]
+    seqs = [0] * 40 + [2] * 10 + [1]
+    nxt, lg = e.forward_batch(toks, poss, seqs, logits=True)
+    for i, (t, p, s_) in enumerate(zip(toks, poss, seqs)):
+        want = refs[s_].forward(int(t), p)
+        worst = max(worst, float(np.max(np.abs(lg[i] - want))))
+        assert int(nxt[i]) == int(np.argmax(want)), i
+    # the rest of sequence 2's prompt in a second chunk
+    nxt, lg = e.forward_batch(p2[10:], list(range(10, 20)), [2] * 10, logits=True)
+    for i, t in enumerate(p2[10:]):
+        want = refs[2].forward(int(t), 10 + i)
+        worst = max(worst, float(np.max(np.abs(lg[i] - want))))
+        assert int(nxt[i]) == int(np.argmax(want)), i
+    for r in refs:
+        r.close()
+    e.close()
+    assert worst <= LOGIT_TOL, worst
+
+
 def test_batch_refuses_bad_arguments(synth_model):
     path = synth_model("tiny-q4km")
     e = pk_b200.Engine(path, 64, device=0)
     assert e.forward_batch([1], [0], [0]) is None  # before engine_batch_open
     e.batch_open(4)
-    assert e.forward_batch([1, 2], [0, 0], [1, 1]) is None          # repeated sequence
+    assert e.forward_batch([1, 2], [0, 0], [1, 1]) is None          # repeated (sequence, position)
     assert e.forward_batch([1], [64], [0]) is None                  # position past the context
     assert e.forward_batch([e.vocab_size], [0], [0]) is None        # token outside the vocabulary
     assert e.forward_batch([1], [0], [4]) is None                   # sequence id past max_seqs
-    assert e.forward_batch([1] * 5, [0] * 5, [0, 1, 2, 3, 0]) is None  # more than max_seqs
+    assert e.forward_batch([1] * 65, list(range(65)), [0] * 65) is None  # more than 64 rows
     out = e.forward_batch([1, 2], [0, 0], [2, 0])
     assert out is not None and out[1] is None
     # the single-sequence path is independent of the batched state
