@@ -10,11 +10,14 @@ timed greedy decode steps; one step = one decoded token.
   e2e    the same K steps through the reference-facing C ABI with host
          buffers: engine_forward() (token/pos up, logits down) + host argmax.
 
-Under torchrun (N > 1) the ranks decode ONE sequence tensor-parallel (strong
-scaling): each GPU holds its attention heads, FFN hidden slice and vocabulary
-rows, and the decode kernels all-reduce the partial sums over NVLink peer
-memory; value = the sequence's tokens / the slowest rank's time, and the
-roofline peak is N x the HBM figure.
+Under torchrun (N > 1), on the TinyLlama shape every GPU decodes its own
+independent sequence (data parallel, weak scaling, no collective on the
+data path; value = N x the tokens / the slowest rank's time; the B=64 line
+likewise runs 64 sequences per GPU). The 7B/8B shapes (and --tp) decode ONE
+sequence tensor-parallel (strong scaling): each GPU holds its attention
+heads, FFN hidden slice and vocabulary rows, and the decode kernels
+all-reduce the partial sums over NVLink peer memory; value = the sequence's
+tokens / the slowest rank's time. The roofline peak is N x the HBM figure.
 
   --impl reference   times the reference's own CPU engine (compiled from its
                      sources into oracle/_ref) on the same model file.
@@ -291,7 +294,7 @@ def run_matmul_sweep(args):
     return 0
 
 
-def run_b64(path, args, cfg):
+def run_b64(path, args, cfg, device=0, barrier=lambda: None):
     """Batched decode of 64 independent sequences (engine_forward_batch):
     each sequence first decodes a seeded random context (512 tokens by
     default, --b64-context) into its KV cache, then W warm-up and K timed
@@ -300,7 +303,7 @@ def run_b64(path, args, cfg):
     back (synchronous), so the wall time per step is end to end."""
     import pk_b200
     B, W, K, C = 64, args.warmup, args.b64_steps, args.b64_context
-    e = pk_b200.Engine(path, C + W + K + 8, device=0)
+    e = pk_b200.Engine(path, C + W + K + 8, device=device)
     e.batch_open(B)
     rng = np.random.default_rng(MODEL_SEED + 64)
     ctx = rng.integers(0, e.vocab_size, size=(B, C))
@@ -314,11 +317,13 @@ def run_b64(path, args, cfg):
     for i in range(W):
         nxt, _ = e.forward_batch(nxt, np.full(B, pos), seq)
         pos += 1
+    barrier()
     t0 = time.perf_counter()
     for i in range(K):
         nxt, _ = e.forward_batch(nxt, np.full(B, pos), seq)
         pos += 1
     dt = time.perf_counter() - t0
+    barrier()
     e.close()
     wbytes = pk_synth.weight_bytes_per_token(WORKLOADS["tinyllama"]["preset"])
     kvb = kv_bytes_per_step(cfg, list(range(C + W, C + W + K))) * B
@@ -326,6 +331,7 @@ def run_b64(path, args, cfg):
     hbm, peak_kind = peaks()
     achieved = (wbytes + kvb) / step_s / 1e9
     return {"metric": "decode tok/s (B=64)", "value": B * K / dt, "unit": "tok/s", "steps": K, "warmup": W,
+            "seconds": dt,
             "ms_per_step": step_s * 1e3,
             "config": {"workload": "TinyLlama-1.1B-arch Q4_K_M, 64 independent sequences, greedy decode",
                        "context_per_sequence": [C + W, C + W + K - 1],
@@ -352,6 +358,8 @@ def main():
     ap.add_argument("--only", default=None, help="matvec workload: one TYPE:ROWSxCOLS case")
     ap.add_argument("--b64-steps", type=int, default=32, help="timed steps of the B=64 batched decode (0: skip)")
     ap.add_argument("--b64-context", type=int, default=512, help="tokens decoded into each sequence's KV cache first")
+    ap.add_argument("--tp", action="store_true",
+                    help="N > 1 on the TinyLlama shape: one sequence tensor-parallel instead of one per GPU")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -392,16 +400,23 @@ def main():
 
     path = ensure_model(wl["preset"], rank, barrier)
     need = wl["prompt"] + args.warmup + args.steps + 1
-    # N > 1: one sequence decoded tensor-parallel over the N GPUs (each rank
-    # holds its heads, hidden slice and vocabulary rows; the decode kernels
-    # all-reduce over NVLink peer memory)
-    e = pk_b200.Engine(path, max(need, 64), device=local, rank=rank, world=world)
-    if world > 1:
+    # N > 1: the 7B/8B shapes (or --tp) decode one sequence tensor-parallel
+    # over the N GPUs (each rank holds its heads, hidden slice and vocabulary
+    # rows; the decode kernels all-reduce over NVLink peer memory). The
+    # TinyLlama shape fits one GPU many times over, so by default every GPU
+    # decodes its own independent sequence (data parallel, no collective on
+    # the data path; weak scaling).
+    tp = world > 1 and (args.tp or args.workload != "tinyllama")
+    if tp:
+        e = pk_b200.Engine(path, max(need, 64), device=local, rank=rank, world=world)
         e.tp_connect(pk_b200.tp_exchange(e.tp_handle(), world))
+    else:
+        e = pk_b200.Engine(path, max(need, 64), device=local)
     cfg = e.config
     if need > e.seq_len:
         raise SystemExit(f"prompt + warmup + steps = {need} exceeds the context {e.seq_len}")
-    prompt = prompt_ids(wl["prompt"], e.vocab_size, 0)  # every rank feeds the same sequence
+    # tensor parallel: every rank feeds the same sequence; data parallel: its own
+    prompt = prompt_ids(wl["prompt"], e.vocab_size, 0 if tp or world == 1 else rank)
 
     def feed_prompt():
         logits = None
@@ -442,45 +457,57 @@ def main():
     ms_max, e2e_ms_max = float(t[0]), float(t[1])
 
     hbm1, peak_kind = peaks()
-    hbm = hbm1 * world  # the weights are spread over the N GPUs' HBM
+    hbm = hbm1 * world  # the N GPUs' HBM together
     wbytes = pk_synth.weight_bytes_per_token(wl["preset"])
     positions = list(range(pos0, pos0 + args.steps))
     kvb = kv_bytes_per_step(cfg, positions)
     step_s = ms_max / 1000.0 / args.steps
-    achieved = (wbytes + kvb) / step_s / 1e9
+    replicas = 1 if tp else world  # sequences decoded at once, each streaming all weights
+    achieved = replicas * (wbytes + kvb) / step_s / 1e9
     launches_per_step = e.launches_per_step()
     if launches_per_step == 2:
-        per = 7 if world > 1 else 5
+        per = 7 if tp else 5
         kernel = (f"phase_kernel (one cooperative launch per step per GPU: {per * cfg['n_layers'] + 1} phases, "
                   f"tagged-word hand-offs, no grid barrier) + finish_kernel (1 thread)")
     else:
         kernel = f"phase_kernel x{launches_per_step - 1} (one per phase) + finish_kernel"
 
     b64 = None
-    if world == 1 and args.b64_steps > 0 and args.workload == "tinyllama":
-        b64 = run_b64(path, args, cfg)
+    if not tp and args.b64_steps > 0 and args.workload == "tinyllama":
+        b64 = run_b64(path, args, cfg, device=local, barrier=barrier)
+        tb = torch.tensor([b64["seconds"]], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(tb, op=dist.ReduceOp.MAX)
+        b64["value"] = world * 64 * args.b64_steps / float(tb[0])  # all GPUs, slowest rank's time
+        b64["ms_per_step"] = float(tb[0]) / args.b64_steps * 1e3
+        b64["n_gpus"] = world
+        b64["roofline"]["achieved"] *= world * b64["seconds"] / float(tb[0])
+        b64["roofline"]["peak"] = hbm
+        b64["roofline"]["frac"] = b64["roofline"]["achieved"] / hbm
 
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         base = reference_decode(path, wl["prompt"], 64, 2, budget_s=15.0)
 
     if rank == 0:
-        value = args.steps / (ms_max / 1000.0)
+        value = replicas * args.steps / (ms_max / 1000.0)
         line = {
             "metric": "decode tok/s (B=1)", "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
-            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "higher_is_better": True, "scaling": "strong" if tp else "weak",
             "vs_baseline": value / PUBLISHED_TOKS,
             "dtype": "f32 (packed Q4_K/Q6_K weights)",
             "data": "synthetic random-init weights N(0,0.02), seeded prompt ids",
-            "config": {"workload": wl["name"], "model_file": os.path.basename(path), "batch_per_gpu": 1,
+            "config": {"workload": wl["name"], "model_file": os.path.basename(path),
+                       "batch_per_gpu": 1 if not tp else 1.0 / world,
                        "prompt": wl["prompt"], "positions": [pos0, pos0 + args.steps - 1],
-                       "parallelism": f"tensor parallel over {world} GPUs (one sequence)" if world > 1
-                       else "1 GPU",
+                       "parallelism": f"tensor parallel over {world} GPUs (one sequence)" if tp
+                       else (f"data parallel: {world} GPUs, one independent sequence each" if world > 1
+                             else "1 GPU"),
                        "l2": f"weights {wbytes / 1e6:.0f} MB streamed per step > 126 MB L2 (no flush needed)",
                        "vs_baseline_note": "published 8.03 tok/s: reference on 8 laptop cores, real TinyLlama "
                                            "Q4_K_M file"},
-            "e2e": {"value": args.steps / (e2e_ms_max / 1000.0), "unit": "tok/s",
+            "e2e": {"value": replicas * args.steps / (e2e_ms_max / 1000.0), "unit": "tok/s",
                     "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4 * e.vocab_size + 20,
                     "path": "engine_forward (host logits) + host argmax",
                     "same_tokens_as_device_loop": bool(e2e_tokens_match)},
@@ -490,7 +517,7 @@ def main():
                          "duration": "CUDA events around the graph replays of the timed steps, per step",
                          "algorithmic_bytes_per_step": wbytes + kvb,
                          "weight_bytes_per_step": wbytes,
-                         "weight_stream_frac": wbytes / step_s / 1e9 / hbm,
+                         "weight_stream_frac": replicas * wbytes / step_s / 1e9 / hbm,
                          "peak_source": (f"{peak_kind} MEASURED_PEAKS.json hbm_gbs" if peak_kind == "measured"
                                          else "fallback 6.65 TB/s") + (f" x {world} GPUs" if world > 1 else "")},
             "cpu_baseline": base,
