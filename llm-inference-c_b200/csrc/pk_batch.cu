@@ -11,9 +11,9 @@
 //                format on CUDA cores by mv_tile_kernel, which stages the
 //                packed rows in shared memory and decodes each weight once
 //                per 64-vector tile;
-//   elementwise  embedding rows, RMSNorm, RoPE + cache append, attention
-//                (one CTA per head and sequence), residual adds, SwiGLU,
-//                greedy argmax per sequence.
+//   elementwise  embedding rows, residual add + RMSNorm (one kernel), RoPE
+//                + cache append, attention, SwiGLU, greedy argmax per
+//                sequence.
 // The launches of one step are captured once per batch size n in a CUDA
 // graph (inputs and outputs through fixed pinned buffers).
 //
@@ -220,13 +220,25 @@ __global__ void embed_kernel(const uint8_t *embd, uint64_t rb, int type, const i
 }
 
 // out[b] = w * (x[b] / sqrt(mean(x[b]^2) + eps)), as rmsnorm in
-// src/gguf_forward.c (the same rounding steps as the single-sequence step).
-__global__ void rmsnorm_kernel(const float *x, const float *w, int dim, float eps, float *out)
+// src/gguf_forward.c (the same rounding steps as the single-sequence step);
+// with delta != NULL the residual x[b] += delta[b] comes first (and is
+// stored). One CTA per sequence.
+__global__ void __launch_bounds__(1024) rmsnorm_kernel(float *x, const float *delta, const float *w, int dim,
+                                                       float eps, float *out)
 {
     __shared__ float red[32];
-    const float *xb = x + (size_t)blockIdx.x * dim;
+    float *xb = x + (size_t)blockIdx.x * dim;
     float ss = 0.0f;
-    for (int c = threadIdx.x; c < dim; c += blockDim.x) ss = fmaf(xb[c], xb[c], ss);
+    if (delta != nullptr) {
+        const float *db = delta + (size_t)blockIdx.x * dim;
+        for (int c = threadIdx.x; c < dim; c += blockDim.x) {
+            const float v = xb[c] + db[c];
+            xb[c] = v;
+            ss = fmaf(v, v, ss);
+        }
+    } else {
+        for (int c = threadIdx.x; c < dim; c += blockDim.x) ss = fmaf(xb[c], xb[c], ss);
+    }
     const float tot = block_sum(ss, red);
     const float m = __fadd_rn(__fdiv_rn(tot, (float)dim), eps);
     const float sc = __fdiv_rn(1.0f, __fsqrt_rn(m));
@@ -445,11 +457,6 @@ __global__ void __launch_bounds__(512) attention_gqa_kernel(const float *q, cons
     }
 }
 
-__global__ void add_kernel(float *x, const float *y, int count)
-{
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) x[i] += y[i];
-}
-
 // g = silu(g) * u, the reference's rounding steps (src/gguf_forward.c).
 __global__ void swiglu_kernel(float *g, const float *u, int count)
 {
@@ -461,7 +468,7 @@ __global__ void swiglu_kernel(float *g, const float *u, int count)
 
 // Greedy token of sequence b: the largest logit, the lowest index on ties
 // (src/sampler.c:39-52); -1 when a logit is not finite.
-__global__ void argmax_kernel(const float *logits, int vocab, int *next)
+__global__ void __launch_bounds__(1024) argmax_kernel(const float *logits, int vocab, int *next)
 {
     __shared__ float bv[32];
     __shared__ int bi[32], bad[32];
@@ -603,7 +610,8 @@ static int enqueue_step(PkbCtx *b, int n)
                                         b->x);
     const size_t att_smem = (((size_t)m.seq_len + 3) / 4 * 4 + hs + 128 * 4) * 4;
     for (int l = 0; l < L; l++) {
-        bt::rmsnorm_kernel<<<n, 256, 0, st>>>(b->x, b->norms + (size_t)(2 * l) * dim, dim, m.rms_eps, b->xn);
+        if (l == 0)  // later layers: the residual add and this norm at the end of the previous layer
+            bt::rmsnorm_kernel<<<n, 1024, 0, st>>>(b->x, nullptr, b->norms, dim, m.rms_eps, b->xn);
         const PkdTensor *qkv[3] = {&m.wq[l], &m.wk[l], &m.wv[l]};
         float *const qkv_y[3] = {b->q, b->k, b->v};
         if (!bmatmul_group(b, qkv, qkv_y, 3, b->xn, n)) return 0;
@@ -620,18 +628,19 @@ static int enqueue_step(PkbCtx *b, int n)
                                                                              b->att);
         }
         if (!bmatmul(b, m.wo[l], b->att, n, b->tmp)) return 0;
-        bt::add_kernel<<<(n * dim + 255) / 256, 256, 0, st>>>(b->x, b->tmp, n * dim);
-        bt::rmsnorm_kernel<<<n, 256, 0, st>>>(b->x, b->norms + (size_t)(2 * l + 1) * dim, dim, m.rms_eps, b->xn);
+        bt::rmsnorm_kernel<<<n, 1024, 0, st>>>(b->x, b->tmp, b->norms + (size_t)(2 * l + 1) * dim, dim, m.rms_eps,
+                                               b->xn);
         const PkdTensor *gu[2] = {&m.gate[l], &m.up[l]};
         float *const gu_y[2] = {b->g, b->u};
         if (!bmatmul_group(b, gu, gu_y, 2, b->xn, n)) return 0;
         bt::swiglu_kernel<<<ew, 256, 0, st>>>(b->g, b->u, n * hid);
         if (!bmatmul(b, m.down[l], b->g, n, b->tmp)) return 0;
-        bt::add_kernel<<<(n * dim + 255) / 256, 256, 0, st>>>(b->x, b->tmp, n * dim);
+        // x += down, then the next layer's attention norm (the output norm after the last)
+        bt::rmsnorm_kernel<<<n, 1024, 0, st>>>(b->x, b->tmp, b->norms + (size_t)(2 * (l + 1)) * dim, dim,
+                                               m.rms_eps, b->xn);
     }
-    bt::rmsnorm_kernel<<<n, 256, 0, st>>>(b->x, b->norms + (size_t)(2 * L) * dim, dim, m.rms_eps, b->xn);
     if (!bmatmul(b, m.output, b->xn, n, b->logits)) return 0;
-    bt::argmax_kernel<<<n, 256, 0, st>>>(b->logits, m.vocab_size, b->io_d + 3 * B);
+    bt::argmax_kernel<<<n, 1024, 0, st>>>(b->logits, m.vocab_size, b->io_d + 3 * B);
     // the greedy tokens and the matmul error word come back with the step
     cudaMemcpyAsync(b->io_d + 4 * B, b->mm.err, sizeof(int), cudaMemcpyDeviceToDevice, st);
     cudaMemcpyAsync(b->io_h + 3 * B, b->io_d + 3 * B, (B + 1) * sizeof(int), cudaMemcpyDeviceToHost, st);
