@@ -35,11 +35,12 @@ int engine_generate_greedy(LLMModel *model, int token, int pos, int n,
                            int *out_tokens, float *device_ms);
 
 /* Tracing: when the handle was opened with POCKET_CUDA_TRACE=1, copies the
- * device timestamps (ns, %globaltimer, taken by CTA 0) of the last decode
- * step into out and returns how many were written (0 when tracing is off):
- * the step's start, then for each of its 5 * n_layers + 1 phases the time
- * after staging the input vector, after the phase's work and after the
- * grid barrier that ends it. */
+ * device timestamps (ns, %globaltimer) of the last decode step into out and
+ * returns how many were written (0 when tracing is off). First CTA 0's: the
+ * step's start, then for each of its P = 5 * n_layers + 1 phases the time
+ * after staging the input vector, after the phase's work and again at the
+ * phase's end (3P + 1 words). Then, for every CTA b of the step's grid in
+ * order, 2P words: per phase, after staging and after the work. */
 int engine_trace(LLMModel *model, unsigned long long *out, int cap);
 
 /* Message of the last device error of this handle ("" if none). */

@@ -89,9 +89,9 @@ int pkd_forward_greedy(PkdCtx *ctx, int token, int pos);
 int pkd_generate_greedy(PkdCtx *ctx, int token, int pos, int n, int *out, float *device_ms);
 
 /* With POCKET_CUDA_TRACE=1: the %globaltimer stamps (ns) of the last
- * persistent step taken by CTA 0 - its start, then for each phase: after
- * staging x, after the phase's work, after the grid barrier; returns the
- * count. */
+ * persistent step - CTA 0's start, then for each phase: after staging x,
+ * after the phase's work, at the phase's end; then for every CTA and phase:
+ * after staging x, after the work. Returns the count. */
 int pkd_trace(PkdCtx *ctx, unsigned long long *out, int cap);
 
 /* Last device error message ("" if none). */

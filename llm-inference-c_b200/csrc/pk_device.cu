@@ -45,8 +45,9 @@ struct DecodeArgs {
     const float *rope_cs;  // RoPE cos/sin table [position][rope_dim]
     int rope_dim;
     int *err;
-    unsigned long long *trace;  // optional, CTA 0: %globaltimer at start, then per phase: after
-                                //   staging x, after its work, and again at its end
+    unsigned long long *trace;  // optional: CTA 0's %globaltimer at start, then per phase: after
+                                //   staging x, after its work, and again at its end; then
+                                //   for every CTA and phase: after staging x, after its work
 };
 
 __device__ __forceinline__ unsigned long long global_ns()
@@ -73,6 +74,8 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
     const uint32_t tag = a.step != nullptr ? (uint32_t)a.step[4] : 0u;
     const int token = a.step != nullptr ? a.step[0] : 0, pos = a.step != nullptr ? a.step[1] : 0;
     const bool tracing = a.trace != nullptr && blockIdx.x == 0;
+    unsigned long long *ctr =
+        a.trace != nullptr ? a.trace + 3 * nph + 1 + (size_t)blockIdx.x * 2 * nph : nullptr;
 
     Ring r;
     r.bars = reinterpret_cast<uint64_t *>(smem) + warp * a.stages;
@@ -113,7 +116,10 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
                 __syncthreads();  // every warp is done with the previous phase's x
                 if (p.epi == EPI_LOGITS && threadIdx.x == 0) cta_amax[0] = cta_amax[1] = 0ull;
                 stage_x(p, a.step, xq, xg, tag, a.err);  // ends with __syncthreads
-                if (tracing && threadIdx.x == 0) a.trace[3 * pi + 1] = global_ns();
+                if (ctr != nullptr && threadIdx.x == 0) {
+                    ctr[2 * pi] = global_ns();
+                    if (tracing) a.trace[3 * pi + 1] = ctr[2 * pi];
+                }
                 float racc = 0.0f;  // a chunked row's running sum
                 for (int k = 0;; k++) {
                     const int t = tile_at(p, gw, NW, k / p.nchunk);
@@ -158,12 +164,16 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
                         }
                     }
                 }
-            } else if (tracing && threadIdx.x == 0) {
-                a.trace[3 * pi + 1] = global_ns();
+            } else if (ctr != nullptr && threadIdx.x == 0) {
+                ctr[2 * pi] = global_ns();
+                if (tracing) a.trace[3 * pi + 1] = ctr[2 * pi];
             }
         } else if (p.kind == PH_AR) {
             const int items = (p.own[p.rank] + (int)blockDim.x - 1) / (int)blockDim.x;
-            if (tracing && threadIdx.x == 0) a.trace[3 * pi + 1] = global_ns();
+            if (ctr != nullptr && threadIdx.x == 0) {
+                ctr[2 * pi] = global_ns();
+                if (tracing) a.trace[3 * pi + 1] = ctr[2 * pi];
+            }
             for (int it = (blockIdx.x + gridDim.x - p.off % gridDim.x) % gridDim.x; it < items; it += gridDim.x) {
                 ar_item(p, it, a.step, tag, a.err);
             }
@@ -171,16 +181,22 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
             const int n = pos + 1, nh = p.n_kv * p.kv_mul;
             const int span = attn_span(n, p.nsplit_max);
             const int nsplit = (n + span - 1) / span;
-            if (tracing && threadIdx.x == 0) a.trace[3 * pi + 1] = global_ns();
+            if (ctr != nullptr && threadIdx.x == 0) {
+                ctr[2 * pi] = global_ns();
+                if (tracing) a.trace[3 * pi + 1] = ctr[2 * pi];
+            }
             for (int it = (blockIdx.x + gridDim.x - p.off % gridDim.x) % gridDim.x; it < nh * nsplit;
                  it += gridDim.x) {
                 __syncthreads();  // the scratch aliases the previous phase's x
                 attn_item(p, it % nh, it / nh, nsplit, n, span, att, tag, a.err);
             }
         }
-        if (tracing) {
+        if (ctr != nullptr) {
             __syncthreads();
-            if (threadIdx.x == 0) a.trace[3 * pi + 2] = a.trace[3 * pi + 3] = global_ns();
+            if (threadIdx.x == 0) {
+                ctr[2 * pi + 1] = global_ns();
+                if (tracing) a.trace[3 * pi + 2] = a.trace[3 * pi + 3] = ctr[2 * pi + 1];
+            }
         }
     }
     if (lane == 0 && r.issued != r.consumed) ring_drain(r);
@@ -1283,7 +1299,7 @@ static int finalize(PkdCtx *c, char *err, size_t cap)
         return 0;
     }
     if (env_flag("POCKET_CUDA_TRACE", 0) &&
-        cuda_fail(c, cudaMalloc(&c->trace_d, (size_t)(3 * c->nphases + 1) * 8), "cudaMalloc", err, cap)) {
+        cuda_fail(c, cudaMalloc(&c->trace_d, (size_t)(3 * c->nphases + 1 + 2 * c->grid * c->nphases) * 8), "cudaMalloc", err, cap)) {
         return 0;
     }
     unsigned need = 0u;
@@ -1422,7 +1438,8 @@ extern "C" int pkd_generate_greedy(PkdCtx *c, int token, int pos, int n, int *ou
 extern "C" int pkd_trace(PkdCtx *c, unsigned long long *out, int cap)
 {
     if (c == NULL || c->trace_d == NULL || out == NULL) return 0;
-    const int n = 3 * c->nphases + 1 < cap ? 3 * c->nphases + 1 : cap;
+    const int all = 3 * c->nphases + 1 + 2 * c->grid * c->nphases;
+    const int n = all < cap ? all : cap;
     if (cudaMemcpy(out, c->trace_d, (size_t)n * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return 0;
     return n;
 }

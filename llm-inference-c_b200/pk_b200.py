@@ -238,14 +238,21 @@ class Engine:
             raise RuntimeError("engine_generate_greedy failed: " + self.last_error())
         return out[:n], ms.value
 
-    def trace(self):
-        """Per-phase device times (us) of the last step as an array of rows
-        (stage x, work, barrier), or None when tracing is off."""
-        out = np.zeros(4096, dtype=np.uint64)
+    def trace(self, all_ctas=False):
+        """Per-phase device times (us) of the last step, or None when tracing
+        is off. CTA 0's rows (stage x, work, 0); with all_ctas, an array
+        [cta][phase][2] of (after staging, after work) in us from CTA 0's
+        start instead."""
+        nph = 5 * self.config["n_layers"] + 1
+        out = np.zeros(3 * nph + 1 + 2 * 1024 * nph, dtype=np.uint64)
         n = lib().engine_trace(self.h, out.ctypes.data, out.size)
         if n <= 1:
             return None
-        d = np.diff(out[:n].astype(np.float64)) / 1000.0
+        head = out[:3 * nph + 1].astype(np.float64)
+        if all_ctas:
+            rest = out[3 * nph + 1:n].astype(np.float64)
+            return ((rest - head[0]) / 1000.0).reshape(-1, nph, 2)
+        d = np.diff(head) / 1000.0
         return d[: (len(d) // 3) * 3].reshape(-1, 3)
 
     def description(self):
