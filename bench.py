@@ -83,10 +83,14 @@ def ensure_model(preset, rank, barrier):
     return path
 
 
-def kv_bytes_per_step(cfg, positions):
+def kv_bytes_per_step(cfg, positions, entry_bytes=4):
     kvd = cfg["dim"] // cfg["n_heads"] * cfg["n_kv_heads"]
     # K and V read for positions 0..pos, plus the K/V row written
-    return sum(2 * cfg["n_layers"] * (p + 2) * kvd * 4 for p in positions) / len(positions)
+    return sum(2 * cfg["n_layers"] * (p + 2) * kvd * entry_bytes for p in positions) / len(positions)
+
+
+def kv_entry_bytes():
+    return 2 if os.environ.get("POCKET_CUDA_KV") == "f16" else 4
 
 
 class ClockSampler:
@@ -326,7 +330,7 @@ def run_b64(path, args, cfg, device=0, barrier=lambda: None):
     barrier()
     e.close()
     wbytes = pk_synth.weight_bytes_per_token(WORKLOADS["tinyllama"]["preset"])
-    kvb = kv_bytes_per_step(cfg, list(range(C + W, C + W + K))) * B
+    kvb = kv_bytes_per_step(cfg, list(range(C + W, C + W + K)), kv_entry_bytes()) * B
     step_s = dt / K
     hbm, peak_kind = peaks()
     achieved = (wbytes + kvb) / step_s / 1e9
@@ -335,6 +339,7 @@ def run_b64(path, args, cfg, device=0, barrier=lambda: None):
             "ms_per_step": step_s * 1e3,
             "config": {"workload": "TinyLlama-1.1B-arch Q4_K_M, 64 independent sequences, greedy decode",
                        "context_per_sequence": [C + W, C + W + K - 1],
+                       "kv_cache": "f16" if kv_entry_bytes() == 2 else "f32",
                        "context_fill": f"{C} seeded random tokens per sequence decoded through "
                                        f"engine_forward_batch ({fill_s:.1f} s, untimed)"},
             "path": "engine_forward_batch: Q4_K matrices on the tcgen05 tensor-core matmul, Q6_K on the "
@@ -358,10 +363,13 @@ def main():
     ap.add_argument("--only", default=None, help="matvec workload: one TYPE:ROWSxCOLS case")
     ap.add_argument("--b64-steps", type=int, default=32, help="timed steps of the B=64 batched decode (0: skip)")
     ap.add_argument("--b64-context", type=int, default=512, help="tokens decoded into each sequence's KV cache first")
+    ap.add_argument("--kv", default="f32", choices=["f32", "f16"],
+                    help="KV cache entries (f16: the half cache option, POCKET_CUDA_KV)")
     ap.add_argument("--tp", action="store_true",
                     help="N > 1 on the TinyLlama shape: one sequence tensor-parallel instead of one per GPU")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    os.environ["POCKET_CUDA_KV"] = args.kv
 
     if args.workload == "matvec":
         return run_matvec_sweep(args)
@@ -460,7 +468,7 @@ def main():
     hbm = hbm1 * world  # the N GPUs' HBM together
     wbytes = pk_synth.weight_bytes_per_token(wl["preset"])
     positions = list(range(pos0, pos0 + args.steps))
-    kvb = kv_bytes_per_step(cfg, positions)
+    kvb = kv_bytes_per_step(cfg, positions, kv_entry_bytes())
     step_s = ms_max / 1000.0 / args.steps
     replicas = 1 if tp else world  # sequences decoded at once, each streaming all weights
     achieved = replicas * (wbytes + kvb) / step_s / 1e9
@@ -501,6 +509,7 @@ def main():
             "config": {"workload": wl["name"], "model_file": os.path.basename(path),
                        "batch_per_gpu": 1 if not tp else 1.0 / world,
                        "prompt": wl["prompt"], "positions": [pos0, pos0 + args.steps - 1],
+                       "kv_cache": args.kv,
                        "parallelism": f"tensor parallel over {world} GPUs (one sequence)" if tp
                        else (f"data parallel: {world} GPUs, one independent sequence each" if world > 1
                              else "1 GPU"),

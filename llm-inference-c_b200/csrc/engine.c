@@ -107,6 +107,7 @@ struct LLMModel {
     int tp_world;      /* tensor-parallel ranks (1: single GPU) */
     int connected;     /* the decode step exists (tensor parallel: after engine_tp_connect) */
     int batch_seqs;    /* sequences of the batched state */
+    int kv_half;       /* KV cache entries in IEEE half (POCKET_CUDA_KV=f16) */
     char last_error[256];
 };
 
@@ -602,6 +603,16 @@ static int env_device(void)
     return (s != NULL && *s) ? atoi(s) : 0;
 }
 
+/* KV cache entry type from POCKET_CUDA_KV: unset, "" or "f32" -> float (0),
+ * "f16" -> IEEE half (1), anything else -> -1 (the open fails). */
+static int env_kv_half(void)
+{
+    const char *s = getenv("POCKET_CUDA_KV");
+    if (s == NULL || *s == '\0' || strcmp(s, "f32") == 0) return 0;
+    if (strcmp(s, "f16") == 0) return 1;
+    return -1;
+}
+
 void engine_close(LLMModel *m)
 {
     if (m == NULL) return;
@@ -619,6 +630,11 @@ static LLMModel *open_impl(const LLMOptions *o, int device, int rank, int world,
     }
     if (o->max_context < 0) {
         seterr(err, cap, "Context size must be positive.");
+        return NULL;
+    }
+    const int kv_half = env_kv_half();
+    if (kv_half < 0) {
+        seterr(err, cap, "POCKET_CUDA_KV must be f32 or f16.");
         return NULL;
     }
     const int fd = open(o->model_path, O_RDONLY);
@@ -658,6 +674,7 @@ static LLMModel *open_impl(const LLMOptions *o, int device, int rank, int world,
         return NULL;
     }
     m->format = LLM_FORMAT_GGUF;
+    m->kv_half = kv_half;
     if (!parse(&p, err, cap)) goto fail;
     if (find(&p, "rope_freqs.weight") != NULL) {
         seterr(err, cap, "Model uses RoPE frequency factors (rope_freqs.weight, Llama 3.1 style), which are not supported.");
@@ -820,6 +837,7 @@ static LLMModel *open_impl(const LLMOptions *o, int device, int rank, int world,
         dm.rope_dim = c->rope_dim;
         dm.rms_eps = c->rms_norm_eps;
         dm.att_scale = 1.0f / sqrtf((float)hs);
+        dm.kv_half = m->kv_half;
         dm.embd = b[0].dev;
         dm.output_norm = b[1].dev;
         dm.output = b[2].dev;
@@ -1027,7 +1045,7 @@ size_t engine_kv_cache_bytes(const LLMModel *m)
     const Config *c = engine_config(m);
     if (c == NULL) return 0;
     const size_t kvd = (size_t)(c->dim / c->n_heads * c->n_kv_heads);
-    return 2u * (size_t)c->n_layers * (size_t)c->seq_len * kvd * sizeof(float);
+    return 2u * (size_t)c->n_layers * (size_t)c->seq_len * kvd * (m->kv_half ? 2u : sizeof(float));
 }
 
 const char *engine_description(const LLMModel *m)

@@ -248,10 +248,12 @@ __global__ void __launch_bounds__(1024) rmsnorm_kernel(float *x, const float *de
 
 // RoPE on q and k of sequence b at its position (pairs (2i, 2i + 1) of each
 // head, cos/sin from the reference's table), then k and v appended to the
-// sequence's cache (src/gguf_forward.c:50-66 and the cache writes).
+// sequence's cache (src/gguf_forward.c:50-66 and the cache writes; a half
+// cache rounds each entry to nearest even).
+template <typename KV>
 __global__ void rope_cache_kernel(float *q, const float *k, const float *v, const float *rope_cs, int rope_dim,
                                   int hs, int qd, int kvd, const int *io, int bmax, int layer, int L, int seq_len,
-                                  float *kc, float *vc)
+                                  KV *kc, KV *vc)
 {
     const int b = blockIdx.x;
     const int pos = io[bmax + b], seq = io[2 * bmax + b];
@@ -277,10 +279,10 @@ __global__ void rope_cache_kernel(float *q, const float *k, const float *v, cons
             v0 = r0;
             v1 = r1;
         }
-        kc[row + 2 * p] = v0;
-        kc[row + 2 * p + 1] = v1;
-        vc[row + 2 * p] = vb[2 * p];
-        vc[row + 2 * p + 1] = vb[2 * p + 1];
+        kv_store(kc, row + 2 * p, v0);
+        kv_store(kc, row + 2 * p + 1, v1);
+        kv_store(vc, row + 2 * p, vb[2 * p]);
+        kv_store(vc, row + 2 * p + 1, vb[2 * p + 1]);
     }
 }
 
@@ -291,7 +293,8 @@ __global__ void rope_cache_kernel(float *q, const float *k, const float *v, cons
 // for the weighted sum thread (g, d4) adds float4 d4 of the values of the
 // positions t = g mod G, and the G partial sums are added in order.
 // 128 threads; hs a multiple of 4, at most 256.
-__global__ void __launch_bounds__(128) attention_kernel(const float *q, const float *kc, const float *vc,
+template <typename KV>
+__global__ void __launch_bounds__(128) attention_kernel(const float *q, const KV *kc, const KV *vc,
                                                         const int *io, int bmax, int layer, int L, int seq_len,
                                                         int hs, int qd, int kvd, int kv_mul, float scale, float *out)
 {
@@ -308,10 +311,10 @@ __global__ void __launch_bounds__(128) attention_kernel(const float *q, const fl
     const float4 *q4 = reinterpret_cast<const float4 *>(qs);
     float m = -INFINITY;
     for (int t = tid; t < P; t += blockDim.x) {
-        const float4 *kt = reinterpret_cast<const float4 *>(kc + base + (size_t)t * kvd);
+        const KV *kt = kc + base + (size_t)t * kvd;
         float dot = 0.0f;
         for (int i = 0; i < F4; i++) {
-            const float4 kv = kt[i], qv = q4[i];
+            const float4 kv = kv_load4(kt, 4 * (size_t)i), qv = q4[i];
             dot = fmaf(qv.x, kv.x, dot);
             dot = fmaf(qv.y, kv.y, dot);
             dot = fmaf(qv.z, kv.z, dot);
@@ -335,11 +338,10 @@ __global__ void __launch_bounds__(128) attention_kernel(const float *q, const fl
     const int G = blockDim.x / F4, g = tid / F4, d4 = tid - g * F4;
     float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     if (g < G) {
-        const float4 *vb = reinterpret_cast<const float4 *>(vc + base) + d4;
-        const size_t stride = (size_t)(kvd >> 2);
+        const KV *vb = vc + base + 4 * d4;
 #pragma unroll 4
         for (int t = g; t < P; t += G) {
-            const float4 vv = vb[(size_t)t * stride];
+            const float4 vv = kv_load4(vb, (size_t)t * kvd);
             const float pt = sc[t];
             o.x = fmaf(pt, vv.x, o.x);
             o.y = fmaf(pt, vv.y, o.y);
@@ -369,7 +371,8 @@ __global__ void __launch_bounds__(128) attention_kernel(const float *q, const fl
 // w, w + 16, ...; weighted sum: thread (tg, h, d4) adds float4 d4 of the
 // value rows t = tg mod G times p_h, and the G partials are added in order.
 // 512 threads; H * hs / 4 <= 128.
-__global__ void __launch_bounds__(512) attention_gqa_kernel(const float *q, const float *kc, const float *vc,
+template <typename KV>
+__global__ void __launch_bounds__(512) attention_gqa_kernel(const float *q, const KV *kc, const KV *vc,
                                                             const int *io, int bmax, int layer, int L, int seq_len,
                                                             int hs, int qd, int kvd, int H, float scale, float *out)
 {
@@ -383,12 +386,12 @@ __global__ void __launch_bounds__(512) attention_gqa_kernel(const float *q, cons
     const size_t base = ((size_t)seq * L + layer) * seq_len * kvd + (size_t)g * hs;
     const float4 *q4 = reinterpret_cast<const float4 *>(qs);
     for (int t = tid; t < P; t += blockDim.x) {
-        const float4 *kt = reinterpret_cast<const float4 *>(kc + base + (size_t)t * kvd);
+        const KV *kt = kc + base + (size_t)t * kvd;
         float dot[8];
 #pragma unroll
         for (int h = 0; h < 8; h++) dot[h] = 0.0f;
         for (int i = 0; i < F4; i++) {
-            const float4 kv = kt[i];
+            const float4 kv = kv_load4(kt, 4 * (size_t)i);
 #pragma unroll
             for (int h = 0; h < 8; h++) {
                 if (h < H) {
@@ -427,13 +430,12 @@ __global__ void __launch_bounds__(512) attention_gqa_kernel(const float *q, cons
     const int tg = tid / HF, hd = tid - tg * HF, h = hd / F4, d4 = hd - h * F4;
     float4 *part = reinterpret_cast<float4 *>(sc + H * sl);
     if (tg < G) {
-        const float4 *vb = reinterpret_cast<const float4 *>(vc + base) + d4;
+        const KV *vb = vc + base + 4 * d4;
         const float *ph = sc + h * sl;
-        const size_t stride = (size_t)(kvd >> 2);
         float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll 4
         for (int t = tg; t < P; t += G) {
-            const float4 vv = vb[(size_t)t * stride];
+            const float4 vv = kv_load4(vb, (size_t)t * kvd);
             const float pt = ph[t];
             o.x = fmaf(pt, vv.x, o.x);
             o.y = fmaf(pt, vv.y, o.y);
@@ -523,7 +525,7 @@ struct PkbCtx {
     PkdModel m;  // tensor tables owned by the PkdCtx
     const uint8_t *arena;
     const float *norms, *rope_cs;
-    float *kc, *vc;                                           // [max_seqs][L][seq_len][kvd]
+    void *kc, *vc;                                            // [max_seqs][L][seq_len][kvd], float or half
     float *x, *xn, *q, *k, *v, *att, *tmp, *g, *u, *logits;  // [64][width]
     float *part;                                              // split-K partial sums of mv_tile_kernel
     int *io_d, *io_h;  // [tokens 64][pos 64][seq 64][next 64][error word]
@@ -599,10 +601,29 @@ static int bmatmul_group(PkbCtx *b, const PkdTensor *const *ts, float *const *ys
 }
 
 // The launches of one step for n sequences (inputs already in io_d).
+// Layer l's KV append (after RoPE) and attention for the n rows of a step,
+// over a cache of KV entries (float or half).
+template <typename KV>
+static void attend(PkbCtx *b, int l, int n, size_t att_smem, KV *kc, KV *vc)
+{
+    const PkdModel &m = b->m;
+    const int hs = m.head_size, qd = m.n_heads * hs, kvd = m.n_kv_heads * hs, L = m.n_layers, B = bt::BMAX;
+    cudaStream_t st = b->st;
+    bt::rope_cache_kernel<KV><<<n, 256, 0, st>>>(b->q, b->k, b->v, b->rope_cs, m.rope_dim, hs, qd, kvd, b->io_d, B,
+                                                 l, L, m.seq_len, kc, vc);
+    if (b->gqa_smem > 0) {
+        bt::attention_gqa_kernel<KV><<<dim3(m.n_kv_heads, n), 512, b->gqa_smem, st>>>(
+            b->q, kc, vc, b->io_d, B, l, L, m.seq_len, hs, qd, kvd, m.n_heads / m.n_kv_heads, m.att_scale, b->att);
+    } else {
+        bt::attention_kernel<KV><<<dim3(m.n_heads, n), 128, att_smem, st>>>(
+            b->q, kc, vc, b->io_d, B, l, L, m.seq_len, hs, qd, kvd, m.n_heads / m.n_kv_heads, m.att_scale, b->att);
+    }
+}
+
 static int enqueue_step(PkbCtx *b, int n)
 {
     const PkdModel &m = b->m;
-    const int dim = m.dim, hs = m.head_size, qd = m.n_heads * hs, kvd = m.n_kv_heads * hs, hid = m.hidden_dim;
+    const int dim = m.dim, hs = m.head_size, hid = m.hidden_dim;
     const int L = m.n_layers, B = bt::BMAX;
     cudaStream_t st = b->st;
     const int ew = (n * (hid > dim ? hid : dim) + 255) / 256;
@@ -615,17 +636,10 @@ static int enqueue_step(PkbCtx *b, int n)
         const PkdTensor *qkv[3] = {&m.wq[l], &m.wk[l], &m.wv[l]};
         float *const qkv_y[3] = {b->q, b->k, b->v};
         if (!bmatmul_group(b, qkv, qkv_y, 3, b->xn, n)) return 0;
-        bt::rope_cache_kernel<<<n, 256, 0, st>>>(b->q, b->k, b->v, b->rope_cs, m.rope_dim, hs, qd, kvd, b->io_d, B, l,
-                                                 L, m.seq_len, b->kc, b->vc);
-        if (b->gqa_smem > 0) {
-            bt::attention_gqa_kernel<<<dim3(m.n_kv_heads, n), 512, b->gqa_smem, st>>>(
-                b->q, b->kc, b->vc, b->io_d, B, l, L, m.seq_len, hs, qd, kvd, m.n_heads / m.n_kv_heads, m.att_scale,
-                b->att);
+        if (m.kv_half) {
+            attend(b, l, n, att_smem, static_cast<__half *>(b->kc), static_cast<__half *>(b->vc));
         } else {
-            bt::attention_kernel<<<dim3(m.n_heads, n), 128, att_smem, st>>>(b->q, b->kc, b->vc, b->io_d, B, l, L,
-                                                                             m.seq_len, hs, qd, kvd,
-                                                                             m.n_heads / m.n_kv_heads, m.att_scale,
-                                                                             b->att);
+            attend(b, l, n, att_smem, static_cast<float *>(b->kc), static_cast<float *>(b->vc));
         }
         if (!bmatmul(b, m.wo[l], b->att, n, b->tmp)) return 0;
         bt::rmsnorm_kernel<<<n, 1024, 0, st>>>(b->x, b->tmp, b->norms + (size_t)(2 * l + 1) * dim, dim, m.rms_eps,
@@ -678,7 +692,7 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
     cudaSetDevice(b->device);
     cudaDeviceGetAttribute(&b->sms, cudaDevAttrMultiProcessorCount, b->device);
     const int B = bt::BMAX, dim = m.dim, hs = m.head_size, qd = m.n_heads * hs, kvd = m.n_kv_heads * hs;
-    const size_t cache = (size_t)max_seqs * m.n_layers * m.seq_len * kvd;
+    const size_t cache = (size_t)max_seqs * m.n_layers * m.seq_len * kvd * (m.kv_half ? 2 : 4);  // bytes
     // matmul scratch: the largest need over the model's Q4_K launches at
     // n = 64 (Q/K/V and gate/up each one launch of their Q4_K matrices)
     PkMmNeed mx = {0, 0, 0, 0, 0};
@@ -713,8 +727,8 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
     b->mm.smem_max = pk_mm_smem_max(b->device);
     int ok = b->mm.smem_max > 0 || mx.xs == 0;
     if (!ok) snprintf(b->msg, sizeof(b->msg), "The tensor-core matmul cannot run on this device.");
-    ok = ok && !bfail(b, cudaMalloc(&b->kc, cache * 4), "cudaMalloc(batched KV cache)") &&
-         !bfail(b, cudaMalloc(&b->vc, cache * 4), "cudaMalloc(batched KV cache)") &&
+    ok = ok && !bfail(b, cudaMalloc(&b->kc, cache), "cudaMalloc(batched KV cache)") &&
+         !bfail(b, cudaMalloc(&b->vc, cache), "cudaMalloc(batched KV cache)") &&
          !bfail(b, cudaMalloc(&b->x, (size_t)B * dim * 4), "cudaMalloc") &&
          !bfail(b, cudaMalloc(&b->xn, (size_t)B * dim * 4), "cudaMalloc") &&
          !bfail(b, cudaMalloc(&b->tmp, (size_t)B * dim * 4), "cudaMalloc") &&
@@ -736,8 +750,8 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
          !bfail(b, cudaMalloc(&b->mm.err, 16), "cudaMalloc") &&
          !bfail(b, cudaMemsetAsync(b->mm.arrived, 0, mx.arrived + 16, b->st), "cudaMemset") &&
          !bfail(b, cudaMemsetAsync(b->mm.err, 0, 16, b->st), "cudaMemset") &&
-         !bfail(b, cudaMemsetAsync(b->kc, 0, cache * 4, b->st), "cudaMemset") &&
-         !bfail(b, cudaMemsetAsync(b->vc, 0, cache * 4, b->st), "cudaMemset");
+         !bfail(b, cudaMemsetAsync(b->kc, 0, cache, b->st), "cudaMemset") &&
+         !bfail(b, cudaMemsetAsync(b->vc, 0, cache, b->st), "cudaMemset");
 #define PKB_ATTR(T)                                                                                           \
     ok = ok && !bfail(b, cudaFuncSetAttribute(bt::mv_tile_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                               bt::mv_smem<T>()),                                              \
@@ -752,7 +766,10 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
 #undef PKB_ATTR
     const size_t att_smem = (((size_t)m.seq_len + 3) / 4 * 4 + hs + 128 * 4) * 4;
     if (ok && att_smem > 48 * 1024)
-        ok = !bfail(b, cudaFuncSetAttribute(bt::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        ok = !bfail(b, cudaFuncSetAttribute(bt::attention_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)att_smem),
+                    "cudaFuncSetAttribute") &&
+             !bfail(b, cudaFuncSetAttribute(bt::attention_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             (int)att_smem),
                     "cudaFuncSetAttribute");
     // grouped attention when a CTA can hold the group's queries and scores
@@ -761,8 +778,11 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
         const int H = m.n_heads / m.n_kv_heads;
         const size_t gs = ((size_t)H * hs + (size_t)H * ((m.seq_len + 3) / 4 * 4)) * 4 + 512 * 16;
         if (ok && H >= 2 && H <= 8 && H * (hs / 4) >= 64 && H * (hs / 4) <= 128 && gs <= 200 * 1024) {
-            ok = !bfail(b, cudaFuncSetAttribute(bt::attention_gqa_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                (int)gs),
+            ok = !bfail(b, cudaFuncSetAttribute(bt::attention_gqa_kernel<float>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gs),
+                        "cudaFuncSetAttribute") &&
+                 !bfail(b, cudaFuncSetAttribute(bt::attention_gqa_kernel<__half>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gs),
                         "cudaFuncSetAttribute");
             b->gqa_smem = (int)gs;
         }

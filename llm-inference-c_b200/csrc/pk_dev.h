@@ -50,6 +50,7 @@ typedef struct {
     const PkdTensor *attn_norm, *ffn_norm;                  /* n_layers each, decoded on the device */
     PkdTensor output_norm;
     const float *rope_cs;       /* host: seq_len * rope_dim floats, (cos, sin) pairs */
+    int kv_half;                /* KV cache entries: IEEE half (1) or float (0) */
 } PkdModel;
 
 typedef struct PkdCtx PkdCtx;

@@ -797,7 +797,8 @@ struct PkdCtx {
     uint64_t arena_bytes;
     void *staging;  // pinned upload staging
     // run state
-    float *logits, *kc, *vc, *part, *norms, *rope_cs;
+    float *logits, *part, *norms, *rope_cs;
+    void *kc, *vc;  // KV cache: float entries, or half with model.kv_half
     uint64_t *ll;  // tagged activations, per layer: q, k, v, attention out, x after Wo, gate and up, x after down
     int rope_dim;
     unsigned *count;
@@ -999,6 +1000,7 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total, int cap)
         qkv.v_ll = ll + lp.v;
         qkv.kc = c->kc;
         qkv.vc = c->vc;
+        qkv.kv_half = m->kv_half;
         qkv.hs = hs;
         qkv.rope_dim = m->rope_dim;
         qkv.kv_dim = kvd;
@@ -1015,6 +1017,7 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total, int cap)
         att.aout_ll = ll + lp.att;
         att.kc = c->kc;
         att.vc = c->vc;
+        att.kv_half = m->kv_half;
         att.part = c->part;
         att.count = c->count + (size_t)l * tp.q_heads;
         att.layer = l;
@@ -1166,9 +1169,9 @@ static int finalize(PkdCtx *c, char *err, size_t cap);
 extern "C" int pkd_build(PkdCtx *c, const PkdModel *m, char *err, size_t cap)
 {
     const size_t dim = (size_t)m->dim, hs = (size_t)m->head_size, kvd = hs * (size_t)m->n_kv_heads;
-    const size_t cache = (size_t)m->n_layers * (size_t)m->seq_len * kvd;
+    const size_t cache = (size_t)m->n_layers * (size_t)m->seq_len * kvd * (m->kv_half ? 2 : 4);  // bytes
     const size_t nnorm = (2 * (size_t)m->n_layers + 1) * dim;
-    if ((size_t)m->rope_dim > hs || hs % 4 || hs > 256 || hs * (size_t)m->tp.q_heads > dim) {
+    if ((size_t)m->rope_dim > hs || hs % (m->kv_half ? 8 : 4) || hs > 256 || hs * (size_t)m->tp.q_heads > dim) {
         if (err && cap) snprintf(err, cap, "Unsupported model shape.");
         return 0;
     }
@@ -1177,8 +1180,8 @@ extern "C" int pkd_build(PkdCtx *c, const PkdModel *m, char *err, size_t cap)
     const size_t part = (size_t)m->n_heads * nsplit * (hs + 2);
     const LLPlan lp = ll_plan(m);
     if (cuda_fail(c, cudaMalloc(&c->ll, lp.total * 8), "cudaMalloc", err, cap) ||
-        cuda_fail(c, cudaMalloc(&c->kc, cache * 4), "cudaMalloc(KV cache)", err, cap) ||
-        cuda_fail(c, cudaMalloc(&c->vc, cache * 4), "cudaMalloc(KV cache)", err, cap) ||
+        cuda_fail(c, cudaMalloc(&c->kc, cache), "cudaMalloc(KV cache)", err, cap) ||
+        cuda_fail(c, cudaMalloc(&c->vc, cache), "cudaMalloc(KV cache)", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->part, part * 4), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->norms, nnorm * 4), "cudaMalloc", err, cap) ||
         cuda_fail(c, cudaMalloc(&c->rope_cs, (size_t)m->seq_len * m->rope_dim * 4 + 4), "cudaMalloc", err, cap) ||
@@ -1201,8 +1204,8 @@ extern "C" int pkd_build(PkdCtx *c, const PkdModel *m, char *err, size_t cap)
     c->tp = m->tp;
     c->peers[m->tp.rank] = c->ll;
     cudaStream_t st = c->stream;
-    cudaMemsetAsync(c->kc, 0, cache * 4, st);
-    cudaMemsetAsync(c->vc, 0, cache * 4, st);
+    cudaMemsetAsync(c->kc, 0, cache, st);
+    cudaMemsetAsync(c->vc, 0, cache, st);
     cudaMemsetAsync(c->count, 0, (size_t)m->n_layers * m->n_heads * 4, st);
     cudaMemsetAsync(c->lcount, 0, 16, st);
     cudaMemsetAsync(c->err_d, 0, 16, st);

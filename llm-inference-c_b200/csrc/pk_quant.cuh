@@ -523,4 +523,47 @@ __device__ __forceinline__ float unit_float(int t, const uint8_t *row, int u, in
     return s;
 }
 
+// ------------------------------------------------------------------ //
+// KV cache entries: float, or IEEE half (round to nearest even on the //
+// append, exact widening on the read)                                //
+// ------------------------------------------------------------------ //
+
+__device__ __forceinline__ float kv_load(const float *p, size_t i)
+{
+    return p[i];
+}
+__device__ __forceinline__ float kv_load(const __half *p, size_t i)
+{
+    return __half2float(p[i]);
+}
+__device__ __forceinline__ void kv_store(float *p, size_t i, float v)
+{
+    p[i] = v;
+}
+__device__ __forceinline__ void kv_store(__half *p, size_t i, float v)
+{
+    p[i] = __float2half_rn(v);
+}
+// The value an entry holds once stored.
+__device__ __forceinline__ float kv_round(const float *, float v)
+{
+    return v;
+}
+__device__ __forceinline__ float kv_round(const __half *, float v)
+{
+    return __half2float(__float2half_rn(v));
+}
+// Entries i .. i+3 (i a multiple of 4) as a float4: one 16- or 8-byte load.
+__device__ __forceinline__ float4 kv_load4(const float *p, size_t i)
+{
+    return *reinterpret_cast<const float4 *>(p + i);
+}
+__device__ __forceinline__ float4 kv_load4(const __half *p, size_t i)
+{
+    const uint2 u = *reinterpret_cast<const uint2 *>(p + i);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+
 }  // namespace pk

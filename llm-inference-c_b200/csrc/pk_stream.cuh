@@ -270,7 +270,8 @@ struct Phase {
     uint64_t embd_rb;         //   and the residual of layer 0's EPI_ADD)
     int embd_type;
     uint64_t *q_ll, *k_ll, *v_ll;  // EPI_QKV outputs (tagged)
-    float *kc, *vc;                // KV cache (EPI_QKV appends, attention reads)
+    void *kc, *vc;                 // KV cache (EPI_QKV appends, attention reads):
+    int kv_half;                   //   float entries, or IEEE half when kv_half
     int hs, rope_dim, kv_dim, seq_len, layer;
     unsigned long long *amax;  // EPI_LOGITS: [0] packed argmax, [1] non-finite flag
     // attention
@@ -716,7 +717,12 @@ __device__ __forceinline__ void run_tile(const Phase &p, int t, int chunk, const
             } else {
                 // the cache row serves later steps; this step reads the tagged copy
                 const size_t cache_row = ((size_t)p.layer * p.seq_len + pos) * p.kv_dim;
-                (s.kind == KIND_K ? p.kc : p.vc)[cache_row + r] = v;
+                void *cache = s.kind == KIND_K ? p.kc : p.vc;
+                if (p.kv_half) {
+                    kv_store(static_cast<__half *>(cache), cache_row + r, v);
+                } else {
+                    kv_store(static_cast<float *>(cache), cache_row + r, v);
+                }
                 st_ll((s.kind == KIND_K ? p.k_ll : p.v_ll) + r, v, tag);
             }
         }
@@ -833,7 +839,7 @@ __host__ __device__ inline int attn_scratch_floats(int hs, int nwarps)
     return 3 * hs + 4 * T * hs + T + 2 * nwarps;
 }
 
-__device__ __forceinline__ void cp_async16(float *dst, const float *src)
+__device__ __forceinline__ void cp_async16(void *dst, const void *src)
 {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
@@ -848,11 +854,14 @@ __device__ __forceinline__ void cp_async16(float *dst, const float *src)
 // writes the head's output; otherwise the last split to finish (per-head
 // counter) merges the splits' (max, sum, output) in split order. q and this
 // position's K/V row are tagged words (the QKV phase of the same step wrote
-// them); earlier positions come from the KV cache. All threads of the CTA
+// them; with a half cache they are rounded to half as the cache holds
+// them); earlier positions come from the KV cache (KV: float or __half
+// entries, widened to float exactly on the read). All threads of the CTA
 // (blockDim.x >= 256, a multiple of 32: threads beyond the first 256 take
 // no position when scoring).
-__device__ __forceinline__ void attn_item(const Phase &p, int h, int s, int nsplit, int n, int span, float *sm,
-                                          uint32_t tag, int *err)
+template <typename KV>
+__device__ __forceinline__ void attn_item_t(const Phase &p, int h, int s, int nsplit, int n, int span, float *sm,
+                                            uint32_t tag, int *err)
 {
     const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
     const int hs = p.hs, hs4 = hs >> 2, kvd = p.kv_dim, g = h / p.kv_mul;
@@ -861,33 +870,40 @@ __device__ __forceinline__ void attn_item(const Phase &p, int h, int s, int nspl
     float *qs = sm;                // hs
     float *kcur = qs + hs;         // hs: K row of this step
     float *vcur = kcur + hs;       // hs: V row of this step
-    float *Kt = vcur + hs;         // 2 x T x hs
-    float *Vt = Kt + 2 * T * hs;   // 2 x T x hs
-    float *pt = Vt + 2 * T * hs;   // T probabilities
+    KV *Kt = reinterpret_cast<KV *>(vcur + hs);         // 2 x T x hs (room for floats)
+    KV *Vt = reinterpret_cast<KV *>(vcur + hs + 2 * T * hs);  // 2 x T x hs
+    float *pt = vcur + hs + 4 * T * hs;  // T probabilities
     float *red = pt + T;           // 2 x nw
     __shared__ int last_sh;
 
     const bool has_cur = t1 == n;  // the item covers this step's position
+    const KV *kc0 = static_cast<const KV *>(p.kc);
     for (int i = tid; i < hs; i += nt) {
         qs[i] = ll_read(p.aq_ll + (size_t)h * hs + i, tag, err);
         if (has_cur) {
-            kcur[i] = ll_read(p.ak_ll + (size_t)g * hs + i, tag, err);
-            vcur[i] = ll_read(p.av_ll + (size_t)g * hs + i, tag, err);
+            // this step's row as the cache holds it
+            kcur[i] = kv_round(kc0, ll_read(p.ak_ll + (size_t)g * hs + i, tag, err));
+            vcur[i] = kv_round(kc0, ll_read(p.av_ll + (size_t)g * hs + i, tag, err));
         }
     }
     __syncthreads();
 
     const size_t lbase = (size_t)p.layer * p.seq_len * kvd + (size_t)g * hs;
-    const float *kc = p.kc + lbase, *vc = p.vc + lbase;
+    const KV *kc = static_cast<const KV *>(p.kc) + lbase, *vc = static_cast<const KV *>(p.vc) + lbase;
     const int ntile = (t1 - t0 + T - 1) / T;
+    constexpr int E16 = 16 / (int)sizeof(KV);  // entries per 16-byte copy
+    const int hsc = hs / E16;
     auto load_tile = [&](int k, int buf) {
         const int tb = t0 + k * T, tc = min(T, t1 - tb);
-        float *K = Kt + buf * T * hs, *V = Vt + buf * T * hs;
-        for (int i = tid; i < tc * hs4; i += nt) {
-            const int r = i / hs4, c = (i - r * hs4) * 4;
+        KV *K = Kt + buf * T * hs, *V = Vt + buf * T * hs;
+        for (int i = tid; i < tc * hsc; i += nt) {
+            const int r = i / hsc, c = (i - r * hsc) * E16;
             if (tb + r == n - 1) {
-                *reinterpret_cast<float4 *>(K + r * hs + c) = *reinterpret_cast<const float4 *>(kcur + c);
-                *reinterpret_cast<float4 *>(V + r * hs + c) = *reinterpret_cast<const float4 *>(vcur + c);
+#pragma unroll
+                for (int e = 0; e < E16; e++) {
+                    kv_store(K, (size_t)r * hs + c + e, kcur[c + e]);
+                    kv_store(V, (size_t)r * hs + c + e, vcur[c + e]);
+                }
             } else {
                 cp_async16(K + r * hs + c, kc + (size_t)(tb + r) * kvd + c);
                 cp_async16(V + r * hs + c, vc + (size_t)(tb + r) * kvd + c);
@@ -909,14 +925,13 @@ __device__ __forceinline__ void attn_item(const Phase &p, int h, int s, int nspl
             asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();
-        const float *K = Kt + buf * T * hs, *V = Vt + buf * T * hs;
+        const KV *K = Kt + buf * T * hs, *V = Vt + buf * T * hs;
         // scores: tpp threads per position, float4 slices i, i + tpp, ...
         float acc = 0.0f;
         if (pr < tc) {  // pr >= T for threads beyond the first 256, and tc <= T
-            const float4 *k4 = reinterpret_cast<const float4 *>(K + pr * hs);
             const float4 *q4 = reinterpret_cast<const float4 *>(qs);
             for (int d4 = pi; d4 < hs4; d4 += tpp) {
-                const float4 kv = k4[d4], qv = q4[d4];
+                const float4 kv = kv_load4(K, (size_t)pr * hs + 4 * d4), qv = q4[d4];
                 acc = fmaf(qv.x, kv.x, acc);
                 acc = fmaf(qv.y, kv.y, acc);
                 acc = fmaf(qv.z, kv.z, acc);
@@ -943,14 +958,14 @@ __device__ __forceinline__ void attn_item(const Phase &p, int h, int s, int nspl
         m_run = m_new;
         if (osub < nsub) {
             float ov = o_acc * alpha;
-            for (int t = osub; t < tc; t += nsub) ov = fmaf(pt[t], V[t * hs + od], ov);
+            for (int t = osub; t < tc; t += nsub) ov = fmaf(pt[t], kv_load(V, (size_t)t * hs + od), ov);
             o_acc = ov;
         }
         __syncthreads();  // tile buffer, pt and red are reused
     }
 
     // sum the position subsets (the K tiles are free now)
-    float *osum = Kt;
+    float *osum = vcur + hs;
     if (osub < nsub) osum[osub * hs + od] = o_acc;
     __syncthreads();
     const int stride = hs + 2;
@@ -991,6 +1006,17 @@ __device__ __forceinline__ void attn_item(const Phase &p, int h, int s, int nspl
         st_ll(p.aout_ll + (size_t)h * hs + d, O / LL, tag);
     }
     if (tid == 0) p.count[h] = 0;
+}
+
+// Attention item over a float or a half KV cache.
+__device__ __forceinline__ void attn_item(const Phase &p, int h, int s, int nsplit, int n, int span, float *sm,
+                                          uint32_t tag, int *err)
+{
+    if (p.kv_half) {
+        attn_item_t<__half>(p, h, s, nsplit, n, span, sm, tag, err);
+    } else {
+        attn_item_t<float>(p, h, s, nsplit, n, span, sm, tag, err);
+    }
 }
 
 }  // namespace pk

@@ -504,6 +504,7 @@ typedef struct {
     float *norms;
     /* RunState, src/model.c:33-100 */
     float *x, *xb, *xb2, *hb, *hb2, *q, *k, *v, *att, *logits, *kc, *vc;
+    int kv_half; /* not in the reference: cache entries rounded to IEEE half */
 } OrcModel;
 
 typedef struct {
@@ -845,6 +846,26 @@ int orc_kv_write(OrcModel *m, int layer, int pos, const float *k, const float *v
     return 1;
 }
 
+/* Not in the reference (its cache is float, README.md:194): the variant
+ * whose appended K/V entries are rounded to IEEE binary16, round to nearest
+ * even (C's _Float16 conversion), and read back exactly. The rest of the
+ * forward is unchanged. */
+int orc_set_kv_half(OrcModel *m, int on)
+{
+    if (m == NULL) return 0;
+    m->kv_half = on != 0;
+    return 1;
+}
+
+static void kv_append(float *dst, const float *src, int n, int half)
+{
+    if (!half) {
+        memcpy(dst, src, (size_t)n * 4);
+        return;
+    }
+    for (int i = 0; i < n; i++) dst[i] = (float)(_Float16)src[i];
+}
+
 /* rmsnorm_eps, src/gguf_forward.c:24-40. */
 static void rmsnorm(float *o, const float *x, const float *w, int n, float eps)
 {
@@ -930,8 +951,8 @@ float *orc_forward(OrcModel *m, int token, int pos)
         for (int h = 0; h < p->n_kv_heads; h++) {
             rope(m->k + (size_t)h * hs, p->rope_dim, pos, p->rope_freq_base, p->rope_scale);
         }
-        memcpy(m->kc + lc + (size_t)pos * kvd, m->k, (size_t)kvd * 4);
-        memcpy(m->vc + lc + (size_t)pos * kvd, m->v, (size_t)kvd * 4);
+        kv_append(m->kc + lc + (size_t)pos * kvd, m->k, kvd, m->kv_half);
+        kv_append(m->vc + lc + (size_t)pos * kvd, m->v, kvd, m->kv_half);
 
         for (int h = 0; h < p->n_heads; h++) {
             const float *qh = m->q + (size_t)h * hs;

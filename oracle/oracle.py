@@ -69,6 +69,8 @@ class Oracle:
         lib.orc_config.argtypes = [_P, _P, _P]
         lib.orc_kv_write.restype = ctypes.c_int
         lib.orc_kv_write.argtypes = [_P, ctypes.c_int, ctypes.c_int, _P, _P]
+        lib.orc_set_kv_half.restype = ctypes.c_int
+        lib.orc_set_kv_half.argtypes = [_P, ctypes.c_int]
         lib.orc_greedy.restype = ctypes.c_int
         lib.orc_greedy.argtypes = [_P, ctypes.c_int]
         lib.orc_rope_table.argtypes = [_P, ctypes.c_int, _P]
@@ -129,6 +131,10 @@ class OracleModel:
         if not p:
             return None
         return np.ctypeslib.as_array(p, shape=(self.vocab_size,)).copy()
+
+    def set_kv_half(self, on=True):
+        """Round appended K/V entries to IEEE half (not a reference mode)."""
+        return self.orc.lib.orc_set_kv_half(self.h, 1 if on else 0)
 
     def kv_write(self, layer, pos, k, v):
         k = np.ascontiguousarray(k, dtype=np.float32)
