@@ -26,7 +26,7 @@ class Spec(ctypes.Structure):
                [(n, ctypes.c_uint32) for n in ("t_embd", "t_output", "t_q", "t_k", "t_v_even",
                                                 "t_v_odd", "t_o", "t_gate", "t_up",
                                                 "t_down_even", "t_down_odd")] + \
-               [("tied_output", ctypes.c_int)]
+               [("tied_output", ctypes.c_int), ("space_piece", ctypes.c_int)]
 
 
 def _q4km(**kw):

@@ -326,6 +326,8 @@ typedef struct {
     uint32_t t_embd, t_output, t_q, t_k, t_v_even, t_v_odd, t_o, t_gate, t_up, t_down_even,
         t_down_odd;
     int tied_output; /* 1: omit output.weight (output tied to token_embd) */
+    int space_piece; /* 1: token 259 is the bare word-start piece, so that a
+                        SentencePiece encoder can tokenize any text (space + bytes) */
 } PksSpec;
 
 typedef struct {
@@ -351,12 +353,13 @@ static void kv_f32(FILE *f, const char *k, float v)
 }
 static void kv_str(FILE *f, const char *k, const char *v) { w_str(f, k); w_u32(f, 8); w_str(f, v); }
 
-static void token_text(int i, char *buf, size_t cap)
+static void token_text(int i, int space_piece, char *buf, size_t cap)
 {
     if (i == 0) snprintf(buf, cap, "<unk>");
     else if (i == 1) snprintf(buf, cap, "<s>");
     else if (i == 2) snprintf(buf, cap, "</s>");
     else if (i < 259) snprintf(buf, cap, "<0x%02X>", i - 3);
+    else if (i == 259 && space_piece) snprintf(buf, cap, "\xE2\x96\x81"); /* "▁" */
     else snprintf(buf, cap, "\xE2\x96\x81t%d", i); /* "▁t<i>": unique normal pieces */
 }
 
@@ -453,7 +456,7 @@ int pks_write_model(const char *path, const PksSpec *s, char *err, size_t cap)
         w_u32(f, 8);
         w_u64(f, (uint64_t)s->vocab_size);
         for (int i = 0; i < s->vocab_size; i++) {
-            token_text(i, buf, sizeof(buf));
+            token_text(i, s->space_piece, buf, sizeof(buf));
             w_str(f, buf);
         }
         w_str(f, "tokenizer.ggml.scores");
