@@ -40,6 +40,8 @@ struct DecodeArgs {
     Phase one;             // the phase to run when `phases` is null
     const Phase *phases;   // device array of nphases phases (one launch per step)
     int nphases;
+    const CopyEnt *copies;  // with `phases`: every warp's weight copies in consumption
+    const int *copy_off;    //   order, warp gw's at copies[copy_off[gw] .. copy_off[gw + 1])
     int stages, stage_bytes, bar_bytes, xq_bytes, xs_bytes, attn_bytes;
     const int *step;       // {token, pos, generated count, last token, tag}
     const float *rope_cs;  // RoPE cos/sin table [position][rope_dim]
@@ -84,6 +86,14 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
     r.stage_bytes = a.stage_bytes;
     r.issued = r.consumed = 0;
     r.cp = r.ck = 0;
+    r.list = nullptr;
+    r.nlist = r.next = 0;
+    if (a.phases != nullptr && a.copies != nullptr) {
+        const int c0 = a.copy_off[gw];
+        r.list = a.copies + c0;
+        r.nlist = (uint32_t)(a.copy_off[gw + 1] - c0);
+        if (lane == 0 && r.nlist > 0) r.pre = ld_copy(r.list);
+    }
     // x digits (matvec phases) and attention scratch share one region
     uint8_t *xq = smem + a.bar_bytes;
     float *xg = reinterpret_cast<float *>(smem + a.bar_bytes + a.xq_bytes);
@@ -97,7 +107,13 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
     }
     __syncwarp();
     // Weights do not depend on activations: start streaming at once.
-    if (lane == 0) ring_fill(r, ph, nph, gw, NW);
+    if (lane == 0) {
+        if (r.list != nullptr) {
+            ring_fill_list(r);
+        } else {
+            ring_fill(r, ph, nph, gw, NW);
+        }
+    }
     if (tracing && threadIdx.x == 0) a.trace[0] = global_ns();
     if (a.rope_cs != nullptr) {
         const float *row = a.rope_cs + (size_t)pos * a.rope_dim;
@@ -137,7 +153,13 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
                     }
                     __syncwarp();
                     r.consumed++;
-                    if (lane == 0 && ok) ring_fill(r, ph, nph, gw, NW);
+                    if (lane == 0 && ok) {
+                        if (r.list != nullptr) {
+                            ring_fill_list(r);
+                        } else {
+                            ring_fill(r, ph, nph, gw, NW);
+                        }
+                    }
                 }
                 if (p.epi == EPI_LOGITS) {
                     __syncthreads();
@@ -806,6 +828,8 @@ struct PkdCtx {
     int tokens_cap;
     unsigned long long *amax_d;
     Phase *phases_d;
+    CopyEnt *copies_d;  // every warp's weight copies of a step (DecodeArgs::copies)
+    int *copy_off_d;
     unsigned long long *trace_d;  // POCKET_CUDA_TRACE=1: per-phase end times of the last step
     cudaEvent_t ev0, ev1;
     // pinned host mirrors
@@ -1123,6 +1147,8 @@ static int record_step(PkdCtx *c)
         memset(&a, 0, sizeof(a));
         a.phases = c->phases_d;
         a.nphases = c->nphases;
+        a.copies = c->copies_d;
+        a.copy_off = c->copy_off_d;
         a.step = c->step_d;
         a.rope_cs = c->rope_cs;
         a.rope_dim = c->rope_dim;
@@ -1285,6 +1311,69 @@ extern "C" int pkd_tp_connect(PkdCtx *c, const void *handles, char *err, size_t 
     return finalize(c, err, cap);
 }
 
+// Every warp's weight copies for one decode step, in the order
+// phase_kernel consumes its tiles (the MV phases in order; in each, tiles
+// tile_at(p, gw, NW, k / nchunk) for k = 0, 1, ... below ntiles, chunk
+// k % nchunk), uploaded for the rings' list refills. A CTA without tiles
+// in a phase consumes nothing there, and neither does any of its warps.
+static int build_copy_lists(PkdCtx *c, char *err, size_t cap)
+{
+    const int nw = c->grid * DK_WARPS;
+    int *off = (int *)malloc(((size_t)nw + 1) * sizeof(int));
+    if (off == NULL) {
+        if (err && cap) snprintf(err, cap, "Out of memory.");
+        return 0;
+    }
+    size_t total = 0;
+    for (int pass = 0; pass < 2; pass++) {
+        CopyEnt *ents = NULL;
+        if (pass == 1) {
+            ents = (CopyEnt *)malloc((total > 0 ? total : 1) * sizeof(CopyEnt));
+            if (ents == NULL) {
+                free(off);
+                if (err && cap) snprintf(err, cap, "Out of memory.");
+                return 0;
+            }
+        }
+        size_t n = 0;
+        for (int gw = 0; gw < nw; gw++) {
+            off[gw] = (int)n;
+            for (int pi = 0; pi < c->nphases; pi++) {
+                const Phase &p = c->phases[pi];
+                if (p.kind != PH_MV) continue;
+                for (int k = 0;; k++) {
+                    const int t = tile_at(p, gw, nw, k / p.nchunk);
+                    if (t >= p.ntiles) break;
+                    if (pass == 1) {
+                        const Span sp = tile_span(p, t, k % p.nchunk);
+                        ents[n].a0 = (uint64_t)sp.a0;
+                        ents[n].bulk = sp.bulk;
+                        ents[n].tail = sp.tail;
+                    }
+                    n++;
+                }
+            }
+        }
+        off[nw] = (int)n;
+        total = n;
+        if (pass == 1) {
+            const int ok = !cuda_fail(c, cudaMalloc(&c->copies_d, (total > 0 ? total : 1) * sizeof(CopyEnt)),
+                                      "cudaMalloc", err, cap) &&
+                           !cuda_fail(c, cudaMalloc(&c->copy_off_d, ((size_t)nw + 1) * sizeof(int)), "cudaMalloc",
+                                      err, cap) &&
+                           !cuda_fail(c, cudaMemcpy(c->copies_d, ents, total * sizeof(CopyEnt),
+                                                    cudaMemcpyHostToDevice), "copy list upload", err, cap) &&
+                           !cuda_fail(c, cudaMemcpy(c->copy_off_d, off, ((size_t)nw + 1) * sizeof(int),
+                                                    cudaMemcpyHostToDevice), "copy list upload", err, cap);
+            free(ents);
+            free(off);
+            return ok;
+        }
+    }
+    free(off);
+    return 0;
+}
+
 // Phases, shared-memory plan, kernel variant and the captured step.
 static int finalize(PkdCtx *c, char *err, size_t cap)
 {
@@ -1337,6 +1426,7 @@ static int finalize(PkdCtx *c, char *err, size_t cap)
                   cudaMemcpyAsync(c->phases_d, c->phases, (size_t)c->nphases * sizeof(Phase),
                                   cudaMemcpyHostToDevice, st),
                   "phase upload", err, cap) ||
+        !build_copy_lists(c, err, cap) ||
         cuda_fail(c, cudaStreamSynchronize(st), "build sync", err, cap)) {
         return 0;
     }
@@ -1485,6 +1575,7 @@ extern "C" void pkd_destroy(PkdCtx *c)
     free(c->tensors);
     void *dev[] = {c->arena, c->ll, c->lcount, c->kc, c->vc, c->part, c->norms,
                    c->rope_cs, c->count, c->step_d, c->err_d, c->amax_d, c->tokens_d, c->phases_d,
+                   c->copies_d, c->copy_off_d,
                    c->trace_d};
     for (size_t i = 0; i < sizeof(dev) / sizeof(dev[0]); i++) {
         if (dev[i]) cudaFree(dev[i]);

@@ -318,7 +318,7 @@ struct Span {
 // Bytes [st, st + n) land at buf + (st & 15): the 16-byte aligned body via
 // the bulk-copy engine, the sub-16-byte tail (only a matrix's last row can
 // end unaligned) via plain loads, so nothing past the matrix is read.
-__device__ __forceinline__ Span make_span(uintptr_t st, uint64_t n)
+__host__ __device__ inline Span make_span(uintptr_t st, uint64_t n)
 {
     Span sp;
     sp.a0 = st & ~(uintptr_t)15;
@@ -335,20 +335,20 @@ __device__ __forceinline__ void fill_span(const Span &sp, uint8_t *buf, uint64_t
     for (uint32_t i = 0; i < sp.tail; i++) buf[sp.bulk + i] = t[i];
 }
 
-__device__ __forceinline__ const MvSeg &find_seg(const Phase &p, int t)
+__host__ __device__ inline const MvSeg &find_seg(const Phase &p, int t)
 {
     if (p.nseg > 2 && t >= p.seg[2].tile0) return p.seg[2];
     if (p.nseg > 1 && t >= p.seg[1].tile0) return p.seg[1];
     return p.seg[0];
 }
 
-// Lane 0: issue the copies of chunk `chunk` of tile t of phase p into buf;
-// completes on bar.
-__device__ __forceinline__ void issue_tile(const Phase &p, int t, int chunk, uint8_t *buf, uint64_t *bar)
+// Bytes of chunk `chunk` of tile t of phase p in global memory, as
+// issue_tile copies them (host and device).
+__host__ __device__ inline Span tile_span(const Phase &p, int t, int chunk)
 {
     const MvSeg &s = find_seg(p, t);
     const int r0 = (t - s.tile0) * s.R;
-    const int nr = min(s.R, s.rows - r0);
+    const int nr = s.R < s.rows - r0 ? s.R : s.rows - r0;
     uintptr_t st = reinterpret_cast<uintptr_t>(s.w) + (uintptr_t)r0 * s.rb;
     uint64_t n = (uint64_t)nr * s.rb;
     if (p.nchunk > 1) {  // one row, one chunk of it
@@ -356,18 +356,46 @@ __device__ __forceinline__ void issue_tile(const Phase &p, int t, int chunk, uin
         st += off;
         n = s.rb - off < (uint64_t)p.cbytes ? s.rb - off : (uint64_t)p.cbytes;
     }
-    const Span sa = make_span(st, n);
+    return make_span(st, n);
+}
+
+// Lane 0: issue the copies of chunk `chunk` of tile t of phase p into buf;
+// completes on bar.
+__device__ __forceinline__ void issue_tile(const Phase &p, int t, int chunk, uint8_t *buf, uint64_t *bar)
+{
+    const Span sa = tile_span(p, t, chunk);
     mbar_expect_tx(bar, sa.bulk);
     fill_span(sa, buf, bar);
 }
 
-// A warp's ring and its producer cursor (phase index, tile ordinal).
+// One entry of a warp's copy list: the span of one tile (or chunk) it
+// consumes, in consumption order. 16 bytes, read with one vector load.
+struct CopyEnt {
+    uint64_t a0;
+    uint32_t bulk, tail;
+};
+
+__device__ __forceinline__ CopyEnt ld_copy(const CopyEnt *p)
+{
+    const uint4 v = __ldg(reinterpret_cast<const uint4 *>(p));
+    CopyEnt e;
+    e.a0 = ((uint64_t)v.y << 32) | v.x;
+    e.bulk = v.z;
+    e.tail = v.w;
+    return e;
+}
+
+// A warp's ring and its producer cursor: (phase index, tile ordinal) when
+// it walks the phase descriptors, or the position in its copy list.
 struct Ring {
     uint64_t *bars;
     uint8_t *buf;
     int stages, stage_bytes;
     uint32_t issued, consumed;
     int cp, ck;
+    const CopyEnt *list;  // null: walk the descriptors
+    uint32_t nlist, next;
+    CopyEnt pre;          // list[next], loaded one refill ahead
 };
 
 // Lane 0: top the ring up with this warp's next tiles, in consumption order,
@@ -386,6 +414,27 @@ __device__ __forceinline__ void ring_fill(Ring &r, const Phase *ph, int nph, int
         issue_tile(p, t, r.ck % p.nchunk, r.buf + slot * r.stage_bytes, r.bars + slot);
         r.issued++;
         r.ck++;
+    }
+}
+
+// Lane 0: ring_fill from the warp's copy list (built on the host in the
+// order the warp consumes its tiles). A refill issues from registers: the
+// entry after the one issued is loaded at once, and that load completes
+// while the warp computes, instead of the descriptor walk's dependent L2
+// round trips at the end of every phase.
+__device__ __forceinline__ void ring_fill_list(Ring &r)
+{
+    while (r.issued - r.consumed < (uint32_t)r.stages && r.next < r.nlist) {
+        const uint32_t slot = r.issued % (uint32_t)r.stages;
+        Span sa;
+        sa.a0 = (uintptr_t)r.pre.a0;
+        sa.bulk = r.pre.bulk;
+        sa.tail = r.pre.tail;
+        mbar_expect_tx(r.bars + slot, sa.bulk);
+        fill_span(sa, r.buf + slot * r.stage_bytes, r.bars + slot);
+        r.issued++;
+        r.next++;
+        if (r.next < r.nlist) r.pre = ld_copy(r.list + r.next);
     }
 }
 
