@@ -32,6 +32,10 @@ constexpr long long WAIT_LIMIT_CYCLES = 4000000000LL;  // ~2 s at 2 GHz
 // Tagged words may come from another GPU whose step started later (ranks
 // launch independently): a longer bound.
 constexpr long long LL_WAIT_LIMIT_CYCLES = 20000000000LL;  // ~10 s at 2 GHz
+// A poll checks the abort flag (one more global load) only once it has
+// been failing this long (~10 us), so that a normal short wait costs one
+// round trip per retry.
+constexpr long long LL_ABORT_CHECK_CYCLES = 20000LL;
 constexpr int TP_MAX = 8;  // ranks of a tensor-parallel group
 
 enum { PH_MV = 0, PH_ATTN = 1, PH_AR = 2 };
@@ -102,10 +106,15 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
 __device__ __forceinline__ bool aborted(const int *err);
 
 // mbar_wait_bounded that also gives up when another thread has recorded a
-// timeout (checked only while waiting, so a ready stage costs no global load).
+// timeout (checked only after ~10 us of waiting, so neither a ready stage
+// nor a short wait costs a global load).
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t *bar, uint32_t parity, const int *err)
 {
     if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (clock64() - t0 < 20000LL) {
+        if (mbar_try_wait(bar, parity)) return true;
+    }
     if (aborted(err)) return false;
     return mbar_wait_bounded(bar, parity);
 }
@@ -177,13 +186,60 @@ __device__ __forceinline__ float ll_read(const uint64_t *p, uint32_t tag, int *e
     do {
         w = ld_ll(p);
         if (ll_is(w, tag)) break;
-        if (aborted(err)) break;
-        if (clock64() - t0 > LL_WAIT_LIMIT_CYCLES) {
+        const long long dt = clock64() - t0;
+        if (dt > LL_ABORT_CHECK_CYCLES && aborted(err)) break;
+        if (dt > LL_WAIT_LIMIT_CYCLES) {
             atomicOr(err, ERR_TIMEOUT_WAIT);
             break;
         }
     } while (true);
     return ll_val(w);
+}
+
+// Values of n (<= 8) tagged words at each of pa and pb (64-byte aligned
+// when n == 8), polled together so that both wait in one round trip per
+// retry; va/vb[e] = 0 for e >= n. Bounded as ll_read.
+__device__ __forceinline__ void ll_read8x2(const uint64_t *pa, const uint64_t *pb, int n, uint32_t tag, float *va,
+                                           float *vb, int *err)
+{
+    uint64_t w[16];
+    long long t0 = 0;
+    bool first = true;
+    for (;;) {
+        if (n >= 8) {
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                ld_ll2(pa + 2 * k, w[2 * k], w[2 * k + 1]);
+                ld_ll2(pb + 2 * k, w[8 + 2 * k], w[8 + 2 * k + 1]);
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                w[e] = e < n ? ld_ll(pa + e) : ((uint64_t)tag << 32);
+                w[8 + e] = e < n ? ld_ll(pb + e) : ((uint64_t)tag << 32);
+            }
+        }
+        bool ok = true;
+#pragma unroll
+        for (int e = 0; e < 16; e++) ok = ok && ll_is(w[e], tag);
+        if (ok) break;
+        if (first) {
+            t0 = clock64();
+            first = false;
+        } else {
+            const long long dt = clock64() - t0;
+            if (dt > LL_ABORT_CHECK_CYCLES && aborted(err)) break;
+            if (dt > LL_WAIT_LIMIT_CYCLES) {
+                atomicOr(err, ERR_TIMEOUT_WAIT);
+                break;
+            }
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        va[e] = e < n ? ll_val(w[e]) : 0.0f;
+        vb[e] = e < n ? ll_val(w[8 + e]) : 0.0f;
+    }
 }
 
 // Values of the n (<= 8) tagged words at p (64-byte aligned when n == 8),
@@ -204,13 +260,17 @@ __device__ __forceinline__ void ll_read8(const uint64_t *p, int n, uint32_t tag,
         bool ok = true;
 #pragma unroll
         for (int e = 0; e < 8; e++) ok = ok && ll_is(w[e], tag);
-        if (ok || aborted(err)) break;
+        if (ok) break;
         if (first) {
             t0 = clock64();
             first = false;
-        } else if (clock64() - t0 > LL_WAIT_LIMIT_CYCLES) {
-            atomicOr(err, ERR_TIMEOUT_WAIT);
-            break;
+        } else {
+            const long long dt = clock64() - t0;
+            if (dt > LL_ABORT_CHECK_CYCLES && aborted(err)) break;
+            if (dt > LL_WAIT_LIMIT_CYCLES) {
+                atomicOr(err, ERR_TIMEOUT_WAIT);
+                break;
+            }
         }
     }
 #pragma unroll
@@ -495,8 +555,7 @@ __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t
             // hb = silu(gate) * up, src/gguf_forward.c:287-290
             if (c0 < n) {
                 float u[8];
-                ll_read8(p.xin_ll + c0, min(8, n - c0), tag, v, err);
-                ll_read8(p.xin_ll + n + c0, min(8, n - c0), tag, u, err);
+                ll_read8x2(p.xin_ll + c0, p.xin_ll + n + c0, min(8, n - c0), tag, v, u, err);
 #pragma unroll
                 for (int e = 0; e < 8; e++) v[e] = __fmul_rn(__fdiv_rn(v[e], __fadd_rn(1.0f, expf(-v[e]))), u[e]);
             }
@@ -851,7 +910,9 @@ __device__ __forceinline__ void ar_item(const Phase &p, int it, const int *step,
 // ------------------------------------------------------------------ //
 
 // Positions one attention item covers at least: one pass of a CTA's
-// warps (8 warps x 32 lanes, one position per lane).
+// warps (8 warps x 32 lanes, one position per lane). Splitting shorter
+// spans over more CTAs was measured slower at ~130 positions (the merge's
+// extra round trip costs more than the parallel tiles save).
 constexpr int ATT_MIN_SPAN = 256;
 
 // Splits of a head's positions over CTAs at most: enough items to cover
