@@ -987,6 +987,40 @@ __device__ __forceinline__ void attn_item_t(const Phase &p, int h, int s, int ns
     __shared__ int last_sh;
 
     const bool has_cur = t1 == n;  // the item covers this step's position
+    const size_t lbase = (size_t)p.layer * p.seq_len * kvd + (size_t)g * hs;
+    const KV *kc = static_cast<const KV *>(p.kc) + lbase, *vc = static_cast<const KV *>(p.vc) + lbase;
+    const int ntile = (t1 - t0 + T - 1) / T;
+    constexpr int E16 = 16 / (int)sizeof(KV);  // entries per 16-byte copy
+    const int hsc = hs / E16;
+    // The cached rows of tile k into buffer buf (16-byte cp.async, one
+    // commit group); this step's row, which the cache may not hold yet, is
+    // skipped and put in by put_cur.
+    auto load_rows = [&](int k, int buf) {
+        const int tb = t0 + k * T, tc = min(T, t1 - tb);
+        KV *K = Kt + buf * T * hs, *V = Vt + buf * T * hs;
+        for (int i = tid; i < tc * hsc; i += nt) {
+            const int r = i / hsc, c = (i - r * hsc) * E16;
+            if (tb + r != n - 1) {
+                cp_async16(K + r * hs + c, kc + (size_t)(tb + r) * kvd + c);
+                cp_async16(V + r * hs + c, vc + (size_t)(tb + r) * kvd + c);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    auto put_cur = [&](int k, int buf) {
+        const int r = n - 1 - (t0 + k * T);
+        if (!has_cur || r < 0 || r >= T) return;
+        KV *K = Kt + buf * T * hs, *V = Vt + buf * T * hs;
+        for (int i = tid; i < hs; i += nt) {
+            kv_store(K, (size_t)r * hs + i, kcur[i]);
+            kv_store(V, (size_t)r * hs + i, vcur[i]);
+        }
+    };
+    // The first two tiles' cached rows do not depend on this step: they are
+    // in flight while q and this position's k, v arrive.
+    load_rows(0, 0);
+    if (ntile > 1) load_rows(1, 1);
+
     const KV *kc0 = static_cast<const KV *>(p.kc);
     for (int i = tid; i < hs; i += nt) {
         qs[i] = ll_read(p.aq_ll + (size_t)h * hs + i, tag, err);
@@ -997,39 +1031,16 @@ __device__ __forceinline__ void attn_item_t(const Phase &p, int h, int s, int ns
         }
     }
     __syncthreads();
-
-    const size_t lbase = (size_t)p.layer * p.seq_len * kvd + (size_t)g * hs;
-    const KV *kc = static_cast<const KV *>(p.kc) + lbase, *vc = static_cast<const KV *>(p.vc) + lbase;
-    const int ntile = (t1 - t0 + T - 1) / T;
-    constexpr int E16 = 16 / (int)sizeof(KV);  // entries per 16-byte copy
-    const int hsc = hs / E16;
-    auto load_tile = [&](int k, int buf) {
-        const int tb = t0 + k * T, tc = min(T, t1 - tb);
-        KV *K = Kt + buf * T * hs, *V = Vt + buf * T * hs;
-        for (int i = tid; i < tc * hsc; i += nt) {
-            const int r = i / hsc, c = (i - r * hsc) * E16;
-            if (tb + r == n - 1) {
-#pragma unroll
-                for (int e = 0; e < E16; e++) {
-                    kv_store(K, (size_t)r * hs + c + e, kcur[c + e]);
-                    kv_store(V, (size_t)r * hs + c + e, vcur[c + e]);
-                }
-            } else {
-                cp_async16(K + r * hs + c, kc + (size_t)(tb + r) * kvd + c);
-                cp_async16(V + r * hs + c, vc + (size_t)(tb + r) * kvd + c);
-            }
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    };
+    put_cur(0, 0);
+    if (ntile > 1) put_cur(1, 1);
 
     float m_run = -INFINITY, l_run = 0.0f, o_acc = 0.0f;
     const int pr = tid / tpp, pi = tid - pr * tpp;  // scoring: position pr of the tile (< T: a position), part pi
     const int od = tid % hs, osub = tid / hs;       // output: dimension od, position subset osub
-    load_tile(0, 0);
     for (int k = 0; k < ntile; k++) {
         const int buf = k & 1, tb = t0 + k * T, tc = min(T, t1 - tb);
+        // tiles k and (if any) k + 1 are in flight: wait for k
         if (k + 1 < ntile) {
-            load_tile(k + 1, buf ^ 1);
             asm volatile("cp.async.wait_group 1;" ::: "memory");
         } else {
             asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -1072,6 +1083,10 @@ __device__ __forceinline__ void attn_item_t(const Phase &p, int h, int s, int ns
             o_acc = ov;
         }
         __syncthreads();  // tile buffer, pt and red are reused
+        if (k + 2 < ntile) {
+            load_rows(k + 2, buf);
+            put_cur(k + 2, buf);
+        }
     }
 
     // sum the position subsets (the K tiles are free now)
