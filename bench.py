@@ -352,13 +352,59 @@ def run_b64(path, args, cfg, device=0, barrier=lambda: None):
                          else "fallback 6.65 TB/s"}}
 
 
+def run_step_trace(args, positions=130):
+    """Per-phase critical path of one B=1 decode step on the TinyLlama
+    shape, from the step trace (POCKET_CUDA_TRACE=1: every CTA's
+    %globaltimer stamps after staging its input and after its work, per
+    phase). Decodes `positions` greedy steps, then reports per phase kind,
+    averaged over layers 1..20: the phase's length on the critical path
+    (last CTA end minus the previous phase's last CTA end), the median time
+    from that previous end until a CTA has staged its input, and the median
+    and maximum work time of the CTAs with work. A diagnostic, not a bench
+    line: the tracing itself adds a barrier per phase."""
+    os.environ["POCKET_CUDA_TRACE"] = "1"
+    import pk_b200
+    path = ensure_model(WORKLOADS["tinyllama"]["preset"], 0, lambda: None)
+    e = pk_b200.Engine(path, positions + 8, device=0)
+    tok = 1
+    for pos in range(positions):
+        tok = int(np.argmax(e.forward(tok, pos)))
+    a = e.trace(all_ctas=True)  # [cta][phase][after staging, after work], us from CTA 0's start
+    e.close()
+    stg, end = a[:, :, 0], a[:, :, 1]
+    kinds = ["qkv", "attention", "wo", "gate_up", "down"]
+    out = {k: [] for k in kinds}
+    nl = (a.shape[1] - 1) // 5
+    for layer in range(1, nl - 1):
+        for i, k in enumerate(kinds):
+            ph = 5 * layer + i
+            prev = end[:, ph - 1].max()
+            work = end[:, ph] - stg[:, ph]
+            busy = work > 0.3
+            out[k].append((end[:, ph].max() - prev, np.median(stg[busy, ph] - prev), np.median(work[busy]),
+                           work.max()))
+    res = {"metric": "decode step trace (B=1)", "unit": "us", "position": positions,
+           "step_us": float(end[:, -1].max()), "phases": {}}
+    for k, v in out.items():
+        v = np.array(v)
+        res["phases"][k] = {"critical_us": round(float(v[:, 0].mean()), 2),
+                            "staged_after_prev_us": round(float(v[:, 1].mean()), 2),
+                            "work_median_us": round(float(v[:, 2].mean()), 2),
+                            "work_max_us": round(float(v[:, 3].mean()), 2)}
+    lg = a.shape[1] - 1
+    res["phases"]["logits"] = {"critical_us": round(float(end[:, lg].max() - end[:, lg - 1].max()), 2)}
+    print(json.dumps(res))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="tinyllama", choices=list(WORKLOADS) + ["matvec", "matmul", "b64"])
+    ap.add_argument("--workload", default="tinyllama",
+                    choices=list(WORKLOADS) + ["matvec", "matmul", "b64", "trace"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", default=None, help="matvec workload: one TYPE:ROWSxCOLS case")
     ap.add_argument("--b64-steps", type=int, default=32, help="timed steps of the B=64 batched decode (0: skip)")
@@ -375,6 +421,8 @@ def main():
         return run_matvec_sweep(args)
     if args.workload == "matmul":
         return run_matmul_sweep(args)
+    if args.workload == "trace":
+        return run_step_trace(args)
     if args.workload == "b64":
         import torch
         import pk_b200

@@ -200,14 +200,31 @@ __global__ void mv_reduce_kernel(const float *part, int splits, int count, float
     }
 }
 
-// Split-K of mv_tile_kernel for `rows` x `cols`: chunks per split.
+// Split-K of mv_tile_kernel for `rows` x `cols`: chunks per split. With
+// two CTAs per SM, the launch takes about waves x cps chunk-steps (waves =
+// CTAs / (2 sms), rounded up, since a partly filled last wave costs a whole
+// one). The split count that minimises that is taken, except that the
+// fewest splits within 5% of the minimum win (each split adds a partial
+// sum per output to write and reduce). E.g. 2048 x 5632: 8 splits of 3
+// chunks, 256 CTAs in one wave (11 splits of 2 would need a second wave
+// for 56 CTAs: 4 chunk-steps instead of 3).
 __host__ inline int mv_cps(int rows, int cols, int sms)
 {
     const int tiles = (rows + TR - 1) / TR, nchunks = (cols + TK - 1) / TK;
-    int splits = (4 * sms + tiles - 1) / tiles;  // two CTAs per SM, two waves
-    if (splits > nchunks) splits = nchunks;
-    if (splits < 1) splits = 1;
-    return (nchunks + splits - 1) / splits;
+    const long long slots = 2LL * (sms > 0 ? sms : 1);
+    long long best = -1;
+    for (int cps = 1; cps <= nchunks; cps++) {
+        const long long ctas = (long long)tiles * ((nchunks + cps - 1) / cps);
+        const long long steps = (ctas + slots - 1) / slots * cps;
+        if (best < 0 || steps < best) best = steps;
+    }
+    // the fewest splits (largest cps) within 5% of the best
+    for (int cps = nchunks; cps >= 1; cps--) {
+        const long long ctas = (long long)tiles * ((nchunks + cps - 1) / cps);
+        const long long steps = (ctas + slots - 1) / slots * cps;
+        if (steps * 100 <= best * 105) return cps;
+    }
+    return 1;
 }
 
 // x[b] = embedding row tokens[b] (src/gguf_forward.c: the token's row of
