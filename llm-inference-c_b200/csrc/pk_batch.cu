@@ -550,6 +550,8 @@ struct PkbCtx {
     cudaGraph_t graph[bt::BMAX + 1];
     cudaGraphExec_t exec[bt::BMAX + 1];
     int gqa_smem;  // dynamic shared memory of attention_gqa_kernel (0: per-head attention instead)
+    cudaStream_t side;             // tile-kernel matrices that run beside a tensor-core launch
+    cudaEvent_t ev_fork, ev_join;  //   (forked from and joined to st inside the captured step)
     char msg[256];
 };
 
@@ -561,19 +563,20 @@ static int bfail(PkbCtx *b, cudaError_t e, const char *what)
 }
 
 // y (n x rows) = x (n x cols) W^T for one weight tensor.
-static int bmatmul(PkbCtx *b, const PkdTensor &t, const float *x, int n, float *y)
+static int bmatmul(PkbCtx *b, const PkdTensor &t, const float *x, int n, float *y, cudaStream_t st = nullptr)
 {
+    if (st == nullptr) st = b->st;
     const uint8_t *w = b->arena + t.offset;
     const int rows = (int)t.rows, cols = (int)t.cols;
-    if (pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, w)) return pk_mm_run(w, t.row_bytes, rows, cols, x, n, y, &b->mm, b->sms, b->st);
+    if (pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, w)) return pk_mm_run(w, t.row_bytes, rows, cols, x, n, y, &b->mm, b->sms, st);
     const int cps = bt::mv_cps(rows, cols, b->sms), nchunks = (cols + bt::TK - 1) / bt::TK;
     const int splits = (nchunks + cps - 1) / cps;
     const dim3 grid((rows + bt::TR - 1) / bt::TR, splits);
     switch (t.type) {
 #define PKB_CASE(T)                                                                                           \
     case T:                                                                                                   \
-        bt::mv_tile_kernel<T><<<grid, 256, bt::mv_smem<T>(), b->st>>>(w, t.row_bytes, rows, cols, x, n, y,    \
-                                                                      b->part, cps);                          \
+        bt::mv_tile_kernel<T><<<grid, 256, bt::mv_smem<T>(), st>>>(w, t.row_bytes, rows, cols, x, n, y,       \
+                                                                   b->part, cps);                             \
         break;
         PKB_CASE(T_F32)
         PKB_CASE(T_F16)
@@ -588,17 +591,36 @@ static int bmatmul(PkbCtx *b, const PkdTensor &t, const float *x, int n, float *
     }
     if (splits > 1) {
         const int count = n * rows;
-        bt::mv_reduce_kernel<<<(count + 255) / 256, 256, 0, b->st>>>(b->part, splits, count, y);
+        bt::mv_reduce_kernel<<<(count + 255) / 256, 256, 0, st>>>(b->part, splits, count, y);
     }
     return cudaGetLastError() == cudaSuccess;
 }
 
 // y_i = x W_i^T for weights that multiply the same x: the Q4_K ones in one
-// tensor-core launch (x staged once), the others on the tile kernel.
+// tensor-core launch (x staged once), the others on the tile kernel. When
+// both kinds are present the tile-kernel ones run on a side stream, forked
+// before and joined after the tensor-core launch, so that they use the SMs
+// the tensor-core grid leaves idle (e.g. the Q6_K attn_v of an even layer
+// beside the Q and K launch of 32 CTAs). Their outputs and the tile
+// kernel's split-K partials are not touched by the tensor-core launch.
 static int bmatmul_group(PkbCtx *b, const PkdTensor *const *ts, float *const *ys, int cnt, const float *x, int n)
 {
     PkMmSeg seg[3];
-    int ns = 0;
+    int ns = 0, tiles = 0;
+    for (int i = 0; i < cnt; i++) {
+        const PkdTensor &t = *ts[i];
+        if (pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, b->arena + t.offset)) {
+            ns++;
+        } else {
+            tiles++;
+        }
+    }
+    const bool fork = ns > 0 && tiles > 0;
+    if (fork && (bfail(b, cudaEventRecord(b->ev_fork, b->st), "event") ||
+                 bfail(b, cudaStreamWaitEvent(b->side, b->ev_fork, 0), "event"))) {
+        return 0;
+    }
+    ns = 0;
     for (int i = 0; i < cnt; i++) {
         const PkdTensor &t = *ts[i];
         const uint8_t *w = b->arena + t.offset;
@@ -608,13 +630,17 @@ static int bmatmul_group(PkbCtx *b, const PkdTensor *const *ts, float *const *ys
             seg[ns].rows = (int)t.rows;
             seg[ns].y = ys[i];
             ns++;
-        } else if (!bmatmul(b, t, x, n, ys[i])) {
+        } else if (!bmatmul(b, t, x, n, ys[i], fork ? b->side : b->st)) {
             return 0;
         }
     }
     if (ns == 0) return 1;
     const int cols = (int)ts[0]->cols;
-    return pk_mm_stage(x, n, cols, &b->mm, b->st) && pk_mm_run_staged(seg, ns, cols, n, &b->mm, b->sms, b->st);
+    if (!pk_mm_stage(x, n, cols, &b->mm, b->st) || !pk_mm_run_staged(seg, ns, cols, n, &b->mm, b->sms, b->st)) {
+        return 0;
+    }
+    return !fork || (!bfail(b, cudaEventRecord(b->ev_join, b->side), "event") &&
+                     !bfail(b, cudaStreamWaitEvent(b->st, b->ev_join, 0), "event"));
 }
 
 // The launches of one step for n sequences (inputs already in io_d).
@@ -701,6 +727,14 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
     }
     b->device = v.device;
     b->st = (cudaStream_t)v.stream;
+    cudaSetDevice(b->device);
+    if (bfail(b, cudaStreamCreateWithFlags(&b->side, cudaStreamNonBlocking), "cudaStreamCreate") ||
+        bfail(b, cudaEventCreateWithFlags(&b->ev_fork, cudaEventDisableTiming), "cudaEventCreate") ||
+        bfail(b, cudaEventCreateWithFlags(&b->ev_join, cudaEventDisableTiming), "cudaEventCreate")) {
+        if (err && cap) snprintf(err, cap, "%s", b->msg);
+        pkb_destroy(b);
+        return NULL;
+    }
     b->m = m;
     b->arena = v.arena;
     b->norms = v.norms;
@@ -870,5 +904,8 @@ extern "C" void pkb_destroy(PkbCtx *b)
     for (void *p : dev)
         if (p) cudaFree(p);
     if (b->io_h) cudaFreeHost(b->io_h);
+    if (b->ev_fork) cudaEventDestroy(b->ev_fork);
+    if (b->ev_join) cudaEventDestroy(b->ev_join);
+    if (b->side) cudaStreamDestroy(b->side);
     free(b);
 }
