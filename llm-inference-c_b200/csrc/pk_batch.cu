@@ -385,15 +385,16 @@ __global__ void __launch_bounds__(128) attention_kernel(const float *q, const KV
 // one CTA, so every key and value row is read once per group rather than
 // once per query head. Scores: one thread per position computes the H dot
 // products from its key row (16-byte loads); softmax: warp w takes heads
-// w, w + 16, ...; weighted sum: thread (tg, h, d4) adds float4 d4 of the
-// value rows t = tg mod G times p_h, and the G partials are added in order.
-// 512 threads; H * hs / 4 <= 128.
+// w, w + 16, ...; weighted sum: thread (tg, d4) reads float4 d4 of the
+// value rows t = tg mod G (G = 512 / (hs / 4)) once and adds p_h[t] times
+// it for every head h, and the G partials are added in order.
+// 512 threads; H <= 8, H * hs / 4 <= 128.
 template <typename KV>
 __global__ void __launch_bounds__(512) attention_gqa_kernel(const float *q, const KV *kc, const KV *vc,
                                                             const int *io, int bmax, int layer, int L, int seq_len,
                                                             int hs, int qd, int kvd, int H, float scale, float *out)
 {
-    extern __shared__ __align__(16) float sg[];  // H * hs queries, H rows of seq_len scores, G x 128 float4 partials
+    extern __shared__ __align__(16) float sg[];  // H * hs queries, H rows of seq_len scores, G x H x hs/4 float4 partials
     const int g = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int P = io[bmax + b] + 1, seq = io[2 * bmax + b];
     const int sl = (seq_len + 3) & ~3, F4 = hs >> 2;
@@ -443,35 +444,45 @@ __global__ void __launch_bounds__(512) attention_gqa_kernel(const float *q, cons
         for (int t = lane; t < P; t += 32) sh[t] *= inv;
     }
     __syncthreads();
-    const int HF = H * F4, G = blockDim.x / HF;
-    const int tg = tid / HF, hd = tid - tg * HF, h = hd / F4, d4 = hd - h * F4;
-    float4 *part = reinterpret_cast<float4 *>(sc + H * sl);
+    // weighted sum: thread (tg, d4) reads float4 d4 of the value rows
+    // t = tg mod G once and adds it into all H heads' sums (p_h[t] from
+    // shared memory); the G partials of each (head, d4) are added in order.
+    const int G = blockDim.x / F4, tg = tid / F4, d4 = tid - tg * F4;
+    float4 *part = reinterpret_cast<float4 *>(sc + H * sl);  // [G][H][F4]
     if (tg < G) {
         const KV *vb = vc + base + 4 * d4;
-        const float *ph = sc + h * sl;
-        float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll 4
+        float4 o[8];
+#pragma unroll
+        for (int h = 0; h < 8; h++) o[h] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 2
         for (int t = tg; t < P; t += G) {
             const float4 vv = kv_load4(vb, (size_t)t * kvd);
-            const float pt = ph[t];
-            o.x = fmaf(pt, vv.x, o.x);
-            o.y = fmaf(pt, vv.y, o.y);
-            o.z = fmaf(pt, vv.z, o.z);
-            o.w = fmaf(pt, vv.w, o.w);
+#pragma unroll
+            for (int h = 0; h < 8; h++) {
+                if (h < H) {
+                    const float pt = sc[h * sl + t];
+                    o[h].x = fmaf(pt, vv.x, o[h].x);
+                    o[h].y = fmaf(pt, vv.y, o[h].y);
+                    o[h].z = fmaf(pt, vv.z, o[h].z);
+                    o[h].w = fmaf(pt, vv.w, o[h].w);
+                }
+            }
         }
-        part[tg * HF + hd] = o;
+#pragma unroll
+        for (int h = 0; h < 8; h++)
+            if (h < H) part[((size_t)tg * H + h) * F4 + d4] = o[h];
     }
     __syncthreads();
-    if (tid < HF) {
-        float4 r = part[tid];
+    if (tid < H * F4) {
+        const int hh = tid / F4, dd = tid - hh * F4;
+        float4 r = part[(size_t)hh * F4 + dd];
         for (int k = 1; k < G; k++) {
-            const float4 pk = part[k * HF + tid];
+            const float4 pk = part[((size_t)k * H + hh) * F4 + dd];
             r.x += pk.x;
             r.y += pk.y;
             r.z += pk.z;
             r.w += pk.w;
         }
-        const int hh = tid / F4, dd = tid - hh * F4;
         reinterpret_cast<float4 *>(out + (size_t)b * qd + ((size_t)g * H + hh) * hs)[dd] = r;
     }
 }
@@ -827,7 +838,7 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
     // and the group fills at least half of its threads
     {
         const int H = m.n_heads / m.n_kv_heads;
-        const size_t gs = ((size_t)H * hs + (size_t)H * ((m.seq_len + 3) / 4 * 4)) * 4 + 512 * 16;
+        const size_t gs = ((size_t)H * hs + (size_t)H * ((m.seq_len + 3) / 4 * 4)) * 4 + (size_t)512 * H * 16;
         if (ok && H >= 2 && H <= 8 && H * (hs / 4) >= 64 && H * (hs / 4) <= 128 && gs <= 200 * 1024) {
             ok = !bfail(b, cudaFuncSetAttribute(bt::attention_gqa_kernel<float>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gs),
