@@ -114,26 +114,84 @@ __global__ void __launch_bounds__(256, 2) mv_tile_kernel(const uint8_t *w, uint6
     const int c0 = blockIdx.y * cps, c1 = min(nchunks, c0 + cps);
     const bool active = 2 * vg < n;  // warp-uniform (a warp holds vg 4w .. 4w+3)
     const int npad = (n + 1) & ~1;
-    const int dc = tid & (TH - 1), dr0 = (tid >> 7) * 32;  // decode: column dc, rows dr0 .. dr0+31
+    // decode: row dr (lanes of a warp take consecutive rows, so the stores
+    // into Ws are conflict-free), columns dc0, dc0 + 4, ...
+    const int dr = tid & (TR - 1), dc0 = tid >> 6;
     float acc[8][2];
 #pragma unroll
     for (int i = 0; i < 8; i++) acc[i][0] = acc[i][1] = 0.0f;
-    for (int ch = c0; ch < c1; ch++) {
+    // Packed bytes of chunk ch for the 64 rows, as halfwords e = tid + 256 j
+    // (fetch/store in batches). Formats whose chunk takes at most 32
+    // halfwords per thread load the next chunk as 4-byte words (fetchw:
+    // the 4-byte aligned window of each row's chunk, NW words per row) during
+    // the current chunk's last FMA pass, and unpack them into Wraw (storew)
+    // after it (PREF, when the rows are 4-byte aligned).
+    constexpr bool PREF = PER <= 32;
+    constexpr int NW = (CB + 2 + 3) / 4;             // words covering a chunk at a 2-byte offset
+    constexpr int PERW = (TR * NW + 255) / 256;      // words per thread
+    uint32_t pre[PREF ? PERW : 1];
+    auto fetch = [&](int ch, uint16_t *raw, int j0) {
         const uint64_t boff = (uint64_t)ch * CB;
         const int have = (int)min((uint64_t)CB, rb - boff) / 2;  // halfwords of this chunk in a row
-        for (int j0 = 0; j0 < PER; j0 += BATCH) {
-            uint16_t raw[BATCH];
 #pragma unroll
-            for (int j = 0; j < BATCH; j++) {
-                const int e = tid + 256 * (j0 + j), r = e / (CB / 2), hw = e - r * (CB / 2);
-                raw[j] = (j0 + j < PER && e < HW && row0 + r < rows && hw < have)
-                             ? ld_u16(w + (size_t)(row0 + r) * rb + boff + 2 * hw)
-                             : (uint16_t)0;
+        for (int j = 0; j < BATCH; j++) {
+            const int e = tid + 256 * (j0 + j), r = e / (CB / 2), hw = e - r * (CB / 2);
+            raw[j] = (j0 + j < PER && e < HW && row0 + r < rows && hw < have)
+                         ? ld_u16(w + (size_t)(row0 + r) * rb + boff + 2 * hw)
+                         : (uint16_t)0;
+        }
+    };
+    auto store = [&](const uint16_t *raw, int j0) {
+#pragma unroll
+        for (int j = 0; j < BATCH; j++) {
+            const int e = tid + 256 * (j0 + j);
+            if (j0 + j < PER && e < HW) Wraw[e] = raw[j];
+        }
+    };
+    auto fetchw = [&](int ch) {
+        const uint64_t boff = (uint64_t)ch * CB, a = boff & ~(uint64_t)3;
+        const uint64_t end = min(boff + (uint64_t)CB, rb);  // the row's bytes end here
+#pragma unroll
+        for (int j = 0; j < (PREF ? PERW : 1); j++) {
+            const int q = tid + 256 * j, r = q / NW, k = q - r * NW;
+            const uint64_t at = a + 4 * (uint64_t)k;
+            uint32_t v = 0u;
+            if (q < TR * NW && row0 + r < rows) {
+                const uint8_t *src = w + (size_t)(row0 + r) * rb + at;
+                if (at + 4 <= end) {
+                    v = *reinterpret_cast<const uint32_t *>(src);
+                } else if (at + 2 <= end) {
+                    v = ld_u16(src);  // never past the row's last byte
+                }
             }
+            pre[j] = v;
+        }
+    };
+    auto storew = [&](int ch) {
+        const int sh = (int)(((uint64_t)ch * CB) & 3) / 2;  // halfwords before the chunk in word 0
 #pragma unroll
-            for (int j = 0; j < BATCH; j++) {
-                const int e = tid + 256 * (j0 + j);
-                if (j0 + j < PER && e < HW) Wraw[e] = raw[j];
+        for (int j = 0; j < (PREF ? PERW : 1); j++) {
+            const int q = tid + 256 * j, r = q / NW, k = q - r * NW;
+            if (q < TR * NW) {
+#pragma unroll
+                for (int hh = 0; hh < 2; hh++) {
+                    const int hw = 2 * k + hh - sh;
+                    if (hw >= 0 && hw < CB / 2) Wraw[r * (CB / 2) + hw] = (uint16_t)(pre[j] >> (16 * hh));
+                }
+            }
+        }
+    };
+    // 4-byte loads need every row to start on a 4-byte boundary
+    const bool pref = PREF && ((rb | (uint64_t)(uintptr_t)w) & 3) == 0;
+    if (pref && c0 < c1) fetchw(c0);
+    for (int ch = c0; ch < c1; ch++) {
+        if (pref) {
+            storew(ch);  // Wraw is free: the previous chunk's decode is done
+        } else {
+            for (int j0 = 0; j0 < PER; j0 += BATCH) {
+                uint16_t raw[BATCH];
+                fetch(ch, raw, j0);
+                store(raw, j0);
             }
         }
         for (int hf = 0; hf < TK / TH; hf++) {
@@ -154,13 +212,17 @@ __global__ void __launch_bounds__(256, 2) mv_tile_kernel(const uint8_t *w, uint6
             }
             asm volatile("cp.async.commit_group;" ::: "memory");
             __syncthreads();  // the chunk's packed rows are staged; Ws is free
+            {
+                const uint8_t *rowp = reinterpret_cast<const uint8_t *>(Wraw + dr * (CB / 2));
 #pragma unroll 4
-            for (int r = dr0; r < dr0 + 32; r++) {
-                const uint8_t *rowp = reinterpret_cast<const uint8_t *>(Wraw + r * (CB / 2));
-                Ws[dc * WS + wpos(r)] = dc < kc ? decode_col(T, rowp, hf * TH + dc) : 0.0f;
+                for (int dc = dc0; dc < TH; dc += 4) {
+                    Ws[dc * WS + wpos(dr)] = dc < kc ? decode_col(T, rowp, hf * TH + dc) : 0.0f;
+                }
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
             __syncthreads();
+            // the next chunk's packed bytes load during this chunk's last FMA pass
+            if (pref && ch + 1 < c1 && (hf + 1 == TK / TH || k0 + TH >= cols)) fetchw(ch + 1);
             if (active) {
                 const float *wk = Ws + wpos(8 * rg);
 #pragma unroll 4
