@@ -51,10 +51,10 @@ WORKLOADS = {
 PUBLISHED_TOKS = 8.03  # reference, TinyLlama-1.1B-Chat Q4_K_M, 8 threads (documentation/PERFORMANCE.md:60)
 
 # DRAM bytes (read + write) of one decode-step launch of phase_kernel, from
-# the ncu capture summarised in profiles/phase_kernel_tinyllama_decode.md
-# (dram__bytes_read.sum + dram__bytes_write.sum); None for workloads without
+# one ncu capture of that launch (the phase_kernel summary under profiles/:
+# dram__bytes_read.sum + dram__bytes_write.sum); None for workloads without
 # a capture.
-NCU_TRAFFIC = {"tinyllama-1.1b-q4km": 637432576 + 10022400}
+NCU_TRAFFIC = {"tinyllama-1.1b-q4km": 639899648 + 7175168}
 FALLBACK_HBM_GBS = 6650.0
 MODEL_SEED = 1234
 
