@@ -81,10 +81,19 @@ __host__ __device__ constexpr int chunk_bytes()
          : T == T_F16 ? 512 : 1024;
 }
 
+// Halfwords per staged row in shared memory: the chunk's bytes padded to
+// an odd number of 4-byte words, so that 32 lanes reading the same offset
+// of 32 consecutive rows hit 32 different banks.
+template <int T>
+__host__ __device__ constexpr int raw_stride()
+{
+    return 2 * (((chunk_bytes<T>() + 3) / 4) | 1);
+}
+
 template <int T>
 __host__ __device__ constexpr int mv_smem()
 {
-    return TR * chunk_bytes<T>() + MV_SMEM;
+    return TR * raw_stride<T>() * 2 + MV_SMEM;
 }
 
 // y[b][r] = sum_c W[r][c] x[b][c] (b < n <= 64) on CUDA cores. Per CTA 64
@@ -103,6 +112,7 @@ __global__ void __launch_bounds__(256, 2) mv_tile_kernel(const uint8_t *w, uint6
 {
     constexpr int CB = chunk_bytes<T>();
     constexpr int HW = TR * (CB / 2);       // halfwords of a staged chunk
+    constexpr int RS = raw_stride<T>();      // halfwords per row in Wraw
     constexpr int PER = (HW + 255) / 256;   // per thread
     constexpr int BATCH = PER < 8 ? PER : 8;
     extern __shared__ __align__(16) float smt[];
@@ -144,8 +154,8 @@ __global__ void __launch_bounds__(256, 2) mv_tile_kernel(const uint8_t *w, uint6
     auto store = [&](const uint16_t *raw, int j0) {
 #pragma unroll
         for (int j = 0; j < BATCH; j++) {
-            const int e = tid + 256 * (j0 + j);
-            if (j0 + j < PER && e < HW) Wraw[e] = raw[j];
+            const int e = tid + 256 * (j0 + j), r = e / (CB / 2), hw = e - r * (CB / 2);
+            if (j0 + j < PER && e < HW) Wraw[r * RS + hw] = raw[j];
         }
     };
     auto fetchw = [&](int ch) {
@@ -176,7 +186,7 @@ __global__ void __launch_bounds__(256, 2) mv_tile_kernel(const uint8_t *w, uint6
 #pragma unroll
                 for (int hh = 0; hh < 2; hh++) {
                     const int hw = 2 * k + hh - sh;
-                    if (hw >= 0 && hw < CB / 2) Wraw[r * (CB / 2) + hw] = (uint16_t)(pre[j] >> (16 * hh));
+                    if (hw >= 0 && hw < CB / 2) Wraw[r * RS + hw] = (uint16_t)(pre[j] >> (16 * hh));
                 }
             }
         }
@@ -213,7 +223,7 @@ __global__ void __launch_bounds__(256, 2) mv_tile_kernel(const uint8_t *w, uint6
             asm volatile("cp.async.commit_group;" ::: "memory");
             __syncthreads();  // the chunk's packed rows are staged; Ws is free
             {
-                const uint8_t *rowp = reinterpret_cast<const uint8_t *>(Wraw + dr * (CB / 2));
+                const uint8_t *rowp = reinterpret_cast<const uint8_t *>(Wraw + dr * RS);
 #pragma unroll 4
                 for (int dc = dc0; dc < TH; dc += 4) {
                     Ws[dc * WS + wpos(dr)] = dc < kc ? decode_col(T, rowp, hf * TH + dc) : 0.0f;
