@@ -99,13 +99,16 @@ __host__ __device__ constexpr int mv_smem()
 // y[b][r] = sum_c W[r][c] x[b][c] (b < n <= 64) on CUDA cores. Per CTA 64
 // rows and a range of 256-column chunks (split-K over blockIdx.y when the
 // row tiles alone are too few for the SMs). Per chunk the packed bytes of
-// the 64 rows are staged in shared memory with batched 2-byte loads; then,
-// per half of 128 columns, the x columns of every vector arrive by 16-byte
-// async copies, each weight is decoded once from shared memory (bit-exact
-// decoders, column-major floats), and thread (rg, vg) accumulates rows
-// 8rg .. 8rg+7 for vectors 2vg, 2vg+1. One split writes y; several write
-// partial sums that mv_reduce_kernel adds in split order. Two CTAs per SM
-// (about 82 KB of shared memory for the K-quants).
+// the 64 rows are staged in shared memory (rows padded to an odd number of
+// words; for formats of at most 32 halfwords per thread and 4-byte aligned
+// rows the next chunk loads as words during the current chunk's last FMA
+// pass, otherwise with batched 2-byte loads); then, per half of 128
+// columns, the x columns of every vector arrive by 16-byte async copies,
+// each weight is decoded once from shared memory (bit-exact decoders,
+// column-major floats; lanes take consecutive rows), and thread (rg, vg)
+// accumulates rows 8rg .. 8rg+7 for vectors 2vg, 2vg+1. One split writes y;
+// several write partial sums that mv_reduce_kernel adds in split order. Two
+// CTAs per SM (about 82 KB of shared memory for the K-quants).
 template <int T>
 __global__ void __launch_bounds__(256, 2) mv_tile_kernel(const uint8_t *w, uint64_t rb, int rows, int cols,
                                                          const float *x, int n, float *y, float *part, int cps)
