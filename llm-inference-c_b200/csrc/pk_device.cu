@@ -1075,14 +1075,15 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total, int cap)
         rotate(wo);
         if (W > 1) all_reduce(P[3], base + lp.rwo, xin, base + lp.xmid);
 
-        // gate and up as two row sets of one phase: gate rows to hb[0, hid),
-        // up rows to hb[hid, 2 hid); the down phase stages silu(gate) * up
+        // gate and up as two row sets of one phase: gate rows to hb[0, hid);
+        // an up row's epilogue takes its gate word and writes
+        // silu(gate) * up to hb[hid, 2 hid), the down phase's input
         up.kind = PH_MV;
         up.pro = PRO_NORM;
         up.epi = EPI_STORE;
         up.nseg = 2;
         seg_of(up.seg[0], c, m->gate[l], KIND_PLAIN);
-        seg_of(up.seg[1], c, m->up[l], KIND_PLAIN);
+        seg_of(up.seg[1], c, m->up[l], KIND_UP);
         up.seg[1].yoff = m->hidden_dim;
         up.cols = dim;
         up.xin_ll = ll + lp.xmid;
@@ -1093,11 +1094,11 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total, int cap)
         rotate(up);
 
         dn.kind = PH_MV;
-        dn.pro = PRO_SWIGLU;
+        dn.pro = PRO_PLAIN;
         dn.nseg = 1;
         seg_of(dn.seg[0], c, m->down[l], KIND_PLAIN);
         dn.cols = m->hidden_dim;
-        dn.xin_ll = ll + lp.hb;
+        dn.xin_ll = ll + lp.hb + m->hidden_dim;
         if (W > 1) {
             dn.epi = EPI_PEER;
             tp_common(dn);

@@ -41,7 +41,7 @@ constexpr int TP_MAX = 8;  // ranks of a tensor-parallel group
 enum { PH_MV = 0, PH_ATTN = 1, PH_AR = 2 };
 enum { PRO_PLAIN = 0, PRO_NORM = 1, PRO_EMBED_NORM = 2, PRO_SWIGLU = 3 };
 enum { EPI_STORE = 0, EPI_ADD = 1, EPI_QKV = 2, EPI_LOGITS = 4, EPI_PEER = 5 };
-enum { KIND_PLAIN = 0, KIND_Q = 1, KIND_K = 2, KIND_V = 3 };
+enum { KIND_PLAIN = 0, KIND_Q = 1, KIND_K = 2, KIND_V = 3, KIND_UP = 4 };
 enum { ERR_TIMEOUT_MV = 1, ERR_TIMEOUT_WAIT = 2, ERR_NONFINITE = 4 };
 constexpr int ERR_FATAL = ERR_TIMEOUT_MV | ERR_TIMEOUT_WAIT;
 
@@ -517,6 +517,13 @@ __device__ __forceinline__ float pow2f(int k)
     return __uint_as_float((uint32_t)(k + 127) << 23);
 }
 
+// hb = silu(gate) * up with the reference's rounding steps,
+// src/gguf_forward.c:287-290.
+__device__ __forceinline__ float swiglu(float g, float u)
+{
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
 // Stage the phase's input vector in integer form (pk_quant.cuh): RMSNorm'ed
 // as src/gguf_forward.c:24-40 (o = w * (ss * x), ss = 1 / sqrtf(mean(x^2) +
 // eps)) for PRO_NORM, and taken from the embedding row (bit-exact decode,
@@ -557,7 +564,7 @@ __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t
                 float u[8];
                 ll_read8x2(p.xin_ll + c0, p.xin_ll + n + c0, min(8, n - c0), tag, v, u, err);
 #pragma unroll
-                for (int e = 0; e < 8; e++) v[e] = __fmul_rn(__fdiv_rn(v[e], __fadd_rn(1.0f, expf(-v[e]))), u[e]);
+                for (int e = 0; e < 8; e++) v[e] = swiglu(v[e], u[e]);
             }
         } else if (p.xin_ll != nullptr) {
             if (c0 < n) ll_read8(p.xin_ll + c0, min(8, n - c0), tag, v, err);
@@ -867,6 +874,12 @@ __device__ __forceinline__ void run_tile(const Phase &p, int t, int chunk, const
         }
     } else if (lane < nr) {
         float out = va;
+        if (s.kind == KIND_UP) {
+            // an up row: hb = silu(gate) * up with this row's gate, which a
+            // gate tile of the same phase writes to y_ll[r] (another warp;
+            // a warp takes its gate tiles before its up tiles)
+            out = swiglu(ll_read(p.y_ll + r, tag, err), va);
+        }
         if (p.epi == EPI_ADD) {
             // residual stream, src/gguf_forward.c:274-276,297-299 (layer 0's input
             // is the embedding row, decoded again here)
