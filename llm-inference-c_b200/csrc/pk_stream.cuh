@@ -39,6 +39,9 @@ constexpr long long LL_ABORT_CHECK_CYCLES = 20000LL;
 constexpr int TP_MAX = 8;  // ranks of a tensor-parallel group
 
 enum { PH_MV = 0, PH_ATTN = 1, PH_AR = 2 };
+// PRO_SWIGLU stages silu(gate) * up from a gate|up vector; the decode step's
+// down phase no longer uses it (its up rows' epilogue, KIND_UP, writes the
+// product), the prologue stays for phases built on a gate|up input.
 enum { PRO_PLAIN = 0, PRO_NORM = 1, PRO_EMBED_NORM = 2, PRO_SWIGLU = 3 };
 enum { EPI_STORE = 0, EPI_ADD = 1, EPI_QKV = 2, EPI_LOGITS = 4, EPI_PEER = 5 };
 enum { KIND_PLAIN = 0, KIND_Q = 1, KIND_K = 2, KIND_V = 3, KIND_UP = 4 };
