@@ -729,7 +729,6 @@ static int bmatmul_group(PkbCtx *b, const PkdTensor *const *ts, float *const *ys
                      !bfail(b, cudaStreamWaitEvent(b->st, b->ev_join, 0), "event"));
 }
 
-// The launches of one step for n sequences (inputs already in io_d).
 // Layer l's KV append (after RoPE) and attention for the n rows of a step,
 // over a cache of KV entries (float or half).
 template <typename KV>
@@ -749,6 +748,7 @@ static void attend(PkbCtx *b, int l, int n, size_t att_smem, KV *kc, KV *vc)
     }
 }
 
+// The launches of one step for n sequences (inputs already in io_d).
 static int enqueue_step(PkbCtx *b, int n)
 {
     const PkdModel &m = b->m;

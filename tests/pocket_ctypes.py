@@ -83,8 +83,7 @@ class Session:
     def generate(self, prompt, max_tokens):
         opts = GenOptions(b"greedy", 0.0, 0, max_tokens)
         self.pieces = []
-        out = self.lib.pocket_model_generate(self.h, prompt.encode(), ctypes.byref(opts), self._cb, None)
-        return None if out is None else out
+        return self.lib.pocket_model_generate(self.h, prompt.encode(), ctypes.byref(opts), self._cb, None)
 
     def chat(self, message, max_tokens):
         opts = GenOptions(b"greedy", 0.0, 0, max_tokens)
