@@ -100,10 +100,24 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
     float *att = reinterpret_cast<float *>(smem + a.bar_bytes);
     __shared__ unsigned long long cta_amax[2];
     __shared__ float rope[256];  // this position's RoPE cos/sin pairs
+    // The decode step's phase descriptors pass through shared memory: the
+    // next one is bulk-copied while the current one runs, so no field read
+    // during a phase waits on L2.
+    __shared__ Phase sph[2];
+    __shared__ uint64_t dbar;
+    const bool staged_desc = a.phases != nullptr;
 
     if (lane == 0) {
         for (int s = 0; s < a.stages; s++) mbar_init(r.bars + s, 1);
+        if (staged_desc && threadIdx.x == 0) mbar_init(&dbar, 1);
         fence_mbar_init();
+    }
+    if (staged_desc) {
+        __syncthreads();  // dbar is initialised before any thread waits on it
+        if (threadIdx.x == 0) {
+            mbar_expect_tx(&dbar, (uint32_t)sizeof(Phase));
+            bulk_g2s(&sph[0], ph, (uint32_t)sizeof(Phase), &dbar);
+        }
     }
     __syncwarp();
     // Weights do not depend on activations: start streaming at once.
@@ -111,7 +125,7 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
         if (r.list != nullptr) {
             ring_fill_list(r);
         } else {
-            ring_fill(r, ph, nph, gw, NW);
+            ring_fill(r, ph, nph, gw, W, NW);
         }
     }
     if (tracing && threadIdx.x == 0) a.trace[0] = global_ns();
@@ -121,15 +135,25 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
     }
 
     for (int pi = 0; pi < nph; pi++) {
-        const Phase &p = ph[pi];
-        // the next phase's descriptor (global memory) into L1 while this one runs
-        if (a.phases != nullptr && pi + 1 < nph && threadIdx.x < (unsigned)((sizeof(Phase) + 127) / 128)) {
-            asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const char *>(ph + pi + 1) +
-                                                           128 * threadIdx.x));
+        if (staged_desc) {
+            // descriptor pi has landed (bounded wait, CTA-uniform outcome)
+            const int ok = __syncthreads_and(mbar_wait_bounded(&dbar, (uint32_t)(pi & 1)) ? 1 : 0);
+            if (!ok) {
+                if (threadIdx.x == 0) atomicOr(a.err, ERR_TIMEOUT_MV);
+                break;
+            }
+            // every thread is done with descriptor pi - 1, whose buffer takes pi + 1
+            if (threadIdx.x == 0 && pi + 1 < nph) {
+                mbar_expect_tx(&dbar, (uint32_t)sizeof(Phase));
+                bulk_g2s(&sph[(pi + 1) & 1], ph + pi + 1, (uint32_t)sizeof(Phase), &dbar);
+            }
         }
+        const Phase &p = staged_desc ? sph[pi & 1] : ph[pi];
         if (p.kind == PH_MV) {
             if (cta_has_tiles(p, blockIdx.x, W, NW)) {
-                __syncthreads();  // every warp is done with the previous phase's x
+                // every warp is done with the previous phase's x (the barrier
+                // above, when the descriptors are staged)
+                if (!staged_desc) __syncthreads();
                 if (p.epi == EPI_LOGITS && threadIdx.x == 0) cta_amax[0] = cta_amax[1] = 0ull;
                 stage_x(p, a.step, xq, xg, tag, a.err);  // ends with __syncthreads
                 if (ctr != nullptr && threadIdx.x == 0) {
@@ -138,7 +162,7 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
                 }
                 float racc = 0.0f;  // a chunked row's running sum
                 for (int k = 0;; k++) {
-                    const int t = tile_at(p, gw, NW, k / p.nchunk);
+                    const int t = tile_at(p, gw, W, NW, k / p.nchunk);
                     if (t >= p.ntiles) break;
                     const uint32_t slot = r.consumed % (uint32_t)a.stages;
                     const uint32_t par = (r.consumed / (uint32_t)a.stages) & 1u;
@@ -157,7 +181,7 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
                         if (r.list != nullptr) {
                             ring_fill_list(r);
                         } else {
-                            ring_fill(r, ph, nph, gw, NW);
+                            ring_fill(r, ph, nph, gw, W, NW);
                         }
                     }
                 }
@@ -512,6 +536,7 @@ static int launch_phase(const Phase &p, const int *step, int *err, cudaStream_t 
     DecodeArgs a;
     memset(&a, 0, sizeof(a));
     a.one = p;
+    a.one.cta0 = a.one.nct = 0;  // this launch's grid is the phase's alone
     a.phases = nullptr;
     a.nphases = 1;
     a.step = step;
@@ -678,7 +703,7 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) na_matvec_kernel(const __gri
         fence_mbar_init();
     }
     __syncwarp();
-    if (lane == 0) ring_fill(r, &p, 1, gw, NW);
+    if (lane == 0) ring_fill(r, &p, 1, gw, W, NW);
 
     const uint4 *sq = reinterpret_cast<const uint4 *>(scratch + NA_Q_OFF);
     const uint4 *sg = reinterpret_cast<const uint4 *>(scratch + NA_G_OFF);
@@ -689,7 +714,7 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) na_matvec_kernel(const __gri
 
     float racc = 0.0f;
     for (int k = 0;; k++) {
-        const int t = tile_at(p, gw, NW, k / p.nchunk);
+        const int t = tile_at(p, gw, W, NW, k / p.nchunk);
         if (t >= p.ntiles) break;
         const uint32_t slot = r.consumed % (uint32_t)a.stages;
         const uint32_t par = (r.consumed / (uint32_t)a.stages) & 1u;
@@ -702,7 +727,7 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) na_matvec_kernel(const __gri
         }
         __syncwarp();
         r.consumed++;
-        if (lane == 0 && ok) ring_fill(r, &p, 1, gw, NW);
+        if (lane == 0 && ok) ring_fill(r, &p, 1, gw, W, NW);
     }
     if (lane == 0 && r.issued != r.consumed) ring_drain(r);
 }
@@ -976,6 +1001,17 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total, int cap)
         p.off = acc;
         acc = (acc + p.ntiles) % nw_total;
     };
+    // The QKV and Wo tiles avoid CTAs [0, heads), where the attention items
+    // of one split each run: those CTAs start an attention item (its first
+    // K/V tiles in flight) while the QKV rows are still being computed.
+    const int heads = tp.q_heads;
+    auto spare_attention_ctas = [&](Phase &p) {
+        const int rest = c->grid - heads;
+        if (rest >= 1 && rest * DK_WARPS >= p.ntiles) {
+            p.cta0 = heads;
+            p.nct = rest;
+        }
+    };
     auto tp_common = [&](Phase &p) {
         p.world = W;
         p.rank = tp.rank;
@@ -1031,10 +1067,11 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total, int cap)
         qkv.seq_len = m->seq_len;
         qkv.layer = l;
         tile_phase(qkv, nw_total, cap, true);
+        spare_attention_ctas(qkv);
         rotate(qkv);
 
         att.kind = PH_ATTN;
-        att.off = (acc + DK_WARPS - 1) / DK_WARPS;  // the CTAs after the QKV tiles
+        att.off = 0;  // head h's first split on CTA h, which has no QKV tiles
         att.aq_ll = ll + lp.q;
         att.ak_ll = ll + lp.k;
         att.av_ll = ll + lp.v;
@@ -1072,6 +1109,7 @@ static int build_phases(PkdCtx *c, const PkdModel *m, int nw_total, int cap)
             wo.y_ll = ll + lp.xmid;
         }
         tile_phase(wo, nw_total, cap, false);
+        spare_attention_ctas(wo);
         rotate(wo);
         if (W > 1) all_reduce(P[3], base + lp.rwo, xin, base + lp.xmid);
 
@@ -1314,7 +1352,7 @@ extern "C" int pkd_tp_connect(PkdCtx *c, const void *handles, char *err, size_t 
 
 // Every warp's weight copies for one decode step, in the order
 // phase_kernel consumes its tiles (the MV phases in order; in each, tiles
-// tile_at(p, gw, NW, k / nchunk) for k = 0, 1, ... below ntiles, chunk
+// tile_at(p, gw, W, NW, k / nchunk) for k = 0, 1, ... below ntiles, chunk
 // k % nchunk), uploaded for the rings' list refills. A CTA without tiles
 // in a phase consumes nothing there, and neither does any of its warps.
 static int build_copy_lists(PkdCtx *c, char *err, size_t cap)
@@ -1343,7 +1381,7 @@ static int build_copy_lists(PkdCtx *c, char *err, size_t cap)
                 const Phase &p = c->phases[pi];
                 if (p.kind != PH_MV) continue;
                 for (int k = 0;; k++) {
-                    const int t = tile_at(p, gw, nw, k / p.nchunk);
+                    const int t = tile_at(p, gw, DK_WARPS, nw, k / p.nchunk);
                     if (t >= p.ntiles) break;
                     if (pass == 1) {
                         const Span sp = tile_span(p, t, k % p.nchunk);

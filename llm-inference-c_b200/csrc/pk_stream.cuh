@@ -312,10 +312,14 @@ struct MvSeg {
     int yoff;          // EPI_STORE: row r goes to output element yoff + r
 };
 
-struct Phase {
+// 16-byte multiple: the decode step bulk-copies each phase's descriptor
+// into shared memory.
+struct alignas(16) Phase {
     int kind, pro, epi;
-    int off;              // work rotation: tile t goes to warp (t + off) % warps,
+    int off;              // work rotation: tile t goes to warp slot (t + off) % slots,
                           // attention item i to CTA (i + off) % CTAs
+    int cta0, nct;        // the tiles go to the warps of CTAs [cta0, cta0 + nct) (mod the
+                          // grid; nct 0: every CTA), warp-major: warp 0 of each CTA first
     // fused matvec
     MvSeg seg[3];
     int nseg, ntiles, cols, nunits;
@@ -355,18 +359,38 @@ struct Phase {
     int ncta;                 // EPI_LOGITS: CTAs with logits tiles
 };
 
-// Tile k (0, 1, ...) of warp gw among nw warps (>= ntiles: none).
-__host__ __device__ inline int tile_at(const Phase &p, int gw, int nw, int k)
+constexpr int NO_TILE = 0x7FFFFFFF;
+
+// Slot of warp gw (W warps per CTA, nw in the grid) among the phase's
+// warps, or -1 when its CTA takes no tiles. Slots run warp-major over the
+// phase's CTAs (warp 0 of every CTA, then warp 1, ...), so that a phase
+// with fewer tiles than warps still spreads over all of its SMs.
+__host__ __device__ inline int warp_slot(const Phase &p, int gw, int W, int nw, int &nslots)
 {
-    return (gw + nw - p.off % nw) % nw + k * nw;
+    const int G = nw / W, b = gw / W, w = gw % W;
+    const int nct = p.nct > 0 && p.nct < G ? p.nct : G;
+    nslots = nct * W;
+    const int lb = ((b - p.cta0) % G + G) % G;
+    return lb < nct ? w * nct + lb : -1;
+}
+
+// Tile k (0, 1, ...) of warp gw among nw warps, W per CTA (>= ntiles: none).
+__host__ __device__ inline int tile_at(const Phase &p, int gw, int W, int nw, int k)
+{
+    int ns = 1;
+    const int s0 = warp_slot(p, gw, W, nw, ns);
+    if (s0 < 0) return NO_TILE;
+    return (s0 + ns - p.off % ns) % ns + k * ns;
 }
 
 // Does any of the W warps of CTA b own a tile of p?
 __host__ __device__ inline bool cta_has_tiles(const Phase &p, int b, int W, int nw)
 {
     if (p.ntiles <= 0) return false;
-    const int f0 = (b * W + nw - p.off % nw) % nw;
-    return f0 + W > nw || f0 < p.ntiles;
+    for (int w = 0; w < W; w++) {
+        if (tile_at(p, b * W + w, W, nw, 0) < p.ntiles) return true;
+    }
+    return false;
 }
 
 // ------------------------------------------------------------------ //
@@ -463,11 +487,11 @@ struct Ring {
 
 // Lane 0: top the ring up with this warp's next tiles, in consumption order,
 // across phase boundaries.
-__device__ __forceinline__ void ring_fill(Ring &r, const Phase *ph, int nph, int gw, int nw_total)
+__device__ __forceinline__ void ring_fill(Ring &r, const Phase *ph, int nph, int gw, int W, int nw_total)
 {
     while (r.issued - r.consumed < (uint32_t)r.stages && r.cp < nph) {
         const Phase &p = ph[r.cp];
-        const int t = p.kind == PH_MV ? tile_at(p, gw, nw_total, r.ck / p.nchunk) : 0;
+        const int t = p.kind == PH_MV ? tile_at(p, gw, W, nw_total, r.ck / p.nchunk) : 0;
         if (p.kind != PH_MV || t >= p.ntiles) {
             r.cp++;
             r.ck = 0;
@@ -608,8 +632,18 @@ __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t
         sc = norm_scale(ss);
     }
     for (int base = 0; base < ng; base += MAXP * nquads) {
-        float v[MAXP][8];
+        float v[MAXP][8], nv[MAXP][8];
         float ss = 0.0f;
+        if (normed) {
+            // the norm weights do not depend on x: their loads are in flight
+            // while the inputs are polled
+#pragma unroll
+            for (int k = 0; k < MAXP; k++) {
+                const int c0 = 32 * (base + quad + k * nquads) + 8 * t;
+#pragma unroll
+                for (int e = 0; e < 8; e++) nv[k][e] = c0 + e < n ? __ldg(norm + c0 + e) : 0.0f;
+            }
+        }
 #pragma unroll
         for (int k = 0; k < MAXP; k++) {
             const int g = base + quad + k * nquads;
@@ -629,7 +663,7 @@ __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t
             if (normed) {
 #pragma unroll
                 for (int e = 0; e < 8; e++) {
-                    if (c0 + e < n) v[k][e] = __fmul_rn(norm[c0 + e], __fmul_rn(sc, v[k][e]));
+                    if (c0 + e < n) v[k][e] = __fmul_rn(nv[k][e], __fmul_rn(sc, v[k][e]));
                 }
             }
             float amax = 0.0f, sum = 0.0f;
