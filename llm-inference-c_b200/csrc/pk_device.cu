@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
                 // above, when the descriptors are staged)
                 if (!staged_desc) __syncthreads();
                 if (p.epi == EPI_LOGITS && threadIdx.x == 0) cta_amax[0] = cta_amax[1] = 0ull;
-                stage_x(p, a.step, xq, xg, tag, a.err);  // ends with __syncthreads
+                const float nscale = stage_x(p, a.step, xq, xg, tag, a.err);  // ends with __syncthreads
                 if (ctr != nullptr && threadIdx.x == 0) {
                     ctr[2 * pi] = global_ns();
                     if (tracing) a.trace[3 * pi + 1] = ctr[2 * pi];
@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
                         if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_MV);
                     } else {
                         run_tile<MASK>(p, t, k % p.nchunk, r.buf + slot * a.stage_bytes, xq, xg, token, pos, rope,
-                                       tag, a.err, lane, cta_amax, racc);
+                                       tag, a.err, lane, cta_amax, racc, nscale);
                     }
                     __syncwarp();
                     r.consumed++;
@@ -723,7 +723,7 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) na_matvec_kernel(const __gri
             if (lane == 0) atomicOr(a.err, ERR_TIMEOUT_MV);
         } else {
             run_tile<FMT_ALL>(p, t, k % p.nchunk, r.buf + slot * a.stage_bytes, xq, xg, 0, 0, nullptr, 0u, a.err,
-                              lane, nullptr, racc);
+                              lane, nullptr, racc, 1.0f);
         }
         __syncwarp();
         r.consumed++;

@@ -551,17 +551,34 @@ __device__ __forceinline__ float swiglu(float g, float u)
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
 }
 
-// Stage the phase's input vector in integer form (pk_quant.cuh): RMSNorm'ed
-// as src/gguf_forward.c:24-40 (o = w * (ss * x), ss = 1 / sqrtf(mean(x^2) +
-// eps)) for PRO_NORM, and taken from the embedding row (bit-exact decode,
-// src/gguf_model.c:314-359) for PRO_EMBED_NORM. All threads of the CTA.
+// The signed base-256 digits of four 23-bit integers X_e, given as
+// Y_e = X_e + 0x808080 (0 <= Y_e < 2^24): digit k of X_e is byte k of Y_e
+// minus 128, so plane k packs byte k of Y_0..Y_3 (a byte transpose), with
+// the sign bit of each byte flipped.
+__device__ __forceinline__ void digit_planes(const uint32_t *Y, uint32_t &p0, uint32_t &p1, uint32_t &p2)
+{
+    const uint32_t t0 = __byte_perm(Y[0], Y[1], 0x5140), t1 = __byte_perm(Y[2], Y[3], 0x5140);
+    const uint32_t u0 = __byte_perm(Y[0], Y[1], 0x0062), u1 = __byte_perm(Y[2], Y[3], 0x0062);
+    p0 = __byte_perm(t0, t1, 0x5410) ^ 0x80808080u;
+    p1 = __byte_perm(t0, t1, 0x7632) ^ 0x80808080u;
+    p2 = __byte_perm(u0, u1, 0x5410) ^ 0x80808080u;
+}
+
+// Stage the phase's input vector in integer form (pk_quant.cuh), for
+// PRO_NORM the RMSNorm'ed vector of src/gguf_forward.c:24-40
+// (o = w * (ss * x), ss = 1 / sqrtf(mean(x^2) + eps)) and for PRO_EMBED_NORM
+// the same of the embedding row (bit-exact decode, src/gguf_model.c:314-359).
+// A matvec is linear in its input, so the digits hold w * x and the caller
+// multiplies each row's sum by the returned ss (1 for the other prologues):
+// the block-wide sum of squares is then reduced beside the digits instead
+// of before them. All threads of the CTA.
 //
 // Four threads own a 32-column group (eight columns each, kept in
 // registers from one load to the digits), so there are no per-element
 // round trips and only two-step shuffles within the quad. Tagged inputs
 // (xin_ll) are polled until they carry `tag`.
-__device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t *xq, float *xg, uint32_t tag,
-                                        int *err)
+__device__ __forceinline__ float stage_x(const Phase &p, const int *step, uint8_t *xq, float *xg, uint32_t tag,
+                                         int *err)
 {
     constexpr int MAXP = 2;  // groups per quad per pass
     __shared__ float red[32];
@@ -570,7 +587,6 @@ __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t
     const float *xin = p.xin, *norm = p.norm;
     const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
     const int quad = tid >> 2, t = tid & 3, nquads = nt >> 2;
-    const bool one_pass = ng <= MAXP * nquads;  // values stay in registers from load to digits
     const uint8_t *erow = nullptr;
     int etype = 0;
     if (pro == PRO_EMBED_NORM) {
@@ -608,32 +624,9 @@ __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t
             }
         }
     };
-    // RMSNorm scale from the block-wide sum of squares.
-    auto norm_scale = [&](float ss) -> float {
-        ss = warp_sum(ss);
-        __syncthreads();  // `red` may still be read by a previous phase's staging
-        if (lane == 0) red[warp] = ss;
-        __syncthreads();
-        float tot = 0.0f;
-        for (int w = 0; w < (nt >> 5); w++) tot += red[w];
-        float m = __fdiv_rn(tot, (float)n);
-        m = __fadd_rn(m, p.eps);
-        return __fdiv_rn(1.0f, __fsqrt_rn(m));
-    };
-    float sc = 1.0f;
-    if (normed && !one_pass) {
-        float ss = 0.0f;
-        for (int g = quad; g < ng; g += nquads) {
-            float v[8];
-            load8(32 * g + 8 * t, v);
-#pragma unroll
-            for (int e = 0; e < 8; e++) ss = fmaf(v[e], v[e], ss);
-        }
-        sc = norm_scale(ss);
-    }
+    float ss = 0.0f;  // this thread's share of the sum of squares (normed)
     for (int base = 0; base < ng; base += MAXP * nquads) {
         float v[MAXP][8], nv[MAXP][8];
-        float ss = 0.0f;
         if (normed) {
             // the norm weights do not depend on x: their loads are in flight
             // while the inputs are polled
@@ -648,10 +641,7 @@ __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t
         for (int k = 0; k < MAXP; k++) {
             const int g = base + quad + k * nquads;
             load8(32 * g + 8 * t, v[k]);  // beyond ng: zeros (c0 >= n)
-#pragma unroll
-            for (int e = 0; e < 8; e++) ss = fmaf(v[k][e], v[k][e], ss);
         }
-        if (normed && one_pass) sc = norm_scale(ss);
 #pragma unroll
         for (int k = 0; k < MAXP; k++) {
             // The shuffles below name all 32 lanes, so the loop may only be
@@ -659,11 +649,11 @@ __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t
             if (base + 8 * warp + k * nquads >= ng) break;
             const int g = base + quad + k * nquads;
             const bool act = g < ng;
-            const int c0 = 32 * g + 8 * t;
             if (normed) {
 #pragma unroll
                 for (int e = 0; e < 8; e++) {
-                    if (c0 + e < n) v[k][e] = __fmul_rn(nv[k][e], __fmul_rn(sc, v[k][e]));
+                    ss = fmaf(v[k][e], v[k][e], ss);
+                    v[k][e] = __fmul_rn(nv[k][e], v[k][e]);
                 }
             }
             float amax = 0.0f, sum = 0.0f;
@@ -681,25 +671,23 @@ __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t
             const int E = (int)((__float_as_uint(amax) >> 23) & 255u) - 126;
             const bool live = E >= -104;
             const float f = live ? pow2f(22 - E) : 0.0f;
-            uint32_t w0[2] = {0u, 0u}, w1[2] = {0u, 0u}, w2[2] = {0u, 0u};
-            int ds0 = 0, ds1 = 0, ds2 = 0;
+            // X = v * f rounded to nearest even (exact: |v * f| < 2^22 and f
+            // is a power of two) via the float 1.5 * 2^23 + X, whose bits
+            // are 0x4B400000 + X; Y = X + 0x808080 carries X's signed
+            // base-256 digits, X = d0 + 2^8 d1 + 2^16 d2, |dk| <= 128
+            uint32_t Y[8];
 #pragma unroll
             for (int e = 0; e < 8; e++) {
-                // exact: |v * f| < 2^22 and f is a power of two
-                const int X = __float2int_rn(v[k][e] * f);
-                // signed base-256 digits: X = d0 + 2^8 d1 + 2^16 d2, |dk| <= 128
-                const int d0 = ((X + 128) & 255) - 128;
-                const int r1 = (X - d0) >> 8;
-                const int d1 = ((r1 + 128) & 255) - 128;
-                const int d2 = (r1 - d1) >> 8;
-                w0[e >> 2] |= (uint32_t)(d0 & 255) << (8 * (e & 3));
-                w1[e >> 2] |= (uint32_t)(d1 & 255) << (8 * (e & 3));
-                w2[e >> 2] |= (uint32_t)(d2 & 255) << (8 * (e & 3));
-                ds0 += d0;
-                ds1 += d1;
-                ds2 += d2;
+                Y[e] = __float_as_uint(fmaf(v[k][e], f, 12582912.0f)) - (0x4B400000u - 0x808080u);
             }
-            // digit sums per 16-column half: threads (0,1) and (2,3)
+            uint32_t w0[2], w1[2], w2[2];
+            digit_planes(Y, w0[0], w1[0], w2[0]);
+            digit_planes(Y + 4, w0[1], w1[1], w2[1]);
+            // digit sums of the thread's eight columns, then per 16-column
+            // half: threads (0,1) and (2,3)
+            int ds0 = dp4a_ss(w0[1], 0x01010101u, dp4a_ss(w0[0], 0x01010101u, 0));
+            int ds1 = dp4a_ss(w1[1], 0x01010101u, dp4a_ss(w1[0], 0x01010101u, 0));
+            int ds2 = dp4a_ss(w2[1], 0x01010101u, dp4a_ss(w2[0], 0x01010101u, 0));
             ds0 += __shfl_xor_sync(0xFFFFFFFFu, ds0, 1);
             ds1 += __shfl_xor_sync(0xFFFFFFFFu, ds1, 1);
             ds2 += __shfl_xor_sync(0xFFFFFFFFu, ds2, 1);
@@ -722,7 +710,19 @@ __device__ __forceinline__ void stage_x(const Phase &p, const int *step, uint8_t
             }
         }
     }
+    if (normed) {
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;  // read after the barrier below, rewritten next phase
+    }
     __syncthreads();
+    if (!normed) return 1.0f;
+    // RMSNorm scale, src/gguf_forward.c:24-40 (sequential sum there; a
+    // block-wide tree here)
+    float tot = 0.0f;
+    for (int w = 0; w < (nt >> 5); w++) tot += red[w];
+    float m = __fdiv_rn(tot, (float)n);
+    m = __fadd_rn(m, p.eps);
+    return __fdiv_rn(1.0f, __fsqrt_rn(m));
 }
 
 // ------------------------------------------------------------------ //
@@ -811,14 +811,16 @@ __device__ __forceinline__ float tile_dispatch(int type, const uint8_t *ra, uint
 }
 
 // Compute tile t of phase p from its ring slot and apply the epilogue.
-// rope: this position's cos/sin pairs (EPI_QKV); tag: the step's tag for
+// nscale: stage_x's row-sum multiplier; rope: this position's cos/sin
+// pairs (EPI_QKV); tag: the step's tag for
 // tagged outputs and the residual. MASK: the formats compiled in.
 // Rows in column chunks (p.nchunk > 1): each chunk's sum adds to racc and
 // the epilogue runs after the last chunk.
 template <unsigned MASK>
 __device__ __forceinline__ void run_tile(const Phase &p, int t, int chunk, const uint8_t *buf, const uint8_t *xq,
                                          const float *xg, int token, int pos, const float *rope, uint32_t tag,
-                                         int *err, int lane, unsigned long long *cta_amax, float &racc)
+                                         int *err, int lane, unsigned long long *cta_amax, float &racc,
+                                         float nscale)
 {
     const MvSeg &s = find_seg(p, t);
     const int r0 = (t - s.tile0) * s.R;
@@ -848,6 +850,7 @@ __device__ __forceinline__ void run_tile(const Phase &p, int t, int chunk, const
         va = racc;
         racc = 0.0f;
     }
+    va *= nscale;  // the RMSNorm scale of a normed input (stage_x), else 1
     // Epilogue: lane i owns row r0 + i.
     const int r = r0 + lane;
     if (p.epi == EPI_QKV) {
