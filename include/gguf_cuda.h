@@ -41,6 +41,18 @@ typedef struct {
 int gguf_cuda_matvec(const GGUFWeight *weight, const float *x, float *out, void *stream);
 
 /*
+ * Whether a gguf_cuda_matvec call on the current device has given up on a
+ * wait inside its kernel (a weight copy that did not complete in ~2 s)
+ * since the last query; read and cleared (synchronises the device). 0: no
+ * call's output was affected; 1: at least one call returned with rows it
+ * could not compute (their output is invalid); -1: the word cannot be
+ * read. Every call starts with a clean abort word, so one such event does
+ * not affect later calls. No counterpart in the reference, whose matvec
+ * has no device waits.
+ */
+int gguf_cuda_matvec_error(void);
+
+/*
  * Decode rows [row0, row0 + nrows) to FP32 into out (nrows * cols floats),
  * bit-identical to the reference's gguf_weight_dequantize_row
  * (include/gguf_model.h:112-116, src/gguf_model.c:314-359) and block
@@ -85,12 +97,25 @@ int gguf_cuda_fp16_table(float *out65536, void *stream);
  * - Calls on one device share the scratch: calls that may overlap in time
  *   (different streams, not ordered by events) race and can return wrong
  *   results. Serialise them, e.g. on one stream.
+ * - A wait inside the kernel that gives up (a weight copy that did not
+ *   complete in ~2 s) is recorded in the scratch header; read it with
+ *   gguf_cuda_matvec_noalloc_error().
  *
  * Returns 1 when the kernels were enqueued on `stream`, 0 otherwise with a
  * message in error[0 .. error_capacity) (may be NULL).
  */
 int gguf_cuda_matvec_noalloc(const GGUFWeight *weight, const float *x, float *out, void *stream,
                              char *error, size_t error_capacity);
+
+/*
+ * gguf_cuda_matvec_error for gguf_cuda_matvec_noalloc on the current
+ * device: read and clear the accumulated error word in the fixed scratch
+ * (cudaMemcpyFromSymbol / cudaMemcpyToSymbol, which allocate nothing and
+ * synchronise). 0: no call gave up on a wait since the last query; 1: at
+ * least one did (its output is invalid); -1: the word cannot be read. No
+ * counterpart in the reference.
+ */
+int gguf_cuda_matvec_noalloc_error(void);
 
 /*
  * Batched counterpart of gguf_cuda_matvec on the tensor cores: for n

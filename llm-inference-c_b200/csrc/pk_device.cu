@@ -47,10 +47,31 @@ struct DecodeArgs {
     const float *rope_cs;  // RoPE cos/sin table [position][rope_dim]
     int rope_dim;
     int *err;
+    // Seam launches (gguf_cuda_matvec and the no-allocation variant): err
+    // is the call's abort word (any wait that gives up records itself there
+    // and the other waits then stop); the last CTA to finish moves it into
+    // err[1], which accumulates until the caller reads it, and clears it, so
+    // the next call starts clean. err[2] counts finished CTAs.
+    int seam;
     unsigned long long *trace;  // optional: CTA 0's %globaltimer at start, then per phase: after
                                 //   staging x, after its work, and again at its end; then
                                 //   for every CTA and phase: after staging x, after its work
 };
+
+// End of a seam launch: the last CTA moves the abort word into the
+// caller-visible accumulated word and clears it (see DecodeArgs::seam).
+__device__ __forceinline__ void seam_finish(int *err)
+{
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    __threadfence();  // this CTA's error records precede its count
+    if (atomicAdd(err + 2, 1) == (int)gridDim.x - 1) {
+        __threadfence();
+        const int e = atomicExch(err, 0);
+        if (e != 0) atomicOr(err + 1, e);
+        atomicExch(err + 2, 0);
+    }
+}
 
 __device__ __forceinline__ unsigned long long global_ns()
 {
@@ -246,6 +267,7 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) phase_kernel(const __grid_co
         }
     }
     if (lane == 0 && r.issued != r.consumed) ring_drain(r);
+    if (a.seam) seam_finish(a.err);
 }
 
 // End of a decode step: the greedy token becomes the next step's input
@@ -530,7 +552,7 @@ static void fill_args(DecodeArgs &a, const Layout &L)
 
 // Launch one phase as its own kernel on `st`.
 static int launch_phase(const Phase &p, const int *step, int *err, cudaStream_t st, int grid_cap,
-                        const float *rope_cs = nullptr, int rope_dim = 0, PhaseFn fn = nullptr)
+                        const float *rope_cs = nullptr, int rope_dim = 0, PhaseFn fn = nullptr, int seam = 0)
 {
     if (fn == nullptr) fn = pick_variant(phase_formats(p));
     DecodeArgs a;
@@ -543,6 +565,7 @@ static int launch_phase(const Phase &p, const int *step, int *err, cudaStream_t 
     a.rope_cs = rope_cs;
     a.rope_dim = rope_dim;
     a.err = err;
+    a.seam = seam;
     Layout L;
     const int attn_floats = p.kind == PH_ATTN ? attn_scratch_floats(p.hs, DK_WARPS) : 0;
     const int stage = p.kind == PH_MV ? stage_need(p) : 128;
@@ -590,15 +613,33 @@ static int weight_ok(const GGUFWeight *w)
     return 1;
 }
 
-// One error word per device, allocated on first use (a timed-out wait in a
-// kernel records itself there).
+// The seam's error words per device (DecodeArgs::seam: abort word,
+// accumulated word, CTA count), allocated and zeroed on first use.
 static int *device_err_word()
 {
     static int *d_err[64] = {NULL};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return NULL;
-    if (d_err[dev] == NULL && cudaMalloc(&d_err[dev], sizeof(int)) != cudaSuccess) return NULL;
+    if (d_err[dev] == NULL) {
+        int *w = NULL;
+        if (cudaMalloc(&w, 4 * sizeof(int)) != cudaSuccess) return NULL;
+        if (cudaMemset(w, 0, 4 * sizeof(int)) != cudaSuccess) {
+            cudaFree(w);
+            return NULL;
+        }
+        d_err[dev] = w;
+    }
     return d_err[dev];
+}
+
+extern "C" int gguf_cuda_matvec_error(void)
+{
+    int *w = device_err_word();
+    if (w == NULL) return -1;
+    int v = 0;
+    if (cudaMemcpy(&v, w + 1, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (v != 0 && cudaMemset(w + 1, 0, sizeof(int)) != cudaSuccess) return -1;
+    return v != 0 ? 1 : 0;
 }
 
 extern "C" int gguf_cuda_matvec(const GGUFWeight *weight, const float *x, float *out, void *stream)
@@ -629,7 +670,7 @@ extern "C" int gguf_cuda_matvec(const GGUFWeight *weight, const float *x, float 
             (const uint8_t *)weight->data, weight->row_bytes, (int)weight->type, rows, (int)weight->cols, x, out);
         return cudaGetLastError() == cudaSuccess;
     }
-    return launch_phase(p, NULL, err, (cudaStream_t)stream, sm_count());
+    return launch_phase(p, NULL, err, (cudaStream_t)stream, sm_count(), nullptr, 0, nullptr, 1);
 }
 
 extern "C" int gguf_cuda_dequantize_rows(const GGUFWeight *weight, uint64_t row0, uint64_t nrows, float *out,
@@ -656,7 +697,8 @@ extern "C" int gguf_cuda_fp16_table(float *out65536, void *stream)
 // gguf_cuda_matvec_noalloc: the matvec with its scratch in device code //
 // ------------------------------------------------------------------ //
 
-// Scratch layout: [0, 256) header (word 0: error word of the tile kernel),
+// Scratch layout: [0, 256) header (words 0-2: the tile kernel's abort word,
+// accumulated error word and CTA count, as DecodeArgs::seam describes),
 // then the integer form of x for up to GGUF_CUDA_NOALLOC_MAX_COLS columns:
 // digits (XQ_UNIT_BYTES per unit) at NA_Q_OFF, group info (XG_UNIT_WORDS
 // words per unit) at NA_G_OFF - the layout stage_x writes to shared memory.
@@ -669,11 +711,10 @@ static_assert(NA_G_OFF % 16 == 0, "16-byte copies of the group info");
 
 static __device__ __align__(256) uint8_t na_scratch[NA_SCRATCH_BYTES];
 
-// One CTA: clear the error word, then write x's integer form into the
-// scratch (stage_x with global instead of shared destinations).
+// One CTA: write x's integer form into the scratch (stage_x with global
+// instead of shared destinations).
 __global__ void __launch_bounds__(DK_WARPS * 32, 1) na_stage_kernel(const __grid_constant__ Phase p, uint8_t *scratch)
 {
-    if (threadIdx.x == 0) *reinterpret_cast<int *>(scratch) = 0;
     stage_x(p, nullptr, scratch + NA_Q_OFF, reinterpret_cast<float *>(scratch + NA_G_OFF), 0u,
             reinterpret_cast<int *>(scratch));
 }
@@ -730,6 +771,7 @@ __global__ void __launch_bounds__(DK_WARPS * 32, 1) na_matvec_kernel(const __gri
         if (lane == 0 && ok) ring_fill(r, &p, 1, gw, W, NW);
     }
     if (lane == 0 && r.issued != r.consumed) ring_drain(r);
+    seam_finish(a.err);
 }
 
 static int na_fail(char *error, size_t cap, const char *msg)
@@ -762,6 +804,23 @@ static uint8_t *na_scratch_addr(char *error, size_t cap)
         addr[dev] = (uint8_t *)p;
     }
     return addr[dev];
+}
+
+extern "C" int gguf_cuda_matvec_noalloc_error(void)
+{
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, na_scratch, sizeof(int), sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    if (v != 0) {
+        const int zero = 0;
+        if (cudaMemcpyToSymbol(na_scratch, &zero, sizeof(int), sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) {
+            cudaGetLastError();
+            return -1;
+        }
+    }
+    return v != 0 ? 1 : 0;
 }
 
 extern "C" int gguf_cuda_matvec_noalloc(const GGUFWeight *weight, const float *x, float *out, void *stream,
@@ -1432,6 +1491,19 @@ static int finalize(PkdCtx *c, char *err, size_t cap)
     if (env_flag("POCKET_CUDA_TRACE", 0) &&
         cuda_fail(c, cudaMalloc(&c->trace_d, (size_t)(3 * c->nphases + 1 + 2 * c->grid * c->nphases) * 8), "cudaMalloc", err, cap)) {
         return 0;
+    }
+    // Failure-injection hook for tests: POCKET_CUDA_TEST_STALL=<phase>:<us>
+    // makes phase <phase>'s input polls wait for a tag that is never
+    // written, giving up after <us> microseconds (at 2 GHz), so that the
+    // step ends with a timed-out wait and the handle reports it.
+    const char *stall = getenv("POCKET_CUDA_TEST_STALL");
+    if (stall != NULL && *stall) {
+        int ph = -1;
+        long long us = 0;
+        if (sscanf(stall, "%d:%lld", &ph, &us) == 2 && ph >= 0 && ph < c->nphases && us > 0 &&
+            c->phases[ph].kind == PH_MV) {
+            c->phases[ph].stall = us * 2000;
+        }
     }
     unsigned need = 0u;
     for (int i = 0; i < c->nphases; i++) need |= phase_formats(c->phases[i]);

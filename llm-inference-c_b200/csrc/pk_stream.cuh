@@ -203,7 +203,7 @@ __device__ __forceinline__ float ll_read(const uint64_t *p, uint32_t tag, int *e
 // when n == 8), polled together so that both wait in one round trip per
 // retry; va/vb[e] = 0 for e >= n. Bounded as ll_read.
 __device__ __forceinline__ void ll_read8x2(const uint64_t *pa, const uint64_t *pb, int n, uint32_t tag, float *va,
-                                           float *vb, int *err)
+                                           float *vb, int *err, long long limit = LL_WAIT_LIMIT_CYCLES)
 {
     uint64_t w[16];
     long long t0 = 0;
@@ -232,7 +232,7 @@ __device__ __forceinline__ void ll_read8x2(const uint64_t *pa, const uint64_t *p
         } else {
             const long long dt = clock64() - t0;
             if (dt > LL_ABORT_CHECK_CYCLES && aborted(err)) break;
-            if (dt > LL_WAIT_LIMIT_CYCLES) {
+            if (dt > limit) {
                 atomicOr(err, ERR_TIMEOUT_WAIT);
                 break;
             }
@@ -247,7 +247,8 @@ __device__ __forceinline__ void ll_read8x2(const uint64_t *pa, const uint64_t *p
 
 // Values of the n (<= 8) tagged words at p (64-byte aligned when n == 8),
 // waiting (bounded) until all carry `tag`; v[e] = 0 for e >= n.
-__device__ __forceinline__ void ll_read8(const uint64_t *p, int n, uint32_t tag, float *v, int *err)
+__device__ __forceinline__ void ll_read8(const uint64_t *p, int n, uint32_t tag, float *v, int *err,
+                                         long long limit = LL_WAIT_LIMIT_CYCLES)
 {
     uint64_t w[8];
     long long t0 = 0;
@@ -270,7 +271,7 @@ __device__ __forceinline__ void ll_read8(const uint64_t *p, int n, uint32_t tag,
         } else {
             const long long dt = clock64() - t0;
             if (dt > LL_ABORT_CHECK_CYCLES && aborted(err)) break;
-            if (dt > LL_WAIT_LIMIT_CYCLES) {
+            if (dt > limit) {
                 atomicOr(err, ERR_TIMEOUT_WAIT);
                 break;
             }
@@ -316,6 +317,8 @@ struct MvSeg {
 // into shared memory.
 struct alignas(16) Phase {
     int kind, pro, epi;
+    long long stall;      // test hook, normally 0: > 0 makes this phase's input polls wait for
+                          // a tag no producer writes, giving up after `stall` cycles
     int off;              // work rotation: tile t goes to warp slot (t + off) % slots,
                           // attention item i to CTA (i + off) % CTAs
     int cta0, nct;        // the tiles go to the warps of CTAs [cta0, cta0 + nct) (mod the
@@ -593,6 +596,9 @@ __device__ __forceinline__ float stage_x(const Phase &p, const int *step, uint8_
         erow = p.embd + (size_t)step[0] * p.embd_rb;
         etype = p.embd_type;
     }
+    // the stall test hook polls for a tag that never comes, with a short limit
+    const uint32_t wtag = p.stall > 0 ? tag + 1u : tag;
+    const long long wlimit = p.stall > 0 ? p.stall : LL_WAIT_LIMIT_CYCLES;
     auto load8 = [&](int c0, float *v) {
 #pragma unroll
         for (int e = 0; e < 8; e++) v[e] = 0.0f;
@@ -605,12 +611,12 @@ __device__ __forceinline__ float stage_x(const Phase &p, const int *step, uint8_
             // hb = silu(gate) * up, src/gguf_forward.c:287-290
             if (c0 < n) {
                 float u[8];
-                ll_read8x2(p.xin_ll + c0, p.xin_ll + n + c0, min(8, n - c0), tag, v, u, err);
+                ll_read8x2(p.xin_ll + c0, p.xin_ll + n + c0, min(8, n - c0), wtag, v, u, err, wlimit);
 #pragma unroll
                 for (int e = 0; e < 8; e++) v[e] = swiglu(v[e], u[e]);
             }
         } else if (p.xin_ll != nullptr) {
-            if (c0 < n) ll_read8(p.xin_ll + c0, min(8, n - c0), tag, v, err);
+            if (c0 < n) ll_read8(p.xin_ll + c0, min(8, n - c0), wtag, v, err, wlimit);
         } else if (c0 + 8 <= n) {
             // x was written by other CTAs (possibly in this launch): read L2
             const float4 a = __ldcg(reinterpret_cast<const float4 *>(xin + c0));

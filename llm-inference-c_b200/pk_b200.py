@@ -30,6 +30,7 @@ EXPORTS = [
     "engine_tp_plan", "engine_open_tp", "engine_tp_handle", "engine_tp_connect",
     "engine_batch_open", "engine_forward_batch",
     "gguf_cuda_matvec", "gguf_cuda_dequantize_rows", "gguf_cuda_fp16_table", "gguf_cuda_matvec_noalloc",
+    "gguf_cuda_matvec_error", "gguf_cuda_matvec_noalloc_error",
     "gguf_cuda_matmul", "gguf_cuda_matmul_plan", "gguf_cuda_matmul_error",
     "tokenizer_free",
 ]
@@ -149,6 +150,10 @@ def lib(path=LIB_PATH):
     L.gguf_cuda_matvec_noalloc.restype = ctypes.c_int
     L.gguf_cuda_matvec_noalloc.argtypes = [ctypes.POINTER(GGUFWeight), _P, _P, _P, ctypes.c_char_p,
                                            ctypes.c_size_t]
+    L.gguf_cuda_matvec_error.restype = ctypes.c_int
+    L.gguf_cuda_matvec_error.argtypes = []
+    L.gguf_cuda_matvec_noalloc_error.restype = ctypes.c_int
+    L.gguf_cuda_matvec_noalloc_error.argtypes = []
     L.gguf_cuda_matmul.restype = ctypes.c_int
     L.gguf_cuda_matmul.argtypes = [ctypes.POINTER(GGUFWeight), _P, ctypes.c_int, _P, _P]
     L.gguf_cuda_matmul_plan.restype = None
@@ -329,6 +334,16 @@ def matvec_noalloc(weight, x_ptr, y_ptr, stream=0):
     err = ctypes.create_string_buffer(256)
     rc = lib().gguf_cuda_matvec_noalloc(ctypes.byref(weight), x_ptr, y_ptr, stream, err, 256)
     return rc, err.value.decode()
+
+
+def matvec_error():
+    """gguf_cuda_matvec_error: 1 if a matvec gave up on a wait since the last read, else 0 (-1: unreadable)."""
+    return lib().gguf_cuda_matvec_error()
+
+
+def matvec_noalloc_error():
+    """gguf_cuda_matvec_noalloc_error: the same for the no-allocation entry point."""
+    return lib().gguf_cuda_matvec_noalloc_error()
 
 
 def matmul(weight, x_ptr, n, y_ptr, stream=0):

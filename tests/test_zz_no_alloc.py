@@ -49,6 +49,7 @@ def test_noalloc_matches_matvec_on_two_calls_in_a_row(torch, qtype, rows, cols):
         assert rc == 1, msg
         assert msg == ""
     torch.cuda.synchronize()
+    assert pk_b200.matvec_noalloc_error() == 0  # no wait gave up in either call
     for a, b in zip(y_ref, y_na):
         a, b = a.cpu().numpy(), b.cpu().numpy()
         assert np.isfinite(a).all()
