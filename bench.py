@@ -19,8 +19,22 @@ heads, FFN hidden slice and vocabulary rows, and the decode kernels
 all-reduce the partial sums over NVLink peer memory; value = the sequence's
 tokens / the slowest rank's time. The roofline peak is N x the HBM figure.
 
+Extra objects of the default line:
+  b64     64 independent sequences after a 512-token context, 128 greedy
+          steps through engine_forward_batch.
+  matvec  (N = 1) the isolated fused dequant-matvec sweep, 8 shapes x 5
+          formats through gguf_cuda_matvec, GB/s of packed weights and the
+          fraction of the measured HBM peak, beside the reference's own
+          gguf_matvec on the same blocks (all host threads) and the relative
+          L2 distance of the outputs.
+  tp7b    the Llama-2-7B shape decoded tensor-parallel over the run's N GPUs
+          (N = 1: one GPU): tok/s, e2e, roofline against N x the HBM peak,
+          and whether the greedy tokens match a 1-GPU run of the same prompt.
+
   --impl reference   times the reference's own CPU engine (compiled from its
-                     sources into oracle/_ref) on the same model file.
+                     sources into oracle/_ref) on the same model file, with
+                     the same `config`; the model file, if missing, is
+                     written by the pk_synth_cli command.
   --workload matvec  the isolated fused dequant-matvec sweep (GB/s per type
                      and shape), printed as extra lines for profiling.
 """
@@ -49,6 +63,7 @@ WORKLOADS = {
                       prompt=32, context=8192),
 }
 PUBLISHED_TOKS = 8.03  # reference, TinyLlama-1.1B-Chat Q4_K_M, 8 threads (documentation/PERFORMANCE.md:60)
+VS_BASELINE_NOTE = "published 8.03 tok/s: reference on 8 laptop cores, real TinyLlama Q4_K_M file"
 
 # DRAM bytes (read + write) of one decode-step launch of phase_kernel, from
 # one ncu capture of that launch (the phase_kernel summary under profiles/:
@@ -73,11 +88,17 @@ def model_path(preset):
     return os.path.join(d, f"{preset}-{MODEL_SEED}.gguf")
 
 
-def ensure_model(preset, rank, barrier):
+def ensure_model(preset, rank, barrier, via_cli=False):
+    """The seeded synthetic GGUF file of `preset` (written once per box by
+    rank 0). via_cli: written by the pk_synth_cli command in a child process,
+    so that the caller never loads the writer library (the reference arm)."""
     path = model_path(preset)
     if rank == 0 and not os.path.exists(path):
         tmp = path + ".tmp"
-        pk_synth.write_model(tmp, preset, seed=MODEL_SEED)
+        if via_cli:
+            pk_synth.write_model_cli(tmp, preset, seed=MODEL_SEED)
+        else:
+            pk_synth.write_model(tmp, preset, seed=MODEL_SEED)
         os.replace(tmp, path)
     barrier()
     return path
@@ -172,27 +193,56 @@ def reference_decode(path, prompt, steps, warmup, budget_s):
                       f"{prompt}-id prompt, same model file, OMP_NUM_THREADS={cores}"}
 
 
+def _mix64(z):
+    """SplitMix64's output function on uint64 arrays (wrapping arithmetic),
+    as pks_uniform_ints in synth/gguf_synth.c computes it."""
+    z = z + np.uint64(0x9E3779B97F4A7C15)
+    z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+    z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+    return z ^ (z >> np.uint64(31))
+
+
+def uniform_ints(seed, n, lo, hi):
+    """pk_synth.uniform_ints without the writer library: lo + (mix64(seed ^
+    mix64(i)) mod (hi - lo)) for i < n."""
+    with np.errstate(over="ignore"):
+        i = np.arange(n, dtype=np.uint64)
+        r = _mix64(np.uint64(seed) ^ _mix64(i))
+    return (lo + (r % np.uint64(hi - lo)).astype(np.int64)).astype(np.int32)
+
+
 def prompt_ids(n, vocab, rank):
-    return pk_synth.uniform_ints(4242 + rank, n, 3, vocab)
+    return uniform_ints(4242 + rank, n, 3, vocab)
+
+
+def workload_config(wl, path, args, world, tp):
+    """The `config` of the B=1 line, identical in both arms."""
+    pos0 = wl["prompt"] + args.warmup
+    return {"workload": wl["name"], "model_file": os.path.basename(path), "batch_per_gpu": 1,
+            "prompt": wl["prompt"], "positions": [pos0, pos0 + args.steps - 1], "kv_cache": args.kv,
+            "parallelism": f"tensor parallel over {world} GPUs (one sequence)" if tp
+            else (f"data parallel: {world} GPUs, one independent sequence each" if world > 1 else "1 GPU"),
+            "l2": "weights streamed per step exceed the 126 MB L2 (no flush needed)"}
 
 
 def run_reference_arm(args, wl):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return 0
-    path = ensure_model(wl["preset"], 0, lambda: None)
+    path = ensure_model(wl["preset"], 0, lambda: None, via_cli=True)
     base = reference_decode(path, wl["prompt"], args.steps, args.warmup, budget_s=150.0)
-    cfg_line = {"workload": wl["name"], "model_file": os.path.basename(path), "batch": 1,
-                "prompt": wl["prompt"], "timed_steps": args.steps}
     if base is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref.so was not built"}))
         return 0
+    tp = world > 1 and (args.tp or args.workload != "tinyllama")
     line = {"metric": "decode tok/s (B=1)", "value": base["value"], "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / base["value"],
-            "higher_is_better": True, "scaling": "strong" if args.gpus > 1 else "weak",
+            "higher_is_better": True, "scaling": "strong" if tp else "weak",
             "vs_baseline": base["value"] / PUBLISHED_TOKS,
-            "dtype": "f32 (packed Q4_K/Q6_K weights)", "data": "synthetic random-init weights, seeded prompt",
-            "config": cfg_line, "impl": "reference", "cpu_baseline": base,
+            "dtype": "f32 (packed Q4_K/Q6_K weights)", "data": "synthetic random-init weights N(0,0.02), seeded prompt ids",
+            "vs_baseline_note": VS_BASELINE_NOTE,
+            "config": workload_config(wl, path, args, world, tp), "impl": "reference", "cpu_baseline": base,
             "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
     return 0
@@ -238,6 +288,159 @@ def run_matvec_sweep(args):
                               "GB/s": gbs, "frac_of_hbm": gbs / hbm}))
             del ws
     return 0
+
+
+MATVEC_TYPES = (("Q4_0", 2), ("Q8_0", 8), ("Q4_K", 12), ("Q5_K", 13), ("Q6_K", 14))
+MATVEC_SHAPES = ((2048, 2048), (256, 2048), (5632, 2048), (2048, 5632), (32000, 2048), (4096, 4096),
+                 (14336, 4096), (128256, 4096))
+
+
+def run_matvec_object(args):
+    """The isolated fused dequant-matvec sweep (8 shapes x 5 formats, x ~
+    N(0,1), weights N(0,0.02) quantized, one seed per shape) through
+    gguf_cuda_matvec: GB/s of packed weight bytes with CUDA events over
+    max(steps, 20) calls, rotating weight copies so that every call streams
+    from HBM (> 2x the L2 together); beside it the reference's own
+    gguf_matvec (src/gguf_model.c:693-771, OpenMP over all host threads) on
+    the same blocks and x, and the relative L2 distance of the two outputs."""
+    import torch
+    import pk_b200
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    ref = oracle.Reference() if oracle.ref_available() else None
+    hbm, peak_kind = peaks()
+    st = torch.cuda.current_stream().cuda_stream
+    entries = []
+    for name, qt in MATVEC_TYPES:
+        for rows, cols in MATVEC_SHAPES:
+            rb = pk_b200.row_bytes(qt, cols)
+            nbytes = rows * rb
+            copies = max(1, min(8, (512 << 20) // nbytes))
+            wb = pk_synth.random_matrix(qt, rows, cols, seed=rows + qt)
+            xh = pk_synth.gaussian(1, cols)
+            ws = [torch.from_numpy(wb).cuda() for _ in range(copies)]
+            x = torch.from_numpy(xh).cuda()
+            y = torch.empty(rows, device="cuda")
+            wts = [pk_b200.make_weight(w.data_ptr(), qt, rows, cols) for w in ws]
+            for i in range(3):
+                pk_b200.matvec(wts[i % copies], x.data_ptr(), y.data_ptr(), st)
+            reps = max(args.steps, 20)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            for i in range(reps):
+                pk_b200.matvec(wts[i % copies], x.data_ptr(), y.data_ptr(), st)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            gbs = nbytes / (us * 1e-6) / 1e9
+            ent = {"type": name, "rows": rows, "cols": cols, "bytes": nbytes, "us": round(us, 2),
+                   "GB/s": round(gbs, 1), "frac": round(gbs / hbm, 4)}
+            if ref is not None:
+                got = y.cpu().numpy()
+                t0, n = time.perf_counter(), 0
+                while n < 3 and (n == 0 or time.perf_counter() - t0 < 0.3):
+                    want = ref.matvec(qt, wb, rows, cols, xh)
+                    n += 1
+                cpu_s = (time.perf_counter() - t0) / n
+                ent["cpu_GB/s"] = round(nbytes / cpu_s / 1e9, 2)
+                ent["vs_cpu"] = round(gbs / ent["cpu_GB/s"], 1)
+                ent["rel_l2_vs_reference"] = float(np.linalg.norm(got - want) / np.linalg.norm(want))
+            entries.append(ent)
+            del ws, wts
+    fr = np.array([e["frac"] for e in entries])
+    return {"metric": "fused dequant-matvec GB/s of packed weights (gguf_cuda_matvec)", "unit": "GB/s",
+            "peak": hbm, "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs",
+            "geomean_frac": float(np.exp(np.log(fr).mean())), "max_frac": float(fr.max()),
+            "cpu": None if ref is None else {"kind": "reference", "function": "gguf_matvec",
+                                             "cores": os.cpu_count(),
+                                             "threads": int(os.environ.get("OMP_NUM_THREADS", "0") or 0)},
+            "l2": "weight copies rotated so that consecutive calls read > 2x the 126 MB L2",
+            "entries": entries}
+
+
+def run_tp7b(args, world, rank, local, barrier, allmax):
+    """Llama-2-7B shape, Q4_K_M mix, one sequence decoded tensor-parallel over
+    the N GPUs of the run (N = 1: the single-GPU engine): a 32-id prompt,
+    W warm-up steps, then K timed greedy steps (CUDA events around the
+    device-resident loop, slowest rank), and the same steps through
+    engine_forward with host logits (e2e). At N > 1, rank 0 first decodes
+    the same prompt on one GPU; tokens_match_n1 says whether the N-GPU run
+    produced the same greedy tokens."""
+    import torch
+    import pk_b200
+    wl = WORKLOADS["llama2-7b"]
+    path = ensure_model(wl["preset"], rank, barrier)
+    P, W, K = wl["prompt"], args.warmup, args.steps
+    ctx = P + W + K + 16
+    prompt = prompt_ids(P, 32000, 0)
+
+    def feed(e):
+        lg = None
+        for pos, t in enumerate(prompt):
+            lg = e.forward(int(t), pos)
+        return int(np.argmax(lg))
+
+    ref_toks = None
+    if world > 1 and rank == 0:
+        e1 = pk_b200.Engine(path, ctx, device=local)
+        first = feed(e1)
+        wt, _ = e1.generate_greedy(first, P, W)
+        t1, _ = e1.generate_greedy(int(wt[-1]), P + W, K)
+        ref_toks = [first] + [int(t) for t in wt] + [int(t) for t in t1]
+        e1.close()
+    barrier()
+    if world > 1:
+        e = pk_b200.Engine(path, ctx, device=local, rank=rank, world=world)
+        e.tp_connect(pk_b200.tp_exchange(e.tp_handle(), world))
+    else:
+        e = pk_b200.Engine(path, ctx, device=local)
+    cfg = e.config
+    first = feed(e)
+    wt, _ = e.generate_greedy(first, P, W)
+    barrier()
+    torch.cuda.synchronize()
+    toks, ms = e.generate_greedy(int(wt[-1]), P + W, K)
+    torch.cuda.synchronize()
+    barrier()
+    mine = [first] + [int(t) for t in wt] + [int(t) for t in toks]
+    # e2e: the same positions through engine_forward, host logits, host argmax
+    feed(e)
+    for i in range(W):
+        e.forward(first if i == 0 else mine[i], P + i)
+    L = pk_b200.lib()
+    tok = mine[W]
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(K):
+        p = L.engine_forward(e.h, tok, P + W + i)
+        tok = int(np.argmax(np.ctypeslib.as_array(p, shape=(e.vocab_size,))))
+    e2e_s = time.perf_counter() - t0
+    barrier()
+    launches = e.launches_per_step()
+    e.close()
+    ms_max, e2e_max = allmax([ms, e2e_s * 1000.0])
+    if rank != 0:
+        return None
+    hbm, peak_kind = peaks()
+    wbytes = pk_synth.weight_bytes_per_token(wl["preset"])
+    kvb = kv_bytes_per_step(cfg, list(range(P + W, P + W + K)), kv_entry_bytes())
+    step_s = ms_max / 1000.0 / K
+    achieved = (wbytes + kvb) / step_s / 1e9
+    return {"metric": "decode tok/s (B=1), Llama-2-7B arch Q4_K_M", "value": K / (ms_max / 1000.0),
+            "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_max / K,
+            "config": {"workload": wl["name"], "model_file": os.path.basename(path), "prompt": P,
+                       "positions": [P + W, P + W + K - 1],
+                       "parallelism": f"tensor parallel over {world} GPUs" if world > 1 else "1 GPU"},
+            "tokens_match_n1": (ref_toks == mine) if world > 1 else True,
+            "e2e": {"value": K / (e2e_max / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": 12,
+                    "d2h_bytes_per_step": 4 * cfg["vocab_size"] + 20,
+                    "path": "engine_forward (host logits) + host argmax, every rank"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm * world, "unit": "GB/s",
+                         "frac": achieved / (hbm * world), "algorithmic_bytes_per_step": wbytes + kvb,
+                         "weight_bytes_per_step": wbytes,
+                         "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs x {world} GPUs"},
+            "gpu_launches_per_step": launches}
 
 
 def run_matmul_sweep(args):
@@ -407,15 +610,20 @@ def main():
                     choices=list(WORKLOADS) + ["matvec", "matmul", "b64", "trace"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", default=None, help="matvec workload: one TYPE:ROWSxCOLS case")
-    ap.add_argument("--b64-steps", type=int, default=32, help="timed steps of the B=64 batched decode (0: skip)")
+    ap.add_argument("--b64-steps", type=int, default=128, help="timed steps of the B=64 batched decode (0: skip)")
     ap.add_argument("--b64-context", type=int, default=512, help="tokens decoded into each sequence's KV cache first")
     ap.add_argument("--kv", default="f32", choices=["f32", "f16"],
                     help="KV cache entries (f16: the half cache option, POCKET_CUDA_KV)")
     ap.add_argument("--tp", action="store_true",
                     help="N > 1 on the TinyLlama shape: one sequence tensor-parallel instead of one per GPU")
+    ap.add_argument("--no-matvec", action="store_true", help="skip the matvec sweep object of the default line")
+    ap.add_argument("--no-tp7b", action="store_true", help="skip the Llama-2-7B tensor-parallel object")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     os.environ["POCKET_CUDA_KV"] = args.kv
+    # the synthetic-model writer and the reference's CPU kernels (OpenMP) use
+    # every host thread
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
 
     if args.workload == "matvec":
         return run_matvec_sweep(args)
@@ -453,6 +661,12 @@ def main():
     def barrier():
         if world > 1:
             dist.barrier()
+
+    def allmax(vals):
+        t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(v) for v in t]
 
     path = ensure_model(wl["preset"], rank, barrier)
     need = wl["prompt"] + args.warmup + args.steps + 1
@@ -541,6 +755,13 @@ def main():
         b64["roofline"]["peak"] = hbm
         b64["roofline"]["frac"] = b64["roofline"]["achieved"] / hbm
 
+    matvec = None
+    if rank == 0 and world == 1 and not args.no_matvec and args.workload == "tinyllama":
+        matvec = run_matvec_object(args)
+    tp7b = None
+    if not args.no_tp7b and args.workload == "tinyllama":
+        tp7b = run_tp7b(args, world, rank, local, barrier, allmax)
+
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         base = reference_decode(path, wl["prompt"], 64, 2, budget_s=15.0)
@@ -554,16 +775,8 @@ def main():
             "vs_baseline": value / PUBLISHED_TOKS,
             "dtype": "f32 (packed Q4_K/Q6_K weights)",
             "data": "synthetic random-init weights N(0,0.02), seeded prompt ids",
-            "config": {"workload": wl["name"], "model_file": os.path.basename(path),
-                       "batch_per_gpu": 1 if not tp else 1.0 / world,
-                       "prompt": wl["prompt"], "positions": [pos0, pos0 + args.steps - 1],
-                       "kv_cache": args.kv,
-                       "parallelism": f"tensor parallel over {world} GPUs (one sequence)" if tp
-                       else (f"data parallel: {world} GPUs, one independent sequence each" if world > 1
-                             else "1 GPU"),
-                       "l2": f"weights {wbytes / 1e6:.0f} MB streamed per step > 126 MB L2 (no flush needed)",
-                       "vs_baseline_note": "published 8.03 tok/s: reference on 8 laptop cores, real TinyLlama "
-                                           "Q4_K_M file"},
+            "vs_baseline_note": VS_BASELINE_NOTE,
+            "config": workload_config(wl, path, args, world, tp),
             "e2e": {"value": replicas * args.steps / (e2e_ms_max / 1000.0), "unit": "tok/s",
                     "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4 * e.vocab_size + 20,
                     "path": "engine_forward (host logits) + host argmax",
@@ -579,6 +792,8 @@ def main():
                                          else "fallback 6.65 TB/s") + (f" x {world} GPUs" if world > 1 else "")},
             "cpu_baseline": base,
             "b64": b64,
+            "matvec": matvec,
+            "tp7b": tp7b,
             "clocks": clocks.summary(),
             "gpu_launches": launches_per_step * args.steps,
         }

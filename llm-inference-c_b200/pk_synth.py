@@ -127,6 +127,22 @@ def write_model(path, preset, seed=1234, **overrides):
     return path
 
 
+CLI = os.path.join(HERE, "lib", "pk_synth_cli")
+
+
+def write_model_cli(path, preset, seed=1234, weight_std=0.02, rms_eps=1e-5, **overrides):
+    """write_model through the pk_synth_cli command: the same file, written by
+    a child process, so the caller never loads the writer library."""
+    d = dict(PRESETS[preset])
+    d.update(overrides)
+    d.update(rms_eps=rms_eps, weight_std=weight_std, seed=seed)
+    args = [CLI, path] + [f"{k}={v!r}" if isinstance(v, float) else f"{k}={int(v)}" for k, v in d.items()]
+    r = subprocess.run(args, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("pk_synth_cli failed: " + r.stderr.strip())
+    return path
+
+
 def weight_bytes_per_token(preset, **overrides):
     """Algorithmic weight bytes read per decoded token: every projection,
     the norms (F32) and one embedding row."""

@@ -12,6 +12,19 @@ for sub in ("oracle", "llm-inference-c_b200"):
 GOLDEN = os.path.join(ROOT, "tests", "golden")
 
 
+def reference_root():
+    """The reference checkout the oracle recipe built from (REF_ROOT in the
+    environment, else the root oracle/Makefile recorded), or None."""
+    env = os.environ.get("REF_ROOT")
+    if env:
+        return env
+    rec = os.path.join(ROOT, "oracle", "_ref", "ref_root.txt")
+    if os.path.exists(rec):
+        root = open(rec).read().strip()
+        return root if os.path.isdir(root) else None
+    return None
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
     config.addinivalue_line("markers", "slow: full-size model cases")

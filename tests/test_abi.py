@@ -11,7 +11,7 @@ import pytest
 
 import gguf_min
 import pk_b200
-from conftest import ROOT
+from conftest import ROOT, reference_root
 
 
 def declared_functions():
@@ -66,7 +66,8 @@ def test_struct_layouts_match_reference(tmp_path):
     gguf_model.h:36-45), checked by compiling both header sets."""
     mine = _layout(os.path.join(ROOT, "include"), "gguf_cuda.h", tmp_path, "mine")
     assert "GGUFWeight 56" in mine and "Config 44" in mine
-    ref_inc = "/root/reference/include"
+    root = reference_root()
+    ref_inc = os.path.join(root, "include") if root else ""
     if not os.path.isdir(ref_inc):
         pytest.skip("reference headers not present")
     assert mine == _layout(ref_inc, "gguf_model.h", tmp_path, "ref")

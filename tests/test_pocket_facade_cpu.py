@@ -18,9 +18,10 @@ import pytest
 
 import pk_synth
 import pocket_ctypes as pc
-from conftest import GOLDEN
+from conftest import GOLDEN, reference_root
 
-REF_PY = "/root/reference/python"
+_ROOT = reference_root()
+REF_PY = os.path.join(_ROOT, "python") if _ROOT else ""
 
 
 def need(path):
