@@ -69,6 +69,10 @@ PRESETS = {
     # for 2 and 4 ranks (512 / 256 Wo columns, 8 hidden blocks), 3 layers.
     "tp-q4km": dict(dim=1024, hidden_dim=2048, n_layers=3, n_heads=8, n_kv_heads=2,
                     vocab_size=2048, context_length=512, rope_theta=10000.0, **_q4km()),
+    # ... and for 8 ranks: 2 query heads of 128 (one Q4_K block of Wo columns)
+    # per rank, 4 KV heads shared by pairs of ranks, 2 hidden blocks per rank.
+    "tp8-q4km": dict(dim=2048, hidden_dim=4096, n_layers=2, n_heads=16, n_kv_heads=4,
+                     vocab_size=4096, context_length=512, rope_theta=10000.0, **_q4km()),
     "tiny-float": dict(dim=128, hidden_dim=256, n_layers=2, n_heads=4, n_kv_heads=2,
                        vocab_size=300, context_length=128, rope_theta=10000.0,
                        t_embd=F16, t_output=F32, t_q=F32, t_k=F16, t_v_even=F32, t_v_odd=F16,

@@ -1,5 +1,6 @@
-"""Tensor-parallel decode (engine_open_tp / engine_tp_connect) on 2 and 4
-GPUs against the oracle's single-process forward of the same model.
+"""Tensor-parallel decode (engine_open_tp / engine_tp_connect) on 2, 4 and 8
+GPUs against the oracle's single-process forward of the same model (at 4
+and 8 ranks there are more ranks than KV heads, so ranks share KV heads).
 
 One spawned process per GPU; the ranks exchange their 64-byte handles over
 gloo on the host, then decode the same token sequence. Every rank's
@@ -67,11 +68,11 @@ def _oracle(orc, path):
     return np.stack(logits), toks
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tensor_parallel_decode_matches_oracle(orc, synth_model, tmp_path, world):
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")
-    path = synth_model("tp-q4km")
+    path = synth_model("tp8-q4km" if world == 8 else "tp-q4km")
     ctx = mp.get_context("spawn")
     port = _free_port()
     procs = [ctx.Process(target=_rank, args=(r, world, port, path, str(tmp_path))) for r in range(world)]
