@@ -118,8 +118,10 @@ int engine_batch_open(LLMModel *model, int max_seqs, char *error, size_t error_c
 /* One step over n <= 64 rows: sequence seq_ids[i] consumes tokens[i] at
  * position pos[i] (seq_ids below max_seqs; tokens in the vocabulary;
  * positions below the context length; each (sequence, position) at most
- * once per call), exactly as engine_forward(tokens[i], pos[i]) would for
- * that sequence alone. Rows of one sequence at consecutive positions form a
+ * once per call; no gaps: positions 0 .. pos[i] - 1 of the sequence were
+ * filled by earlier calls, by engine_kv_write or by rows of this call),
+ * exactly as engine_forward(tokens[i], pos[i]) would for that sequence
+ * alone. Rows of one sequence at consecutive positions form a
  * prompt chunk (prefill): every row's keys and values are appended before
  * any row attends, so row i sees the sequence's positions 0 .. pos[i].
  * next_tokens[i] receives the greedy token of row i (device argmax, lowest
@@ -128,6 +130,20 @@ int engine_batch_open(LLMModel *model, int max_seqs, char *error, size_t error_c
  * (engine_last_error). */
 int engine_forward_batch(LLMModel *model, const int *tokens, const int *pos, const int *seq_ids, int n,
                          int *next_tokens, float *logits);
+
+/* Set the keys and values of positions [pos0, pos0 + npos) of layer `layer`
+ * directly: seq -1 for the cache engine_forward uses, seq >= 0 for a
+ * batched sequence (after engine_batch_open; pos0 must not leave a gap
+ * after the sequence's filled positions, and the written positions count
+ * as filled). k and v are npos rows of n_kv_heads * head_size floats (all
+ * KV heads; a tensor-parallel rank keeps its own), stored as the cache holds
+ * them (float, or rounded to half with POCKET_CUDA_KV=f16). This is how a
+ * caller restores a saved context, and how the parity tests reach long
+ * contexts without decoding them (the reference's CPU engine takes the same
+ * rows into its GGUFTransformer state, include/gguf_forward.h:20-31). No
+ * counterpart in the reference's engine.h. Returns 1, or 0 with a message. */
+int engine_kv_write(LLMModel *model, int seq, int layer, int pos0, int npos, const float *k, const float *v,
+                    char *error, size_t error_capacity);
 
 #ifdef __cplusplus
 }

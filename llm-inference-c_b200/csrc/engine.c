@@ -108,6 +108,8 @@ struct LLMModel {
     int connected;     /* the decode step exists (tensor parallel: after engine_tp_connect) */
     int batch_seqs;    /* sequences of the batched state */
     int kv_half;       /* KV cache entries in IEEE half (POCKET_CUDA_KV=f16) */
+    int kv_head0, kv_heads;  /* this rank's KV heads (all of them on one GPU) */
+    int *filled;       /* batched sequences: positions 0 .. filled[s] - 1 hold K/V */
     char last_error[256];
 };
 
@@ -618,6 +620,7 @@ void engine_close(LLMModel *m)
     if (m == NULL) return;
     tokenizer_free(&m->tokenizer);
     pkb_destroy(m->batch);
+    free(m->filled);
     pkd_destroy(m->dev);
     free(m);
 }
@@ -832,6 +835,8 @@ static LLMModel *open_impl(const LLMOptions *o, int device, int rank, int world,
         dm.n_kv_heads = tp.kv_heads;
         dm.head_size = (int)hs;
         dm.tp = tp;
+        m->kv_head0 = tp.kv_head0;
+        m->kv_heads = tp.kv_heads;
         dm.vocab_size = c->vocab_size;
         dm.seq_len = ctx;
         dm.rope_dim = c->rope_dim;
@@ -973,6 +978,13 @@ int engine_batch_open(LLMModel *m, int max_seqs, char *err, size_t cap)
         return 0;
     }
     pkb_destroy(m->batch);  /* a new open drops the old sequences */
+    m->batch = NULL;
+    free(m->filled);
+    m->filled = (int *)calloc((size_t)max_seqs, sizeof(int));
+    if (m->filled == NULL) {
+        seterr(err, cap, "Out of memory.");
+        return 0;
+    }
     m->batch = pkb_create(m->dev, max_seqs, err, cap);
     if (m->batch == NULL) return 0;
     m->batch_seqs = max_seqs;
@@ -993,11 +1005,84 @@ int engine_forward_batch(LLMModel *m, const int *tokens, const int *pos, const i
         for (int j = 0; j < i; j++)  /* each (sequence, position) once per step */
             if (seq_ids[j] == seq_ids[i] && pos[j] == pos[i]) return 0;
     }
+    /* No gaps: a row at position p of sequence s needs K/V at 0 .. p - 1,
+     * from earlier steps (filled[s]) or from rows of this call (every
+     * position in [filled[s], p) among them). */
+    for (int i = 0; i < n; i++) {
+        const int s0 = seq_ids[i], f = m->filled[s0];
+        if (pos[i] <= f) continue;
+        int have = 0;
+        for (int j = 0; j < n; j++)
+            if (seq_ids[j] == s0 && pos[j] >= f && pos[j] < pos[i]) have++;
+        if (have != pos[i] - f) {
+            snprintf(m->last_error, sizeof(m->last_error),
+                     "Sequence %d has no K/V at positions %d .. %d (row at position %d).", s0, f, pos[i] - 1,
+                     pos[i]);
+            return 0;
+        }
+    }
     if (!pkb_step(m->batch, tokens, pos, seq_ids, n, next_tokens, logits)) {
         snprintf(m->last_error, sizeof(m->last_error), "%s", pkb_error(m->batch));
         return 0;
     }
+    for (int i = 0; i < n; i++)
+        if (pos[i] + 1 > m->filled[seq_ids[i]]) m->filled[seq_ids[i]] = pos[i] + 1;
     return 1;
+}
+
+int engine_kv_write(LLMModel *m, int seq, int layer, int pos0, int npos, const float *k, const float *v,
+                    char *err, size_t cap)
+{
+    if (m == NULL || m->dev == NULL || k == NULL || v == NULL || npos < 0) {
+        seterr(err, cap, "Invalid arguments.");
+        return 0;
+    }
+    const Config *c = &m->config;
+    if (layer < 0 || layer >= c->n_layers || pos0 < 0 || pos0 > c->seq_len - npos) {
+        seterr(err, cap, "KV write outside the cache (layer or positions).");
+        return 0;
+    }
+    if (seq >= 0 && (m->batch == NULL || seq >= m->batch_seqs)) {
+        seterr(err, cap, "No such batched sequence.");
+        return 0;
+    }
+    if (seq >= 0 && pos0 > m->filled[seq]) {
+        seterr(err, cap, "KV write would leave a gap after the sequence's filled positions.");
+        return 0;
+    }
+    if (seq < -1) {
+        seterr(err, cap, "Invalid sequence.");
+        return 0;
+    }
+    if (npos == 0) return 1;
+    /* the caller's rows hold every KV head; a tensor-parallel rank keeps its own */
+    const size_t hs = (size_t)(c->dim / c->n_heads), kvd = hs * (size_t)c->n_kv_heads;
+    const size_t c0 = (size_t)m->kv_head0 * hs, cn = (size_t)m->kv_heads * hs;
+    const float *kp = k, *vp = v;
+    float *tk = NULL, *tv = NULL;
+    if (cn != kvd) {
+        tk = (float *)malloc((size_t)npos * cn * sizeof(float));
+        tv = (float *)malloc((size_t)npos * cn * sizeof(float));
+        if (tk == NULL || tv == NULL) {
+            free(tk);
+            free(tv);
+            seterr(err, cap, "Out of memory.");
+            return 0;
+        }
+        for (int i = 0; i < npos; i++) {
+            memcpy(tk + (size_t)i * cn, k + (size_t)i * kvd + c0, cn * sizeof(float));
+            memcpy(tv + (size_t)i * cn, v + (size_t)i * kvd + c0, cn * sizeof(float));
+        }
+        kp = tk;
+        vp = tv;
+    }
+    const int ok = seq < 0 ? pkd_kv_write(m->dev, layer, pos0, npos, kp, vp, err, cap)
+                           : pkb_kv_write(m->batch, seq, layer, pos0, npos, kp, vp, err, cap);
+    free(tk);
+    free(tv);
+    if (ok && seq >= 0 && pos0 + npos > m->filled[seq]) m->filled[seq] = pos0 + npos;
+    if (ok && err && cap) err[0] = '\0';
+    return ok;
 }
 
 int engine_trace(LLMModel *m, unsigned long long *out, int cap)

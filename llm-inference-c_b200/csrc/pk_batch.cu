@@ -648,6 +648,29 @@ static int bfail(PkbCtx *b, cudaError_t e, const char *what)
     return 1;
 }
 
+extern "C" int pkb_kv_write(PkbCtx *b, int seq, int layer, int pos0, int npos, const float *k, const float *v,
+                            char *err, size_t cap)
+{
+    if (b == NULL || k == NULL || v == NULL) return 0;
+    const PkdModel &m = b->m;
+    if (seq < 0 || seq >= b->max_seqs || layer < 0 || layer >= m.n_layers || pos0 < 0 || npos < 0 ||
+        pos0 > m.seq_len - npos) {
+        if (err && cap) snprintf(err, cap, "KV write outside the cache.");
+        return 0;
+    }
+    cudaSetDevice(b->device);
+    const size_t kvd = (size_t)m.head_size * (size_t)m.n_kv_heads;
+    const size_t off = (((size_t)seq * m.n_layers + layer) * (size_t)m.seq_len + (size_t)pos0) * kvd;
+    const size_t n = (size_t)npos * kvd;
+    cudaError_t e = pk::kv_upload(b->kc, m.kv_half, off, k, n, b->st);
+    if (e == cudaSuccess) e = pk::kv_upload(b->vc, m.kv_half, off, v, n, b->st);
+    if (e != cudaSuccess) {
+        if (err && cap) snprintf(err, cap, "CUDA KV write failed: %s", cudaGetErrorString(e));
+        return 0;
+    }
+    return 1;
+}
+
 // y (n x rows) = x (n x cols) W^T for one weight tensor.
 static int bmatmul(PkbCtx *b, const PkdTensor &t, const float *x, int n, float *y, cudaStream_t st = nullptr)
 {

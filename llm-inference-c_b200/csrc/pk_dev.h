@@ -95,6 +95,12 @@ int pkd_generate_greedy(PkdCtx *ctx, int token, int pos, int n, int *out, float 
  * after staging x, after the work. Returns the count. */
 int pkd_trace(PkdCtx *ctx, unsigned long long *out, int cap);
 
+/* Write positions [pos0, pos0 + npos) of layer `layer` of the decode-step
+ * KV cache: k and v are npos rows of this rank's kv_dim floats each (stored
+ * as the cache holds them: float, or rounded to half). Synchronous. */
+int pkd_kv_write(PkdCtx *ctx, int layer, int pos0, int npos, const float *k, const float *v, char *err,
+                 size_t cap);
+
 /* Last device error message ("" if none). */
 const char *pkd_error(const PkdCtx *ctx);
 
@@ -134,6 +140,10 @@ void pkb_destroy(PkbCtx *b);
  * Returns 1, or 0 on a device error (message in pkb_error). */
 int pkb_step(PkbCtx *b, const int *tokens, const int *pos, const int *seq_ids, int n, int *next, float *logits);
 const char *pkb_error(const PkbCtx *b);
+
+/* pkd_kv_write for sequence `seq` of the batched state. */
+int pkb_kv_write(PkbCtx *b, int seq, int layer, int pos0, int npos, const float *k, const float *v, char *err,
+                 size_t cap);
 
 #ifdef __cplusplus
 }

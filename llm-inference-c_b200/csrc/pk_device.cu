@@ -1648,6 +1648,22 @@ extern "C" int pkd_trace(PkdCtx *c, unsigned long long *out, int cap)
     return n;
 }
 
+extern "C" int pkd_kv_write(PkdCtx *c, int layer, int pos0, int npos, const float *k, const float *v, char *err,
+                            size_t cap)
+{
+    if (c == NULL || c->kc == NULL || k == NULL || v == NULL) return 0;
+    const PkdModel &m = c->model;
+    if (layer < 0 || layer >= m.n_layers || pos0 < 0 || npos < 0 || pos0 > m.seq_len - npos) {
+        if (err && cap) snprintf(err, cap, "KV write outside the cache.");
+        return 0;
+    }
+    cudaSetDevice(c->device);
+    const size_t kvd = (size_t)m.head_size * (size_t)m.tp.kv_heads;
+    const size_t off = ((size_t)layer * (size_t)m.seq_len + (size_t)pos0) * kvd, n = (size_t)npos * kvd;
+    return !cuda_fail(c, kv_upload(c->kc, m.kv_half, off, k, n, c->stream), "KV write", err, cap) &&
+           !cuda_fail(c, kv_upload(c->vc, m.kv_half, off, v, n, c->stream), "KV write", err, cap);
+}
+
 extern "C" const char *pkd_error(const PkdCtx *c)
 {
     return c ? c->msg : "";

@@ -24,7 +24,9 @@
 //   F32 / F16   : columns 64u .. 64u+63 (guarded at the row end)
 #pragma once
 #include <cuda_fp16.h>
+#include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 namespace pk {
 
@@ -564,6 +566,26 @@ __device__ __forceinline__ float4 kv_load4(const __half *p, size_t i)
     const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
     const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
     return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// Host: copy n float entries into a KV cache at entry offset `off`, as the
+// cache holds them (float, or IEEE half rounded to nearest even), on `st`,
+// then wait. Returns the CUDA error.
+static inline cudaError_t kv_upload(void *cache, int half, size_t off, const float *src, size_t n, cudaStream_t st)
+{
+    if (!half) {
+        cudaError_t e = cudaMemcpyAsync(static_cast<float *>(cache) + off, src, n * sizeof(float),
+                                        cudaMemcpyHostToDevice, st);
+        return e != cudaSuccess ? e : cudaStreamSynchronize(st);
+    }
+    __half *h = static_cast<__half *>(malloc(n * sizeof(__half)));
+    if (h == nullptr) return cudaErrorMemoryAllocation;
+    for (size_t i = 0; i < n; i++) h[i] = __float2half_rn(src[i]);
+    cudaError_t e = cudaMemcpyAsync(static_cast<__half *>(cache) + off, h, n * sizeof(__half),
+                                    cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    free(h);
+    return e;
 }
 
 }  // namespace pk

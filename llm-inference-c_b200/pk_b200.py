@@ -28,7 +28,7 @@ EXPORTS = [
     "engine_is_stop_token", "engine_open_device", "engine_forward_greedy", "engine_last_error",
     "engine_weight_bytes", "engine_generate_greedy", "engine_trace", "engine_launches_per_step",
     "engine_tp_plan", "engine_open_tp", "engine_tp_handle", "engine_tp_connect",
-    "engine_batch_open", "engine_forward_batch",
+    "engine_batch_open", "engine_forward_batch", "engine_kv_write",
     "gguf_cuda_matvec", "gguf_cuda_dequantize_rows", "gguf_cuda_fp16_table", "gguf_cuda_matvec_noalloc",
     "gguf_cuda_matvec_error", "gguf_cuda_matvec_noalloc_error",
     "gguf_cuda_matmul", "gguf_cuda_matmul_plan", "gguf_cuda_matmul_error",
@@ -140,6 +140,9 @@ def lib(path=LIB_PATH):
     L.engine_batch_open.argtypes = [_P, ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t]
     L.engine_forward_batch.restype = ctypes.c_int
     L.engine_forward_batch.argtypes = [_P, _P, _P, _P, ctypes.c_int, _P, _P]
+    L.engine_kv_write.restype = ctypes.c_int
+    L.engine_kv_write.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P,
+                                  ctypes.c_char_p, ctypes.c_size_t]
     L.gguf_cuda_matvec.restype = ctypes.c_int
     L.gguf_cuda_matvec.argtypes = [ctypes.POINTER(GGUFWeight), _P, _P, _P]
     L.gguf_cuda_dequantize_rows.restype = ctypes.c_int
@@ -234,6 +237,16 @@ class Engine:
         if ok != 1:
             return None
         return nxt[:n], lg
+
+    def kv_write(self, layer, pos0, k, v, seq=-1):
+        """engine_kv_write: rows pos0 .. of layer `layer` (k, v: npos x kv_dim
+        floats, every KV head); seq -1 is engine_forward's cache."""
+        k = np.ascontiguousarray(k, dtype=np.float32)
+        v = np.ascontiguousarray(v, dtype=np.float32)
+        npos = k.shape[0] if k.ndim > 1 else 1
+        err = ctypes.create_string_buffer(256)
+        if lib().engine_kv_write(self.h, seq, layer, pos0, npos, k.ctypes.data, v.ctypes.data, err, 256) != 1:
+            raise RuntimeError("engine_kv_write failed: " + err.value.decode())
 
     def generate_greedy(self, token, pos, n):
         """n device-side greedy steps: (tokens, device milliseconds)."""

@@ -143,7 +143,9 @@ def test_open_close_cycles(synth_model):
 @pytest.mark.slow
 def test_tinyllama_shape_greedy_128_steps(orc, synth_model):
     """TinyLlama-1.1B shape, Q4_K_M mix: 32 seeded prompt ids, then 128
-    greedy steps identical to the oracle; logits within 1e-3 where checked."""
+    greedy steps on the device identical to the oracle's; then the same 128
+    steps again through engine_forward with the logits of every step within
+    1e-3 of the oracle's."""
     path = synth_model("tinyllama-1.1b-q4km", seed=1234)
     e, o = pk_b200.Engine(path, 2048), orc.open(path, 2048)
     prompt = pk_synth.uniform_ints(42, 32, 3, o.vocab_size)
@@ -157,8 +159,11 @@ def test_tinyllama_shape_greedy_128_steps(orc, synth_model):
     dev_tokens, _ = e.generate_greedy(tok, 32, 128)
     ref_tokens = []
     for step in range(128):
+        a = e.forward(tok, 32 + step)  # rewrites the position generate_greedy filled
         b = o.forward(tok, 32 + step)
+        worst = max(worst, float(np.abs(a - b).max()))
         tok = o.greedy(b)
+        assert int(np.argmax(a)) == tok, step
         ref_tokens.append(tok)
     assert [int(t) for t in dev_tokens] == ref_tokens
     assert worst < LOGIT_TOL, worst
