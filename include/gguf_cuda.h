@@ -124,8 +124,8 @@ int gguf_cuda_matvec_noalloc_error(void);
  *     out[b * rows + r] = sum_c W[r][c] * x[b * cols + c],  b < n, r < rows,
  * i.e. gguf_matvec (reference include/gguf_model.h:141-145) applied to each
  * of n vectors. x is n x cols and out is n x rows, row-major, device
- * pointers; out must not overlap x. Q4_K weights (type 12) only; other
- * types return 0. Every column agrees with gguf_cuda_matvec / the
+ * pointers; out must not overlap x. Q4_K (type 12) and Q5_K (type 13)
+ * weights; other types return 0. Every column agrees with gguf_cuda_matvec / the
  * reference's kernel to float32 rounding (the products run on fp16
  * operands that carry x to 22 significant bits, exact products, fp32
  * accumulation). No counterpart in the reference, whose decode runs one

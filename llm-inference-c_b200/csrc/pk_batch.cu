@@ -677,7 +677,8 @@ static int bmatmul(PkbCtx *b, const PkdTensor &t, const float *x, int n, float *
     if (st == nullptr) st = b->st;
     const uint8_t *w = b->arena + t.offset;
     const int rows = (int)t.rows, cols = (int)t.cols;
-    if (pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, w)) return pk_mm_run(w, t.row_bytes, rows, cols, x, n, y, &b->mm, b->sms, st);
+    if (pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, w))
+        return pk_mm_run(t.type, w, t.row_bytes, rows, cols, x, n, y, &b->mm, b->sms, st);
     const int cps = bt::mv_cps(rows, cols, b->sms), nchunks = (cols + bt::TK - 1) / bt::TK;
     const int splits = (nchunks + cps - 1) / cps;
     const dim3 grid((rows + bt::TR - 1) / bt::TR, splits);
@@ -705,8 +706,9 @@ static int bmatmul(PkbCtx *b, const PkdTensor &t, const float *x, int n, float *
     return cudaGetLastError() == cudaSuccess;
 }
 
-// y_i = x W_i^T for weights that multiply the same x: the Q4_K ones in one
-// tensor-core launch (x staged once), the others on the tile kernel. When
+// y_i = x W_i^T for weights that multiply the same x: the Q4_K (or Q5_K)
+// ones in one tensor-core launch (x staged once), the others (a second
+// tensor-core format through its own launch) on the tile kernel. When
 // both kinds are present the tile-kernel ones run on a side stream, forked
 // before and joined after the tensor-core launch, so that they use the SMs
 // the tensor-core grid leaves idle (e.g. the Q6_K attn_v of an even layer
@@ -716,11 +718,21 @@ static int bmatmul_group(PkbCtx *b, const PkdTensor *const *ts, float *const *ys
 {
     PkMmSeg seg[3];
     int ns = 0, tiles = 0;
+    uint32_t tc_type = 0;  // the tensor-core launch takes the first tensor-core format's matrices
+    auto in_launch = [&](const PkdTensor &t) {
+        return pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, b->arena + t.offset) && t.type == tc_type;
+    };
     for (int i = 0; i < cnt; i++) {
         const PkdTensor &t = *ts[i];
-        if (pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, b->arena + t.offset)) {
+        if (tc_type == 0 && pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, b->arena + t.offset)) tc_type = t.type;
+    }
+    auto other_tc = [&](const PkdTensor &t) {
+        return pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, b->arena + t.offset) && t.type != tc_type;
+    };
+    for (int i = 0; i < cnt; i++) {
+        if (in_launch(*ts[i])) {
             ns++;
-        } else {
+        } else if (!other_tc(*ts[i])) {
             tiles++;
         }
     }
@@ -733,13 +745,14 @@ static int bmatmul_group(PkbCtx *b, const PkdTensor *const *ts, float *const *ys
     for (int i = 0; i < cnt; i++) {
         const PkdTensor &t = *ts[i];
         const uint8_t *w = b->arena + t.offset;
-        if (pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, w)) {
+        if (in_launch(t)) {
+            seg[ns].type = t.type;
             seg[ns].w = w;
             seg[ns].row_bytes = t.row_bytes;
             seg[ns].rows = (int)t.rows;
             seg[ns].y = ys[i];
             ns++;
-        } else if (!bmatmul(b, t, x, n, ys[i], fork ? b->side : b->st)) {
+        } else if (!other_tc(t) && !bmatmul(b, t, x, n, ys[i], fork ? b->side : b->st)) {
             return 0;
         }
     }
@@ -747,6 +760,11 @@ static int bmatmul_group(PkbCtx *b, const PkdTensor *const *ts, float *const *ys
     const int cols = (int)ts[0]->cols;
     if (!pk_mm_stage(x, n, cols, &b->mm, b->st) || !pk_mm_run_staged(seg, ns, cols, n, &b->mm, b->sms, b->st)) {
         return 0;
+    }
+    // a second tensor-core format: its own launches after this one (they
+    // share the staging scratch, so not beside it)
+    for (int i = 0; i < cnt; i++) {
+        if (other_tc(*ts[i]) && !bmatmul(b, *ts[i], x, n, ys[i], b->st)) return 0;
     }
     return !fork || (!bfail(b, cudaEventRecord(b->ev_join, b->side), "event") &&
                      !bfail(b, cudaStreamWaitEvent(b->st, b->ev_join, 0), "event"));

@@ -1,12 +1,13 @@
 // pk_mma.cu - the batched fused dequant-matmul on the sm_100a tensor cores:
 // Y[b][r] = sum_k W[r][k] * x_b[k] for up to 64 activation vectors x_b that
-// share one pass over the packed Q4_K weights (the matmul form of the
-// matvec, src/gguf_model.c:693-771, for several sequences at once).
+// share one pass over the packed Q4_K or Q5_K weights (the matmul form of
+// the matvec, src/gguf_model.c:693-771, for several sequences at once).
 //
 // Operands (fp16 products are exact in the fp32 accumulator):
 //   A (weights): per super-block of 256 columns, the integers sc_j * q
-//       (at most 63 * 15, exact in fp16), one LOP3 and one HFMA2 per two
-//       weights; the super-block scales d and dmin stay out of the product
+//       (at most 63 * 15 for Q4_K, 63 * 31 for Q5_K: below 2048, exact in
+//       fp16), one LOP3 (two for Q5_K, whose fifth bit comes from qh) and
+//       one HFMA2 per two weights; the super-block scales d and dmin stay out of the product
 //       and are applied in fp32 when the accumulator is read out. A second
 //       operand A2 holds the 6-bit mins m_j.
 //   B (activations): each 256-column piece of every x_b, scaled by a power
@@ -69,24 +70,21 @@ namespace mm {
 constexpr int TM = 128;    // weight rows per tile (MMA M)
 constexpr int NMAX = 128;  // MMA N at most: 2 parts x 64 vectors
 constexpr int VMAX = 64;   // activation vectors per call
-constexpr int QK = 256;    // columns per Q4_K super-block
-constexpr int SBB = 144;   // bytes per Q4_K super-block
+constexpr int QK = 256;    // columns per super-block
 constexpr int DQ_WARPS = 8, DQ_THREADS = 256;  // warps 0-7: two per row group of 32
 constexpr int W_PRODUCER = 8, B_PRODUCER = 9, ISSUER = 10;
 constexpr int THREADS = 352;
-constexpr int SA = 6, SW = 3, SB_MAX = 32;  // ring depths: A steps, weight super-blocks, x steps (at most)
+constexpr int SA = 6, SW_MAX = 3, SB_MAX = 32;  // ring depths: A steps, weight super-blocks, x steps (at most)
 constexpr int SA2 = 3, SINV = 4;            // A2 slots, inverse-scale slots (see the dequantisers)
 constexpr int A_BYTES = TM * 128;           // [8 chunks][128 rows][16 B]
 constexpr int A2_BYTES = TM * 32;           // [2 chunks][128 rows][16 B]
-constexpr int W_TILE = TM * SBB;            // 128 rows x one super-block
-constexpr int W_BYTES = W_TILE + VMAX * 4;  // + the inverse scales of the x piece
 // Barriers
 enum {
     FULL_A = 0,
     EMPTY_A = FULL_A + SA,
     FULL_W = EMPTY_A + SA,
-    EMPTY_W = FULL_W + SW,
-    ACC_FULL = EMPTY_W + SW,
+    EMPTY_W = FULL_W + SW_MAX,
+    ACC_FULL = EMPTY_W + SW_MAX,
     ACC_EMPTY = ACC_FULL + 2,
     DRAIN = ACC_EMPTY + 2,
     FULL_B = DRAIN + 1,
@@ -99,12 +97,33 @@ constexpr int OFF_INV = 1024;  // SINV x 64 inverse scales (readout)
 constexpr int OFF_A = 2048;
 constexpr int OFF_A2 = OFF_A + SA * A_BYTES;
 constexpr int OFF_W = OFF_A2 + SA2 * A2_BYTES;  // 128-byte aligned (TMA tensor destination)
-constexpr int OFF_B = OFF_W + SW * W_BYTES;
 constexpr int B_SLOT_MAX = NMAX * 128 + NMAX * 32;
 static_assert(NBARS * 8 <= OFF_INV && OFF_INV + SINV * VMAX * 4 <= OFF_A, "barriers, scales");
-static_assert(OFF_W % 128 == 0 && W_BYTES % 128 == 0, "TMA destinations");
-static_assert(OFF_B + 3 * B_SLOT_MAX + 128 <= 227 * 1024 - 1024, "at least 3 x steps of N = 128");
-static_assert(OFF_B > 227 * 1024 / 2, "one CTA per SM (it allocates all of TMEM)");
+
+// The super-block format: bytes, where its nibbles (qs) and fifth bits (qh)
+// start, and the depth of the weight ring that shared memory leaves room
+// for (src/gguf_quant.c:107-161 Q4_K, :307-345 Q5_K).
+template <int T>
+struct Fmt;
+template <>
+struct Fmt<T_Q4_K> {
+    static constexpr int SBB = 144, QS = 16, QH = 0, SW = 3;
+};
+template <>
+struct Fmt<T_Q5_K> {
+    static constexpr int SBB = 176, QS = 48, QH = 16, SW = 2;
+};
+template <int T>
+struct Lay {
+    static constexpr int SBB = Fmt<T>::SBB, SW = Fmt<T>::SW;
+    static constexpr int W_TILE = TM * SBB;            // 128 rows x one super-block
+    static constexpr int W_BYTES = W_TILE + VMAX * 4;  // + the inverse scales of the x piece
+    static constexpr int OFF_B = OFF_W + SW * W_BYTES;
+    static_assert(OFF_W % 128 == 0 && W_BYTES % 128 == 0, "TMA destinations");
+    static_assert(OFF_B + 3 * B_SLOT_MAX + 128 <= 227 * 1024 - 1024, "at least 3 x steps of N = 128");
+    static_assert(OFF_B > 227 * 1024 / 2, "one CTA per SM (it allocates all of TMEM)");
+    static_assert(SW <= SW_MAX, "weight ring barriers");
+};
 constexpr int TMEM_COLS = 512;  // 2 accumulator sets x (D: 128 columns, D2: 128 columns)
 
 // Position of column k (mod 8) inside its 16-byte run: 1 <-> 2, 5 <-> 6.
@@ -199,12 +218,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v)
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// Two nibbles of w (bits 0-3 and 16-19) as the fp16 pair (sc * q0, sc * q1):
-// 1024 + q by the exponent trick, then (1024 + q) * sc - 1024 * sc in one
-// fma, exact because the result is an integer below 2048.
+// Two quants of w (bits 0-3 and 16-19; Q5_K: 0-4 and 16-20) as the fp16
+// pair (sc * q0, sc * q1): 1024 + q by the exponent trick, then
+// (1024 + q) * sc - 1024 * sc in one fma, exact because the result is an
+// integer below 2048.
+template <int FT>
 __device__ __forceinline__ uint32_t nib2(uint32_t w, __half2 sc2, __half2 nsc2)
 {
-    const uint32_t h = (w & 0x000F000Fu) | 0x64006400u;
+    const uint32_t h = (w & (FT == T_Q5_K ? 0x001F001Fu : 0x000F000Fu)) | 0x64006400u;
     const __half2 r = __hfma2(*reinterpret_cast<const __half2 *>(&h), sc2, nsc2);
     return *reinterpret_cast<const uint32_t *>(&r);
 }
@@ -271,7 +292,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volati
 constexpr int MSEG = 3;  // weight matrices (segments) of one launch, all with the same columns
 
 // The weight matrices of one launch as 2D tensors of bytes [rows][row
-// bytes], box [128 rows][144 bytes] (one super-block of one row tile).
+// bytes], box [128 rows][one super-block's bytes] (one row tile).
 struct MmMaps {
     CUtensorMap m[MSEG];
 };
@@ -354,8 +375,11 @@ __device__ __forceinline__ int seg_of(const MmArgs &a, int T)
     return sg;
 }
 
-__global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constant__ MmMaps maps, MmArgs a)
+template <int FT>
+__global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant__ MmMaps maps, MmArgs a)
 {
+    constexpr int SBB = Fmt<FT>::SBB, SW = Fmt<FT>::SW;
+    constexpr int W_TILE = Lay<FT>::W_TILE, W_BYTES = Lay<FT>::W_BYTES, OFF_B = Lay<FT>::OFF_B;
     extern __shared__ __align__(128) uint8_t sm_raw[];
     uint8_t *sm = sm_raw + ((128u - (smem_u32(sm_raw) & 127u)) & 127u);
     __shared__ uint32_t tmem_slot;
@@ -410,7 +434,7 @@ __global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constan
     volatile int *abrt = &abort_flag;
 
     if (warp == W_PRODUCER) {
-        // weight super-blocks: one tensor copy of 128 rows x 144 bytes each
+        // weight super-blocks: one tensor copy of 128 rows x SBB bytes each
         // (rows past the end of the matrix arrive as zeros), then the 64
         // inverse scales of the matching x piece
         const bool leader = elect_one();
@@ -599,6 +623,13 @@ __global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constan
             const uint8_t *wslot = sm + OFF_W + ws * W_BYTES;
             const uint8_t *wrow = wslot + row * SBB;
             const uint4 hdr = *reinterpret_cast<const uint4 *>(wrow);
+            uint32_t qh[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // Q5_K: the fifth bits of the 32 byte positions
+            if (FT == T_Q5_K) {
+                const uint4 ha = *reinterpret_cast<const uint4 *>(wrow + Fmt<FT>::QH);
+                const uint4 hb = *reinterpret_cast<const uint4 *>(wrow + Fmt<FT>::QH + 16);
+                qh[0] = ha.x; qh[1] = ha.y; qh[2] = ha.z; qh[3] = ha.w;
+                qh[4] = hb.x; qh[5] = hb.y; qh[6] = hb.z; qh[7] = hb.w;
+            }
             if (tid < VMAX) inv_s[(j % SINV) * VMAX + tid] = reinterpret_cast<const float *>(wslot + W_TILE)[tid];
             uint32_t scp[4], mnp[4];  // (scale, min) of sub-blocks 2t (low byte) and 2t + 1
 #pragma unroll
@@ -610,8 +641,8 @@ __global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constan
                     ok = false;
                     break;
                 }
-                const uint4 qa = *reinterpret_cast<const uint4 *>(wrow + 16 + 32 * t);
-                const uint4 qb = *reinterpret_cast<const uint4 *>(wrow + 32 + 32 * t);
+                const uint4 qa = *reinterpret_cast<const uint4 *>(wrow + Fmt<FT>::QS + 32 * t);
+                const uint4 qb = *reinterpret_cast<const uint4 *>(wrow + Fmt<FT>::QS + 16 + 32 * t);
                 if (t == 3) mbar_arrive(bars + EMPTY_W + ws);
                 const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
                 // this half's sub-block: 2t (low nibbles, low scale byte) or 2t + 1
@@ -623,10 +654,16 @@ __global__ void __launch_bounds__(THREADS, 1) q4k_mm_kernel(const __grid_constan
 #pragma unroll
                 for (int cc = 0; cc < 4; cc++) {
                     // columns 8cc .. 8cc+7 of the sub-block: nibbles of bytes 8cc .. 8cc+7
-                    const uint32_t w0 = q[2 * cc] >> sh, w1 = q[2 * cc + 1] >> sh;
+                    uint32_t w0 = q[2 * cc] >> sh, w1 = q[2 * cc + 1] >> sh;
+                    if (FT == T_Q5_K) {
+                        // the fifth bit of byte l is bit 2t + half of qh[l], moved to bit 4
+                        const int hs = 2 * t + half;
+                        w0 = (w0 & 0x0F0F0F0Fu) | (((qh[2 * cc] >> hs) & 0x01010101u) << 4);
+                        w1 = (w1 & 0x0F0F0F0Fu) | (((qh[2 * cc + 1] >> hs) & 0x01010101u) << 4);
+                    }
                     *reinterpret_cast<uint4 *>(arow + cc * (TM * 16)) =
-                        make_uint4(nib2(w0, sc2, nsc2), nib2(w0 >> 8, sc2, nsc2), nib2(w1, sc2, nsc2),
-                                   nib2(w1 >> 8, sc2, nsc2));
+                        make_uint4(nib2<FT>(w0, sc2, nsc2), nib2<FT>(w0 >> 8, sc2, nsc2), nib2<FT>(w1, sc2, nsc2),
+                                   nib2<FT>(w1 >> 8, sc2, nsc2));
                 }
                 if (t == 0 && half == 0) {
                     // A2 row: the 8 mins of this super-block (chunk 0, natural order)
@@ -812,12 +849,23 @@ extern "C" void gguf_cuda_matmul_plan(int rows, int nsb, int sms, int *ctas, int
     plan_tiles((rows + mm::TM - 1) / mm::TM, nsb, sms, ctas, maxp);
 }
 
+static int mm_sbb(uint32_t type)
+{
+    return type == T_Q4_K ? mm::Fmt<T_Q4_K>::SBB : type == T_Q5_K ? mm::Fmt<T_Q5_K>::SBB : 0;
+}
+
+static int mm_off_b(uint32_t type)
+{
+    return type == T_Q5_K ? mm::Lay<T_Q5_K>::OFF_B : mm::Lay<T_Q4_K>::OFF_B;
+}
+
 int pk_mm_shape_ok(uint32_t type, uint64_t rows, uint64_t cols, uint64_t row_bytes, const void *data)
 {
-    if (type != T_Q4_K || cols == 0 || cols % mm::QK || rows == 0) return 0;
+    const int sbb = mm_sbb(type);
+    if (sbb == 0 || cols == 0 || cols % mm::QK || rows == 0) return 0;
     if (rows > 0x7FFFFF00ull || cols > 0x7FFFFF00ull) return 0;
     if ((rows + 127) / 128 * (cols / mm::QK) > 0x7FFFFFFFull / 256) return 0;  // units and their products fit int
-    return row_bytes == cols / mm::QK * mm::SBB && ((uintptr_t)data & 15) == 0;
+    return row_bytes == cols / mm::QK * (uint64_t)sbb && ((uintptr_t)data & 15) == 0;
 }
 
 void pk_mm_need(int rows, int cols, int n, int sms, PkMmNeed *need)
@@ -838,14 +886,19 @@ int pk_mm_smem_max(int dev)
     if (dev < 0 || dev >= 64) return 0;
     if (per[dev] == 0) {
         int optin = 0;
-        cudaFuncAttributes fa;
+        cudaFuncAttributes fa, fb;
         if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
-            cudaFuncGetAttributes(&fa, mm::q4k_mm_kernel) != cudaSuccess)
+            cudaFuncGetAttributes(&fa, mm::qk_mm_kernel<T_Q4_K>) != cudaSuccess ||
+            cudaFuncGetAttributes(&fb, mm::qk_mm_kernel<T_Q5_K>) != cudaSuccess)
             return 0;
-        const int avail = optin - (int)fa.sharedSizeBytes;
-        if (avail < mm::OFF_B + 3 * mm::B_SLOT_MAX + 128) return 0;
-        if (cudaFuncSetAttribute(mm::q4k_mm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, avail) !=
-            cudaSuccess) {
+        const int avail = optin - (int)(fa.sharedSizeBytes > fb.sharedSizeBytes ? fa.sharedSizeBytes : fb.sharedSizeBytes);
+        if (avail < mm::Lay<T_Q5_K>::OFF_B + 3 * mm::B_SLOT_MAX + 128 ||
+            avail < mm::Lay<T_Q4_K>::OFF_B + 3 * mm::B_SLOT_MAX + 128)
+            return 0;
+        if (cudaFuncSetAttribute(mm::qk_mm_kernel<T_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, avail) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(mm::qk_mm_kernel<T_Q5_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, avail) !=
+                cudaSuccess) {
             cudaGetLastError();
             return 0;
         }
@@ -865,6 +918,11 @@ int pk_mm_stage(const float *x, int n, int cols, const PkMmScratch *s, cudaStrea
 int pk_mm_run_staged(const PkMmSeg *seg, int nseg, int cols, int n, const PkMmScratch *s, int sms, cudaStream_t st)
 {
     if (n < 1 || n > mm::VMAX || s == nullptr || s->smem_max <= 0 || nseg < 1 || nseg > mm::MSEG) return 0;
+    const uint32_t type = seg[0].type;
+    const int sbb = mm_sbb(type), off_b = mm_off_b(type);
+    if (sbb == 0) return 0;
+    for (int i = 1; i < nseg; i++)
+        if (seg[i].type != type) return 0;  // one format per launch
     const int nsb = cols / mm::QK;
     const int N = (2 * n + 15) / 16 * 16;
     PFN_cuTensorMapEncodeTiled_v12000 enc = encode_tiled();
@@ -877,7 +935,7 @@ int pk_mm_run_staged(const PkMmSeg *seg, int nseg, int cols, int n, const PkMmSc
     for (int i = 0; i < nseg; i++) {
         const cuuint64_t gdim[2] = {(cuuint64_t)seg[i].row_bytes, (cuuint64_t)seg[i].rows};
         const cuuint64_t gstride[1] = {(cuuint64_t)seg[i].row_bytes};
-        const cuuint32_t box[2] = {(cuuint32_t)mm::SBB, (cuuint32_t)mm::TM};
+        const cuuint32_t box[2] = {(cuuint32_t)sbb, (cuuint32_t)mm::TM};
         const cuuint32_t estride[2] = {1, 1};
         if (enc(&maps.m[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(seg[i].w), gdim, gstride, box,
                 estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -898,7 +956,7 @@ int pk_mm_run_staged(const PkMmSeg *seg, int nseg, int cols, int n, const PkMmSc
     a.n = n;
     a.N = N;
     a.b_slot = N * 160;
-    a.sb = (s->smem_max - mm::OFF_B - 128) / a.b_slot;
+    a.sb = (s->smem_max - off_b - 128) / a.b_slot;
     if (a.sb > mm::SB_MAX) a.sb = mm::SB_MAX;
     a.U = tiles * nsb;
     a.G = G;
@@ -906,15 +964,20 @@ int pk_mm_run_staged(const PkMmSeg *seg, int nseg, int cols, int n, const PkMmSc
     a.ypart = s->ypart;
     a.arrived = s->arrived;
     a.err = s->err;
-    const int smem = mm::OFF_B + a.sb * a.b_slot + 128;
-    mm::q4k_mm_kernel<<<G, mm::THREADS, smem, st>>>(maps, a);
+    const int smem = off_b + a.sb * a.b_slot + 128;
+    if (type == T_Q5_K) {
+        mm::qk_mm_kernel<T_Q5_K><<<G, mm::THREADS, smem, st>>>(maps, a);
+    } else {
+        mm::qk_mm_kernel<T_Q4_K><<<G, mm::THREADS, smem, st>>>(maps, a);
+    }
     return cudaGetLastError() == cudaSuccess;
 }
 
-int pk_mm_run(const uint8_t *w, uint64_t row_bytes, int rows, int cols, const float *x, int n, float *y,
-              const PkMmScratch *s, int sms, cudaStream_t st)
+int pk_mm_run(uint32_t type, const uint8_t *w, uint64_t row_bytes, int rows, int cols, const float *x, int n,
+              float *y, const PkMmScratch *s, int sms, cudaStream_t st)
 {
     PkMmSeg seg;
+    seg.type = type;
     seg.w = w;
     seg.row_bytes = row_bytes;
     seg.rows = rows;
@@ -943,7 +1006,8 @@ extern "C" int gguf_cuda_matmul(const GGUFWeight *w, const float *x, int n, floa
     sc.arrived = s->arrived;
     sc.err = s->err;
     sc.smem_max = s->smem_max;
-    return pk_mm_run((const uint8_t *)w->data, w->row_bytes, rows, K, x, n, y, &sc, sms, (cudaStream_t)stream);
+    return pk_mm_run(w->type, (const uint8_t *)w->data, w->row_bytes, rows, K, x, n, y, &sc, sms,
+                     (cudaStream_t)stream);
 }
 
 // Error word of gguf_cuda_matmul on the current device (0: no wait has run

@@ -137,3 +137,11 @@ def test_batch_tinyllama_shape(orc, synth_model):
     worst = run_batched(orc, path, nseq=64, steps=3, seq_ids=list(range(64)), seed=9, ctx=64, stagger=False,
                         check={0, 17, 63})
     assert worst <= LOGIT_TOL, worst
+
+
+def test_batch_q5k_model_matches_oracle(orc, synth_model):
+    """Q5_K attention and gate/up matrices on the tensor-core matmul, Q6_K
+    ffn_down and Q8_0 output on the tile kernel (the Llama-3-8B mix)."""
+    path = synth_model("tiny-q5k")
+    worst = run_batched(orc, path, nseq=8, steps=12, seq_ids=list(range(8)), seed=21)
+    assert worst <= LOGIT_TOL, worst

@@ -1,5 +1,6 @@
-"""The batched dequant-matmul on the tensor cores (gguf_cuda_matmul) against
-the oracle, through the C ABI. torch only provides device buffers.
+"""The batched dequant-matmul on the tensor cores (gguf_cuda_matmul, Q4_K and
+Q5_K weights) against the oracle, through the C ABI. torch only provides
+device buffers.
 
 Every output column b is the matvec of the weights with x_b, so each column
 is held to the matvec bar: within 1e-4 relative L2 of the oracle's
@@ -48,25 +49,25 @@ def activations(n, cols, seed):
     return x
 
 
-def gpu_matmul(torch, wb, rows, cols, x):
+def gpu_matmul(torch, wb, rows, cols, x, qtype=pk_b200.Q4_K):
     n = x.shape[0]
     w = dev(torch, wb)
     xd = dev(torch, x)
     y = torch.full((n, rows), float("nan"), dtype=torch.float32, device="cuda")
-    wt = pk_b200.make_weight(w.data_ptr(), pk_b200.Q4_K, rows, cols)
+    wt = pk_b200.make_weight(w.data_ptr(), qtype, rows, cols)
     assert pk_b200.matmul(wt, xd.data_ptr(), n, y.data_ptr()) == 1
     torch.cuda.synchronize()
     assert pk_b200.matmul_error() == 0
     return y.cpu().numpy()
 
 
-def normalised_error(orc, wb, rows, cols, x, y):
-    rb = pk_b200.row_bytes(pk_b200.Q4_K, cols)
+def normalised_error(orc, wb, rows, cols, x, y, qtype=pk_b200.Q4_K):
+    rb = pk_b200.row_bytes(qtype, cols)
     worst = 0.0
     for r in np.linspace(0, rows - 1, 8).astype(int):
         w = np.empty(cols, dtype=np.float32)
         row = np.ascontiguousarray(wb[r * rb:(r + 1) * rb])
-        assert orc.lib.orc_dequantize_row(pk_b200.Q4_K, row.ctypes.data, cols, w.ctypes.data) == 1
+        assert orc.lib.orc_dequantize_row(qtype, row.ctypes.data, cols, w.ctypes.data) == 1
         exact = w.astype(np.float64) @ x.astype(np.float64)
         scale = np.abs(w.astype(np.float64)) @ np.abs(x.astype(np.float64))
         if scale > 0:
@@ -80,21 +81,22 @@ SHAPES = [(128, 256, 1), (1, 256, 2), (300, 768, 5), (130, 4096, 64), (1000, 204
           (4096, 4096, 8), (20000, 1024, 3), (640, 5632, 64)]
 
 
+@pytest.mark.parametrize("qtype", [pk_b200.Q4_K, pk_b200.Q5_K])
 @pytest.mark.parametrize("shape", SHAPES)
-def test_matmul_columns_match_oracle(torch, orc, shape):
+def test_matmul_columns_match_oracle(torch, orc, shape, qtype):
     rows, cols, n = shape
-    wb = pk_synth.random_matrix(pk_b200.Q4_K, rows, cols, seed=rows + cols + n)
+    wb = pk_synth.random_matrix(qtype, rows, cols, seed=rows + cols + n + qtype)
     x = activations(n, cols, seed=rows + n)
-    y = gpu_matmul(torch, wb, rows, cols, x)
+    y = gpu_matmul(torch, wb, rows, cols, x, qtype)
     assert np.isfinite(y).all()
     for b in range(n):
-        want = orc.matvec(pk_b200.Q4_K, wb, rows, cols, x[b])
+        want = orc.matvec(qtype, wb, rows, cols, x[b])
         if not np.any(x[b]):
             assert np.array_equal(y[b], np.zeros(rows, np.float32)), b
             continue
         assert rel_l2(y[b], want) < REL_L2, (b, rel_l2(y[b], want))
         if b in (0, n - 1):
-            assert normalised_error(orc, wb, rows, cols, x[b], y[b]) < NORM_ERR
+            assert normalised_error(orc, wb, rows, cols, x[b], y[b], qtype) < NORM_ERR
 
 
 def test_matmul_repeat_is_deterministic(torch):
