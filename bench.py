@@ -74,6 +74,14 @@ FALLBACK_HBM_GBS = 6650.0
 MODEL_SEED = 1234
 
 
+_T0 = time.perf_counter()
+
+
+def note(msg):
+    """Progress on stderr (the JSON line is the only stdout)."""
+    print(f"[bench {time.perf_counter() - _T0:7.1f}s] {msg}", file=sys.stderr, flush=True)
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -371,6 +379,7 @@ def run_tp7b(args, world, rank, local, barrier, allmax):
     import pk_b200
     wl = WORKLOADS["llama2-7b"]
     path = ensure_model(wl["preset"], rank, barrier)
+    note("7B model ready")
     P, W, K = wl["prompt"], args.warmup, args.steps
     ctx = P + W + K + 16
     prompt = prompt_ids(P, 32000, 0)
@@ -545,9 +554,10 @@ def run_b64(path, args, cfg, device=0, barrier=lambda: None):
                        "kv_cache": "f16" if kv_entry_bytes() == 2 else "f32",
                        "context_fill": f"{C} seeded random tokens per sequence decoded through "
                                        f"engine_forward_batch ({fill_s:.1f} s, untimed)"},
-            "path": "engine_forward_batch: Q4_K matrices on the tcgen05 tensor-core matmul, Q6_K on the "
-                    "CUDA-core tile kernel, one CUDA graph per step; token ids in and greedy tokens out every "
-                    "step (h2d 768 B, d2h 260 B), timed on the host around synchronous steps",
+            "path": "engine_forward_batch: Q4_K and Q6_K matrices on the tcgen05 tensor-core matmul (the Q6_K "
+                    "attn_v of even layers on the CUDA-core tile kernel beside the Q/K launch), one CUDA graph "
+                    "per step; token ids in and greedy tokens out every step (h2d 768 B, d2h 260 B), timed on the "
+                    "host around synchronous steps",
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "algorithmic_bytes_per_step": wbytes + kvb, "weight_bytes_per_step": wbytes,
                          "kv_bytes_per_step": kvb,
@@ -668,7 +678,9 @@ def main():
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return [float(v) for v in t]
 
+    note("model file")
     path = ensure_model(wl["preset"], rank, barrier)
+    note("model ready")
     need = wl["prompt"] + args.warmup + args.steps + 1
     # N > 1: the 7B/8B shapes (or --tp) decode one sequence tensor-parallel
     # over the N GPUs (each rank holds its heads, hidden slice and vocabulary
@@ -755,12 +767,15 @@ def main():
         b64["roofline"]["peak"] = hbm
         b64["roofline"]["frac"] = b64["roofline"]["achieved"] / hbm
 
+    note("b=1 and b64 done")
     matvec = None
     if rank == 0 and world == 1 and not args.no_matvec and args.workload == "tinyllama":
         matvec = run_matvec_object(args)
+        note("matvec sweep done")
     tp7b = None
     if not args.no_tp7b and args.workload == "tinyllama":
         tp7b = run_tp7b(args, world, rank, local, barrier, allmax)
+        note("tp7b done")
 
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

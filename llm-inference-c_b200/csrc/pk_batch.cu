@@ -672,12 +672,15 @@ extern "C" int pkb_kv_write(PkbCtx *b, int seq, int layer, int pos0, int npos, c
 }
 
 // y (n x rows) = x (n x cols) W^T for one weight tensor.
-static int bmatmul(PkbCtx *b, const PkdTensor &t, const float *x, int n, float *y, cudaStream_t st = nullptr)
+// tc: the tensor-core launch may be used (not beside another launch that
+// shares its staging scratch).
+static int bmatmul(PkbCtx *b, const PkdTensor &t, const float *x, int n, float *y, cudaStream_t st = nullptr,
+                   bool tc = true)
 {
     if (st == nullptr) st = b->st;
     const uint8_t *w = b->arena + t.offset;
     const int rows = (int)t.rows, cols = (int)t.cols;
-    if (pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, w))
+    if (tc && pk_mm_arena_ok(t.type, t.rows, t.cols, t.row_bytes, w))
         return pk_mm_run(t.type, w, t.row_bytes, rows, cols, x, n, y, &b->mm, b->sms, st);
     const int cps = bt::mv_cps(rows, cols, b->sms), nchunks = (cols + bt::TK - 1) / bt::TK;
     const int splits = (nchunks + cps - 1) / cps;
@@ -706,9 +709,9 @@ static int bmatmul(PkbCtx *b, const PkdTensor &t, const float *x, int n, float *
     return cudaGetLastError() == cudaSuccess;
 }
 
-// y_i = x W_i^T for weights that multiply the same x: the Q4_K (or Q5_K)
-// ones in one tensor-core launch (x staged once), the others (a second
-// tensor-core format through its own launch) on the tile kernel. When
+// y_i = x W_i^T for weights that multiply the same x: the ones of the first
+// tensor-core format (Q4_K, Q5_K or Q6_K) in one tensor-core launch (x
+// staged once), the others (a second format included) on the tile kernel. When
 // both kinds are present the tile-kernel ones run on a side stream, forked
 // before and joined after the tensor-core launch, so that they use the SMs
 // the tensor-core grid leaves idle (e.g. the Q6_K attn_v of an even layer
@@ -720,19 +723,16 @@ static int bmatmul_group(PkbCtx *b, const PkdTensor *const *ts, float *const *ys
     int ns = 0, tiles = 0;
     uint32_t tc_type = 0;  // the tensor-core launch takes the first tensor-core format's matrices
     auto in_launch = [&](const PkdTensor &t) {
-        return pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, b->arena + t.offset) && t.type == tc_type;
+        return pk_mm_arena_ok(t.type, t.rows, t.cols, t.row_bytes, b->arena + t.offset) && t.type == tc_type;
     };
     for (int i = 0; i < cnt; i++) {
         const PkdTensor &t = *ts[i];
-        if (tc_type == 0 && pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, b->arena + t.offset)) tc_type = t.type;
+        if (tc_type == 0 && pk_mm_arena_ok(t.type, t.rows, t.cols, t.row_bytes, b->arena + t.offset)) tc_type = t.type;
     }
-    auto other_tc = [&](const PkdTensor &t) {
-        return pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, b->arena + t.offset) && t.type != tc_type;
-    };
     for (int i = 0; i < cnt; i++) {
         if (in_launch(*ts[i])) {
             ns++;
-        } else if (!other_tc(*ts[i])) {
+        } else {
             tiles++;
         }
     }
@@ -752,19 +752,15 @@ static int bmatmul_group(PkbCtx *b, const PkdTensor *const *ts, float *const *ys
             seg[ns].rows = (int)t.rows;
             seg[ns].y = ys[i];
             ns++;
-        } else if (!other_tc(t) && !bmatmul(b, t, x, n, ys[i], fork ? b->side : b->st)) {
+        } else if (!bmatmul(b, t, x, n, ys[i], fork ? b->side : b->st, false)) {
             return 0;
         }
     }
     if (ns == 0) return 1;
     const int cols = (int)ts[0]->cols;
-    if (!pk_mm_stage(x, n, cols, &b->mm, b->st) || !pk_mm_run_staged(seg, ns, cols, n, &b->mm, b->sms, b->st)) {
+    if (!pk_mm_stage(tc_type, x, n, cols, &b->mm, b->st) ||
+        !pk_mm_run_staged(seg, ns, cols, n, &b->mm, b->sms, b->st)) {
         return 0;
-    }
-    // a second tensor-core format: its own launches after this one (they
-    // share the staging scratch, so not beside it)
-    for (int i = 0; i < cnt; i++) {
-        if (other_tc(*ts[i]) && !bmatmul(b, *ts[i], x, n, ys[i], b->st)) return 0;
     }
     return !fork || (!bfail(b, cudaEventRecord(b->ev_join, b->side), "event") &&
                      !bfail(b, cudaStreamWaitEvent(b->st, b->ev_join, 0), "event"));
@@ -886,7 +882,7 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
         if (nd.arrived > mx.arrived) mx.arrived = nd.arrived;
     };
     auto q4k_rows = [&](const PkdTensor &t) -> int {
-        return pk_mm_shape_ok(t.type, t.rows, t.cols, t.row_bytes, v.arena + t.offset) ? (int)t.rows : 0;
+        return pk_mm_arena_ok(t.type, t.rows, t.cols, t.row_bytes, v.arena + t.offset) ? (int)t.rows : 0;
     };
     for (int l = 0; l < m.n_layers; l++) {
         consider(q4k_rows(m.wq[l]) + q4k_rows(m.wk[l]) + q4k_rows(m.wv[l]), m.dim);

@@ -105,19 +105,35 @@ static_assert(NBARS * 8 <= OFF_INV && OFF_INV + SINV * VMAX * 4 <= OFF_A, "barri
 // for (src/gguf_quant.c:107-161 Q4_K, :307-345 Q5_K).
 template <int T>
 struct Fmt;
+// SBB: shared-memory bytes per row and super-block; STEPS: MMA steps of 64
+// k per super-block; OFFW: the weight ring's offset.
 template <>
 struct Fmt<T_Q4_K> {
-    static constexpr int SBB = 144, QS = 16, QH = 0, SW = 3;
+    static constexpr int SBB = 144, QS = 16, QH = 0, SW = 3, STEPS = 4, OFFW = OFF_W;
 };
 template <>
 struct Fmt<T_Q5_K> {
-    static constexpr int SBB = 176, QS = 48, QH = 16, SW = 2;
+    static constexpr int SBB = 176, QS = 48, QH = 16, SW = 2, STEPS = 4, OFFW = OFF_W;
+};
+// Q6_K (src/gguf_quant.c:185-252): 210-byte super-blocks, which no tensor
+// map can address (neither the blocks nor, in general, the rows start on 16
+// bytes), so each row's block arrives by its own bulk copy of the 224-byte
+// aligned window that holds it. Its signed 8-bit scales do not give exact
+// fp16 products with q - 32, so each 64-k step holds 32 columns twice: k
+// 0-31 as 16 a (q - 32), k 32-63 as b (q - 32) with sc = 16 a + b,
+// a in [-8, 7], b in [0, 15] (both exact in fp16), against x staged twice;
+// the sum over the step is sum sc (q - 32) x. No mins, so the A2 slots hold
+// the weight ring.
+template <>
+struct Fmt<T_Q6_K> {
+    static constexpr int SBB = 224, BLK = 210, SW = 2, STEPS = 8, OFFW = OFF_A2;
 };
 template <int T>
 struct Lay {
     static constexpr int SBB = Fmt<T>::SBB, SW = Fmt<T>::SW;
     static constexpr int W_TILE = TM * SBB;            // 128 rows x one super-block
     static constexpr int W_BYTES = W_TILE + VMAX * 4;  // + the inverse scales of the x piece
+    static constexpr int OFF_W = Fmt<T>::OFFW;
     static constexpr int OFF_B = OFF_W + SW * W_BYTES;
     static_assert(OFF_W % 128 == 0 && W_BYTES % 128 == 0, "TMA destinations");
     static_assert(OFF_B + 3 * B_SLOT_MAX + 128 <= 227 * 1024 - 1024, "at least 3 x steps of N = 128");
@@ -230,6 +246,16 @@ __device__ __forceinline__ uint32_t nib2(uint32_t w, __half2 sc2, __half2 nsc2)
     return *reinterpret_cast<const uint32_t *>(&r);
 }
 
+// Two 6-bit quants of w (bits 0-5 and 16-21) as the fp16 pair
+// ((q0 - 32) s, (q1 - 32) s): 1024 + q by the exponent trick, minus 1056,
+// times s; each step exact (the products are integers of at most 12 bits).
+__device__ __forceinline__ uint32_t q6pair(uint32_t w, __half2 s2)
+{
+    const uint32_t h = (w & 0x003F003Fu) | 0x64006400u;
+    const __half2 r = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&h), __float2half2_rn(1056.0f)), s2);
+    return *reinterpret_cast<const uint32_t *>(&r);
+}
+
 // mbarrier.try_wait with a suspend-time hint: the thread sleeps until the
 // phase completes (or about a millisecond passes) instead of spinning, so
 // waiting warps take no issue slots from the working ones.
@@ -302,8 +328,10 @@ struct MmArgs {
     int tile0[MSEG + 1];
     int seg_rows[MSEG];
     float *seg_y[MSEG];     // [n][rows of the segment]
+    const uint8_t *seg_w[MSEG];  // Q6_K: row 0 of each matrix, and its row bytes
+    uint64_t seg_rb[MSEG];
     int nsb;                // super-blocks per row
-    const uint8_t *xs;      // staged x: [nsb][4 steps][8 chunks][N rows][16 B]
+    const uint8_t *xs;      // staged x: [nsb][STEPS][8 chunks][N rows][16 B]
     const uint8_t *x2s;     // staged x sums: [nsb][2 chunks][N rows][16 B]
     const float *xinv;      // [nsb][64] inverse scales of the staged pieces
     int n, N;               // vectors, MMA N
@@ -378,8 +406,10 @@ __device__ __forceinline__ int seg_of(const MmArgs &a, int T)
 template <int FT>
 __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant__ MmMaps maps, MmArgs a)
 {
-    constexpr int SBB = Fmt<FT>::SBB, SW = Fmt<FT>::SW;
+    constexpr int SBB = Fmt<FT>::SBB, SW = Fmt<FT>::SW, STEPS = Fmt<FT>::STEPS;
     constexpr int W_TILE = Lay<FT>::W_TILE, W_BYTES = Lay<FT>::W_BYTES, OFF_B = Lay<FT>::OFF_B;
+    constexpr int OFF_W = Lay<FT>::OFF_W;
+    constexpr bool Q6 = FT == T_Q6_K;
     extern __shared__ __align__(128) uint8_t sm_raw[];
     uint8_t *sm = sm_raw + ((128u - (smem_u32(sm_raw) & 127u)) & 127u);
     __shared__ uint32_t tmem_slot;
@@ -422,7 +452,7 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
         abort_flag = 0;
     }
     // A2 column chunk 1 (k 8..15) stays zero in every slot
-    for (int i = tid; i < SA2 * TM; i += THREADS) {
+    for (int i = tid; !Q6 && i < SA2 * TM; i += THREADS) {
         const int slot = i / TM, row = i % TM;
         *reinterpret_cast<uint4 *>(sm + OFF_A2 + slot * A2_BYTES + TM * 16 + row * 16) = make_uint4(0, 0, 0, 0);
     }
@@ -438,18 +468,32 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
         // (rows past the end of the matrix arrive as zeros), then the 64
         // inverse scales of the matching x piece
         const bool leader = elect_one();
-        if (leader) {
+        if (leader && !Q6) {
             for (int sg = 0; sg < a.nseg; sg++)
                 asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.m[sg])) : "memory");
         }
+        const int lane = tid & 31;
         int issued = 0, T = T0, s = s0;
         for (int j = 0; j < nu; j++) {
             const int slot = j % SW;
             if (j >= SW && !warp_wait(bars + EMPTY_W + slot, ((j / SW) - 1) & 1, abrt, a.err)) break;
-            if (leader) {
-                uint8_t *dst = sm + OFF_W + slot * W_BYTES;
+            uint8_t *dst = sm + OFF_W + slot * W_BYTES;
+            const int sg = seg_of(a, T);
+            if (Q6) {
+                // each row's block in its 16-byte aligned 224-byte window; rows
+                // past the matrix are not copied (their sums are never stored)
+                const int r0 = (T - a.tile0[sg]) * TM, nr = min(TM, a.seg_rows[sg] - r0);
+                if (leader) mbar_expect_tx(bars + FULL_W + slot, (uint32_t)(nr * SBB + VMAX * 4));
+                __syncwarp();
+                for (int r = lane; r < nr; r += 32) {
+                    const uintptr_t src = reinterpret_cast<uintptr_t>(a.seg_w[sg]) +
+                                          (uintptr_t)(r0 + r) * a.seg_rb[sg] + (uintptr_t)s * Fmt<T_Q6_K>::BLK;
+                    bulk_g2s(dst + r * SBB, reinterpret_cast<const void *>(src & ~(uintptr_t)15), SBB,
+                             bars + FULL_W + slot);
+                }
+                if (leader) bulk_g2s(dst + W_TILE, a.xinv + (size_t)s * VMAX, VMAX * 4, bars + FULL_W + slot);
+            } else if (leader) {
                 mbar_expect_tx(bars + FULL_W + slot, (uint32_t)W_BYTES);
-                const int sg = seg_of(a, T);
                 tma_load_2d(dst, &maps.m[sg], s * SBB, (T - a.tile0[sg]) * TM, bars + FULL_W + slot);
                 bulk_g2s(dst + W_TILE, a.xinv + (size_t)s * VMAX, VMAX * 4, bars + FULL_W + slot);
             }
@@ -467,18 +511,19 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
         const uint32_t step_bytes = (uint32_t)N * 128, sum_bytes = (uint32_t)N * 32;
         int issued = 0, slot = 0, s = s0;
         uint32_t phase = 0;  // parity of the slot's next EMPTY_B completion
-        for (int i = 0; i < 4 * nu; i++) {
+        for (int i = 0; i < STEPS * nu; i++) {
             if (i >= SB && !warp_wait(bars + EMPTY_B + slot, phase, abrt, a.err)) break;
-            const int t = i & 3;
+            const int t = i % STEPS;
+            const bool sums = !Q6 && t == STEPS - 1;  // the min term's x sums (Q4_K, Q5_K)
             if (leader) {
                 uint8_t *dst = sm + OFF_B + slot * a.b_slot;
-                mbar_expect_tx(bars + FULL_B + slot, step_bytes + (t == 3 ? sum_bytes : 0u));
-                bulk_g2s(dst, a.xs + ((size_t)s * 4 + t) * step_bytes, step_bytes, bars + FULL_B + slot);
-                if (t == 3) bulk_g2s(dst + step_bytes, a.x2s + (size_t)s * sum_bytes, sum_bytes, bars + FULL_B + slot);
+                mbar_expect_tx(bars + FULL_B + slot, step_bytes + (sums ? sum_bytes : 0u));
+                bulk_g2s(dst, a.xs + ((size_t)s * STEPS + t) * step_bytes, step_bytes, bars + FULL_B + slot);
+                if (sums) bulk_g2s(dst + step_bytes, a.x2s + (size_t)s * sum_bytes, sum_bytes, bars + FULL_B + slot);
             }
             __syncwarp();
             issued = i + 1;
-            if (t == 3 && ++s == a.nsb) s = 0;
+            if (t == STEPS - 1 && ++s == a.nsb) s = 0;
             if (++slot == SB) {
                 slot = 0;
                 if (i >= SB) phase ^= 1u;
@@ -503,7 +548,7 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
             if (j >= 2 && !warp_wait(bars + ACC_EMPTY + acc, ((j / 2) - 1) & 1, abrt, a.err)) break;
             tc_fence_after();
 #pragma unroll 1
-            for (int t = 0; t < 4; t++) {
+            for (int t = 0; t < STEPS; t++) {
                 if (!warp_wait(bars + FULL_A + as, a_ph, abrt, a.err) ||
                     !warp_wait(bars + FULL_B + bs, b_ph, abrt, a.err)) {
                     ok = false;
@@ -518,7 +563,7 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
                         mma_f16(d_col, ad + (uint64_t)(kk * ((2 * TM * 16) >> 4)), bd + (uint64_t)(kk * b_kstep), idesc,
                                 (t | kk) ? 1u : 0u);
                     }
-                    if (t == 3) {
+                    if (!Q6 && t == STEPS - 1) {
                         mma_f16(d_col + 128, a2_desc0 + (uint64_t)((j % SA2) * (A2_BYTES >> 4)),
                                 bd + (uint64_t)(4 * b_kstep), idesc, 0u);
                     }
@@ -580,12 +625,13 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
                 if (2 * b0 + 32 * q < N) {
                     float v[32], v2[32];
                     tmem_ld32(col + 32 * q, v);
-                    tmem_ld32(col + 128 + 32 * q, v2);
+                    if (!Q6) tmem_ld32(col + 128 + 32 * q, v2);
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
                         const int b = 16 * q + i;
                         const float t1 = d * (v[2 * i] + v[2 * i + 1]);
-                        acc[b] = fmaf(iv[b], fmaf(-dmin, v2[2 * i] + v2[2 * i + 1], t1), acc[b]);
+                        acc[b] = Q6 ? fmaf(iv[b], t1, acc[b])
+                                    : fmaf(iv[b], fmaf(-dmin, v2[2 * i] + v2[2 * i + 1], t1), acc[b]);
                     }
                 }
             }
@@ -612,6 +658,7 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
         };
         int as = 0;
         uint32_t ea_ph = 0;  // parity of the A slot's next EMPTY completion
+        int dT = T0, ds = s0;  // tile and super-block being dequantised
         // iteration j dequantises super-block j (j < nu), then reads out j - 1
         for (int j = 0; j <= nu && ok; j++) {
           if (j < nu) {
@@ -621,72 +668,131 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
                 break;
             }
             const uint8_t *wslot = sm + OFF_W + ws * W_BYTES;
-            const uint8_t *wrow = wslot + row * SBB;
-            const uint4 hdr = *reinterpret_cast<const uint4 *>(wrow);
-            uint32_t qh[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // Q5_K: the fifth bits of the 32 byte positions
-            if (FT == T_Q5_K) {
-                const uint4 ha = *reinterpret_cast<const uint4 *>(wrow + Fmt<FT>::QH);
-                const uint4 hb = *reinterpret_cast<const uint4 *>(wrow + Fmt<FT>::QH + 16);
-                qh[0] = ha.x; qh[1] = ha.y; qh[2] = ha.z; qh[3] = ha.w;
-                qh[4] = hb.x; qh[5] = hb.y; qh[6] = hb.z; qh[7] = hb.w;
-            }
-            if (tid < VMAX) inv_s[(j % SINV) * VMAX + tid] = reinterpret_cast<const float *>(wslot + W_TILE)[tid];
-            uint32_t scp[4], mnp[4];  // (scale, min) of sub-blocks 2t (low byte) and 2t + 1
-#pragma unroll
-            for (int t = 0; t < 4; t++) scale_min_pair(hdr.y, hdr.z, hdr.w, t, scp[t], mnp[t]);
+            float d_cur = 0.0f, dmin_cur = 0.0f;
+            if constexpr (Q6) {
+                // this row's block sits in its window at the block's offset
+                // from a 16-byte boundary (an even number: rows and blocks
+                // have even sizes)
+                const int sg = seg_of(a, dT);
+                const uintptr_t gaddr = reinterpret_cast<uintptr_t>(a.seg_w[sg]) +
+                                        (uintptr_t)((dT - a.tile0[sg]) * TM + row) * a.seg_rb[sg] +
+                                        (uintptr_t)ds * Fmt<T_Q6_K>::BLK;
+                const uint8_t *blk = wslot + row * SBB + (gaddr & 15u);
+                if (tid < VMAX) inv_s[(j % SINV) * VMAX + tid] = reinterpret_cast<const float *>(wslot + W_TILE)[tid];
+                uint32_t scw[4], ql[16], qh6[8];
+                ld_words_a2<4>(blk + 192, scw);  // the 16 signed 8-bit scales
+                d_cur = hf(ld_u16(blk + 208));
 #pragma unroll 1
-            for (int t = 0; t < 4; t++) {
-                const int i = 4 * j + t;
-                if (i >= SA && !warp_wait(bars + EMPTY_A + as, ea_ph, abrt, a.err)) {
-                    ok = false;
-                    break;
-                }
-                const uint4 qa = *reinterpret_cast<const uint4 *>(wrow + Fmt<FT>::QS + 32 * t);
-                const uint4 qb = *reinterpret_cast<const uint4 *>(wrow + Fmt<FT>::QS + 16 + 32 * t);
-                if (t == 3) mbar_arrive(bars + EMPTY_W + ws);
-                const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-                // this half's sub-block: 2t (low nibbles, low scale byte) or 2t + 1
-                const __half sc = __ushort2half_rn((unsigned short)((scp[t] >> (8 * half)) & 255u));
-                const __half2 sc2 = __halves2half2(sc, sc);
-                const __half2 nsc2 = __hmul2(sc2, __float2half2_rn(-1024.0f));
-                const int sh = 4 * half;
-                uint8_t *arow = sm + OFF_A + as * A_BYTES + row * 16 + half * 4 * (TM * 16);
-#pragma unroll
-                for (int cc = 0; cc < 4; cc++) {
-                    // columns 8cc .. 8cc+7 of the sub-block: nibbles of bytes 8cc .. 8cc+7
-                    uint32_t w0 = q[2 * cc] >> sh, w1 = q[2 * cc + 1] >> sh;
-                    if (FT == T_Q5_K) {
-                        // the fifth bit of byte l is bit 2t + half of qh[l], moved to bit 4
-                        const int hs = 2 * t + half;
-                        w0 = (w0 & 0x0F0F0F0Fu) | (((qh[2 * cc] >> hs) & 0x01010101u) << 4);
-                        w1 = (w1 & 0x0F0F0F0Fu) | (((qh[2 * cc + 1] >> hs) & 0x01010101u) << 4);
+                for (int t = 0; t < STEPS; t++) {
+                    const int i = STEPS * j + t;
+                    if (i >= SA && !warp_wait(bars + EMPTY_A + as, ea_ph, abrt, a.err)) {
+                        ok = false;
+                        break;
                     }
-                    *reinterpret_cast<uint4 *>(arow + cc * (TM * 16)) =
-                        make_uint4(nib2<FT>(w0, sc2, nsc2), nib2<FT>(w0 >> 8, sc2, nsc2), nib2<FT>(w1, sc2, nsc2),
-                                   nib2<FT>(w1 >> 8, sc2, nsc2));
-                }
-                if (t == 0 && half == 0) {
-                    // A2 row: the 8 mins of this super-block (chunk 0, natural order)
-                    uint32_t m2[4];
-#pragma unroll
-                    for (int p = 0; p < 4; p++) {
-                        const __half2 h = __halves2half2(__ushort2half_rn((unsigned short)(mnp[p] & 255u)),
-                                                         __ushort2half_rn((unsigned short)(mnp[p] >> 8)));
-                        m2[p] = *reinterpret_cast<const uint32_t *>(&h);
+                    // step t: columns 32t .. 32t + 31 = 128h + 32m + l of the block
+                    const int h = t >> 2, m = t & 3;
+                    if (m == 0) {
+                        ld_words_a2<16>(blk + 64 * h, ql);        // ql bytes 64h .. 64h + 63
+                        ld_words_a2<8>(blk + 128 + 32 * h, qh6);  // qh bytes 32h .. 32h + 31
+                        if (h == 1) mbar_arrive(bars + EMPTY_W + ws);  // the slot's last read
                     }
-                    *reinterpret_cast<uint4 *>(sm + OFF_A2 + (j % SA2) * A2_BYTES + row * 16) =
-                        make_uint4(m2[0], m2[1], m2[2], m2[3]);
+                    const int nsh = m >= 2 ? 4 : 0, hsh = 2 * m, wb = 8 * (m & 1);
+                    uint8_t *arow = sm + OFF_A + as * A_BYTES + row * 16 + half * 4 * (TM * 16);
+#pragma unroll
+                    for (int cc = 0; cc < 4; cc++) {
+                        // columns l = 8cc .. 8cc + 7; scale group 2t + l / 16; this
+                        // half's part of sc = 16 a + b: 16 a (k 0-31) or b (k 32-63)
+                        const int g = 2 * t + (cc >> 1);
+                        const int sc = (int)(int8_t)((scw[g >> 2] >> (8 * (g & 3))) & 255u);
+                        const __half2 s2 = __float2half2_rn(half == 0 ? (float)(16 * (sc >> 4)) : (float)(sc & 15));
+                        const uint32_t q0 = ((ql[wb + 2 * cc] >> nsh) & 0x0F0F0F0Fu) |
+                                            (((qh6[2 * cc] >> hsh) & 0x03030303u) << 4);
+                        const uint32_t q1 = ((ql[wb + 2 * cc + 1] >> nsh) & 0x0F0F0F0Fu) |
+                                            (((qh6[2 * cc + 1] >> hsh) & 0x03030303u) << 4);
+                        *reinterpret_cast<uint4 *>(arow + cc * (TM * 16)) =
+                            make_uint4(q6pair(q0, s2), q6pair(q0 >> 8, s2), q6pair(q1, s2), q6pair(q1 >> 8, s2));
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mbar_arrive(bars + FULL_A + as);
+                    if (++as == SA) {
+                        as = 0;
+                        if (i >= SA) ea_ph ^= 1u;
+                    }
                 }
-                // the generic-proxy writes above, seen by the tensor core's async proxy
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                mbar_arrive(bars + FULL_A + as);
-                if (++as == SA) {
-                    as = 0;
-                    if (i >= SA) ea_ph ^= 1u;
+                if (!ok) break;
+            } else {
+                const uint8_t *wrow = wslot + row * SBB;
+                const uint4 hdr = *reinterpret_cast<const uint4 *>(wrow);
+                uint32_t qh[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // Q5_K: the fifth bits of the 32 byte positions
+                if (FT == T_Q5_K) {
+                    const uint4 ha = *reinterpret_cast<const uint4 *>(wrow + Fmt<FT>::QH);
+                    const uint4 hb = *reinterpret_cast<const uint4 *>(wrow + Fmt<FT>::QH + 16);
+                    qh[0] = ha.x; qh[1] = ha.y; qh[2] = ha.z; qh[3] = ha.w;
+                    qh[4] = hb.x; qh[5] = hb.y; qh[6] = hb.z; qh[7] = hb.w;
                 }
+                if (tid < VMAX) inv_s[(j % SINV) * VMAX + tid] = reinterpret_cast<const float *>(wslot + W_TILE)[tid];
+                uint32_t scp[4], mnp[4];  // (scale, min) of sub-blocks 2t (low byte) and 2t + 1
+#pragma unroll
+                for (int t = 0; t < 4; t++) scale_min_pair(hdr.y, hdr.z, hdr.w, t, scp[t], mnp[t]);
+#pragma unroll 1
+                for (int t = 0; t < 4; t++) {
+                    const int i = 4 * j + t;
+                    if (i >= SA && !warp_wait(bars + EMPTY_A + as, ea_ph, abrt, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint4 qa = *reinterpret_cast<const uint4 *>(wrow + Fmt<FT>::QS + 32 * t);
+                    const uint4 qb = *reinterpret_cast<const uint4 *>(wrow + Fmt<FT>::QS + 16 + 32 * t);
+                    if (t == 3) mbar_arrive(bars + EMPTY_W + ws);
+                    const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                    // this half's sub-block: 2t (low nibbles, low scale byte) or 2t + 1
+                    const __half sc = __ushort2half_rn((unsigned short)((scp[t] >> (8 * half)) & 255u));
+                    const __half2 sc2 = __halves2half2(sc, sc);
+                    const __half2 nsc2 = __hmul2(sc2, __float2half2_rn(-1024.0f));
+                    const int sh = 4 * half;
+                    uint8_t *arow = sm + OFF_A + as * A_BYTES + row * 16 + half * 4 * (TM * 16);
+#pragma unroll
+                    for (int cc = 0; cc < 4; cc++) {
+                        // columns 8cc .. 8cc+7 of the sub-block: nibbles of bytes 8cc .. 8cc+7
+                        uint32_t w0 = q[2 * cc] >> sh, w1 = q[2 * cc + 1] >> sh;
+                        if (FT == T_Q5_K) {
+                            // the fifth bit of byte l is bit 2t + half of qh[l], moved to bit 4
+                            const int hs = 2 * t + half;
+                            w0 = (w0 & 0x0F0F0F0Fu) | (((qh[2 * cc] >> hs) & 0x01010101u) << 4);
+                            w1 = (w1 & 0x0F0F0F0Fu) | (((qh[2 * cc + 1] >> hs) & 0x01010101u) << 4);
+                        }
+                        *reinterpret_cast<uint4 *>(arow + cc * (TM * 16)) =
+                            make_uint4(nib2<FT>(w0, sc2, nsc2), nib2<FT>(w0 >> 8, sc2, nsc2), nib2<FT>(w1, sc2, nsc2),
+                                       nib2<FT>(w1 >> 8, sc2, nsc2));
+                    }
+                    if (t == 0 && half == 0) {
+                        // A2 row: the 8 mins of this super-block (chunk 0, natural order)
+                        uint32_t m2[4];
+#pragma unroll
+                        for (int p = 0; p < 4; p++) {
+                            const __half2 h = __halves2half2(__ushort2half_rn((unsigned short)(mnp[p] & 255u)),
+                                                             __ushort2half_rn((unsigned short)(mnp[p] >> 8)));
+                            m2[p] = *reinterpret_cast<const uint32_t *>(&h);
+                        }
+                        *reinterpret_cast<uint4 *>(sm + OFF_A2 + (j % SA2) * A2_BYTES + row * 16) =
+                            make_uint4(m2[0], m2[1], m2[2], m2[3]);
+                    }
+                    // the generic-proxy writes above, seen by the tensor core's async proxy
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mbar_arrive(bars + FULL_A + as);
+                    if (++as == SA) {
+                        as = 0;
+                        if (i >= SA) ea_ph ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                d_cur = hf(hdr.x & 0xFFFFu);
+                dmin_cur = hf(hdr.x >> 16);
             }
-            if (!ok) break;
-            const float d_cur = hf(hdr.x & 0xFFFFu), dmin_cur = hf(hdr.x >> 16);
+            if (++ds == a.nsb) {
+                ds = 0;
+                dT++;
+            }
             if (j > 0 && !readout(j - 1, d_prev, dmin_prev)) {
                 ok = false;
                 break;
@@ -754,6 +860,43 @@ __global__ void __launch_bounds__(256) mm_stage_kernel(const float *x, int n, in
         *reinterpret_cast<__half *>(row + 16) = slo;
         *reinterpret_cast<__half *>(row + (size_t)N * 16) = __half();  // chunk 1: k 8..15
         *reinterpret_cast<__half *>(row + (size_t)N * 16 + 16) = __half();
+    }
+    if (t == 0) xinv[(size_t)s * VMAX + b] = b < n ? 1.0f / scale : 0.0f;
+}
+
+// x into the B operands of the Q6_K launch: each 32-column piece of a
+// super-block is one step, at k 0-31 and again at k 32-63 (the two parts of
+// the split scale multiply the same x). Scale and inverse scale as above;
+// no sums (Q6_K has no mins).
+__global__ void __launch_bounds__(256) mm_stage6_kernel(const float *x, int n, int K, int N, uint8_t *xs, float *xinv)
+{
+    __shared__ float red[8];
+    const int s = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
+    const float xv = b < n ? x[(size_t)b * K + (size_t)s * QK + t] : 0.0f;
+    float m = fabsf(xv);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    if ((t & 31) == 0) red[t >> 5] = m;
+    __syncthreads();
+    m = red[0];
+#pragma unroll
+    for (int i = 1; i < 8; i++) m = fmaxf(m, red[i]);
+    float scale = 1.0f;
+    if (m > 0.0f && m <= 3.4e38f) {
+        int e = 0;
+        frexpf(m, &e);  // m < 2^e
+        scale = ldexpf(1.0f, max(-100, min(100, 10 - e)));
+    }
+    const float v = xv * scale;
+    const __half hi = __float2half_rn(v);
+    const __half lo = __float2half_rn(v - __half2float(hi));
+    const int step = t >> 5, chunk = (t >> 3) & 3, e = t & 7;
+#pragma unroll
+    for (int dup = 0; dup < 2; dup++) {
+        uint8_t *run = xs + ((size_t)s * 8 + step) * N * 128 + (size_t)(chunk + 4 * dup) * N * 16 + (size_t)(2 * b) * 16 +
+                       perm8(e) * 2;
+        *reinterpret_cast<__half *>(run) = hi;
+        *reinterpret_cast<__half *>(run + 16) = lo;
     }
     if (t == 0) xinv[(size_t)s * VMAX + b] = b < n ? 1.0f / scale : 0.0f;
 }
@@ -851,12 +994,21 @@ extern "C" void gguf_cuda_matmul_plan(int rows, int nsb, int sms, int *ctas, int
 
 static int mm_sbb(uint32_t type)
 {
-    return type == T_Q4_K ? mm::Fmt<T_Q4_K>::SBB : type == T_Q5_K ? mm::Fmt<T_Q5_K>::SBB : 0;
+    return type == T_Q4_K ? mm::Fmt<T_Q4_K>::SBB : type == T_Q5_K ? mm::Fmt<T_Q5_K>::SBB
+                                                  : type == T_Q6_K ? mm::Fmt<T_Q6_K>::SBB : 0;
 }
 
 static int mm_off_b(uint32_t type)
 {
-    return type == T_Q5_K ? mm::Lay<T_Q5_K>::OFF_B : mm::Lay<T_Q4_K>::OFF_B;
+    return type == T_Q5_K ? mm::Lay<T_Q5_K>::OFF_B : type == T_Q6_K ? mm::Lay<T_Q6_K>::OFF_B : mm::Lay<T_Q4_K>::OFF_B;
+}
+
+int pk_mm_arena_ok(uint32_t type, uint64_t rows, uint64_t cols, uint64_t row_bytes, const void *data)
+{
+    if (type != T_Q6_K) return pk_mm_shape_ok(type, rows, cols, row_bytes, data);
+    if (cols == 0 || cols % mm::QK || rows == 0 || rows > 0x7FFFFF00ull || cols > 0x7FFFFF00ull) return 0;
+    if ((rows + 127) / 128 * (cols / mm::QK) > 0x7FFFFFFFull / 256) return 0;
+    return row_bytes == cols / mm::QK * (uint64_t)mm::Fmt<T_Q6_K>::BLK && ((uintptr_t)data & 15) == 0;
 }
 
 int pk_mm_shape_ok(uint32_t type, uint64_t rows, uint64_t cols, uint64_t row_bytes, const void *data)
@@ -873,7 +1025,7 @@ void pk_mm_need(int rows, int cols, int n, int sms, PkMmNeed *need)
     const int nsb = cols / mm::QK, N = (2 * n + 15) / 16 * 16, tiles = (rows + mm::TM - 1) / mm::TM;
     int G = 0, maxp = 0;
     plan_tiles(tiles, nsb, sms, &G, &maxp);
-    need->xs = (size_t)nsb * 4 * N * 128;
+    need->xs = (size_t)nsb * 8 * N * 128;  // 8 steps per super-block (Q6_K; 4 for Q4_K, Q5_K)
     need->x2s = (size_t)nsb * N * 32;
     need->xinv = (size_t)nsb * mm::VMAX * 4;
     need->ypart = (size_t)tiles * maxp * n * mm::TM * sizeof(float);
@@ -886,18 +1038,25 @@ int pk_mm_smem_max(int dev)
     if (dev < 0 || dev >= 64) return 0;
     if (per[dev] == 0) {
         int optin = 0;
-        cudaFuncAttributes fa, fb;
+        cudaFuncAttributes fa, fb, fc;
         if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
             cudaFuncGetAttributes(&fa, mm::qk_mm_kernel<T_Q4_K>) != cudaSuccess ||
-            cudaFuncGetAttributes(&fb, mm::qk_mm_kernel<T_Q5_K>) != cudaSuccess)
+            cudaFuncGetAttributes(&fb, mm::qk_mm_kernel<T_Q5_K>) != cudaSuccess ||
+            cudaFuncGetAttributes(&fc, mm::qk_mm_kernel<T_Q6_K>) != cudaSuccess)
             return 0;
-        const int avail = optin - (int)(fa.sharedSizeBytes > fb.sharedSizeBytes ? fa.sharedSizeBytes : fb.sharedSizeBytes);
+        size_t stat = fa.sharedSizeBytes;
+        if (fb.sharedSizeBytes > stat) stat = fb.sharedSizeBytes;
+        if (fc.sharedSizeBytes > stat) stat = fc.sharedSizeBytes;
+        const int avail = optin - (int)stat;
         if (avail < mm::Lay<T_Q5_K>::OFF_B + 3 * mm::B_SLOT_MAX + 128 ||
-            avail < mm::Lay<T_Q4_K>::OFF_B + 3 * mm::B_SLOT_MAX + 128)
+            avail < mm::Lay<T_Q4_K>::OFF_B + 3 * mm::B_SLOT_MAX + 128 ||
+            avail < mm::Lay<T_Q6_K>::OFF_B + 3 * mm::B_SLOT_MAX + 128)
             return 0;
         if (cudaFuncSetAttribute(mm::qk_mm_kernel<T_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, avail) !=
                 cudaSuccess ||
             cudaFuncSetAttribute(mm::qk_mm_kernel<T_Q5_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, avail) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(mm::qk_mm_kernel<T_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, avail) !=
                 cudaSuccess) {
             cudaGetLastError();
             return 0;
@@ -907,11 +1066,15 @@ int pk_mm_smem_max(int dev)
     return per[dev];
 }
 
-int pk_mm_stage(const float *x, int n, int cols, const PkMmScratch *s, cudaStream_t st)
+int pk_mm_stage(uint32_t type, const float *x, int n, int cols, const PkMmScratch *s, cudaStream_t st)
 {
     if (n < 1 || n > mm::VMAX || s == nullptr) return 0;
     const int N = (2 * n + 15) / 16 * 16;
-    mm::mm_stage_kernel<<<dim3(cols / mm::QK, N / 2), 256, 0, st>>>(x, n, cols, N, s->xs, s->x2s, s->xinv);
+    if (type == T_Q6_K) {
+        mm::mm_stage6_kernel<<<dim3(cols / mm::QK, N / 2), 256, 0, st>>>(x, n, cols, N, s->xs, s->xinv);
+    } else {
+        mm::mm_stage_kernel<<<dim3(cols / mm::QK, N / 2), 256, 0, st>>>(x, n, cols, N, s->xs, s->x2s, s->xinv);
+    }
     return cudaGetLastError() == cudaSuccess;
 }
 
@@ -926,13 +1089,21 @@ int pk_mm_run_staged(const PkMmSeg *seg, int nseg, int cols, int n, const PkMmSc
     const int nsb = cols / mm::QK;
     const int N = (2 * n + 15) / 16 * 16;
     PFN_cuTensorMapEncodeTiled_v12000 enc = encode_tiled();
-    if (enc == nullptr) return 0;
+    if (enc == nullptr && type != T_Q6_K) return 0;
     mm::MmMaps maps;
     memset(&maps, 0, sizeof(maps));
     mm::MmArgs a;
+    memset(&a, 0, sizeof(a));
     a.nseg = nseg;
     int tiles = 0;
     for (int i = 0; i < nseg; i++) {
+        a.seg_w[i] = seg[i].w;
+        a.seg_rb[i] = seg[i].row_bytes;
+        a.tile0[i] = tiles;
+        a.seg_rows[i] = seg[i].rows;
+        a.seg_y[i] = seg[i].y;
+        tiles += (seg[i].rows + mm::TM - 1) / mm::TM;
+        if (type == T_Q6_K) continue;  // each row's window by a bulk copy: no tensor map
         const cuuint64_t gdim[2] = {(cuuint64_t)seg[i].row_bytes, (cuuint64_t)seg[i].rows};
         const cuuint64_t gstride[1] = {(cuuint64_t)seg[i].row_bytes};
         const cuuint32_t box[2] = {(cuuint32_t)sbb, (cuuint32_t)mm::TM};
@@ -941,10 +1112,6 @@ int pk_mm_run_staged(const PkMmSeg *seg, int nseg, int cols, int n, const PkMmSc
                 estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return 0;
-        a.tile0[i] = tiles;
-        a.seg_rows[i] = seg[i].rows;
-        a.seg_y[i] = seg[i].y;
-        tiles += (seg[i].rows + mm::TM - 1) / mm::TM;
     }
     for (int i = nseg; i <= mm::MSEG; i++) a.tile0[i] = tiles;
     int G = 0, maxp = 0;
@@ -967,6 +1134,8 @@ int pk_mm_run_staged(const PkMmSeg *seg, int nseg, int cols, int n, const PkMmSc
     const int smem = off_b + a.sb * a.b_slot + 128;
     if (type == T_Q5_K) {
         mm::qk_mm_kernel<T_Q5_K><<<G, mm::THREADS, smem, st>>>(maps, a);
+    } else if (type == T_Q6_K) {
+        mm::qk_mm_kernel<T_Q6_K><<<G, mm::THREADS, smem, st>>>(maps, a);
     } else {
         mm::qk_mm_kernel<T_Q4_K><<<G, mm::THREADS, smem, st>>>(maps, a);
     }
@@ -982,7 +1151,7 @@ int pk_mm_run(uint32_t type, const uint8_t *w, uint64_t row_bytes, int rows, int
     seg.row_bytes = row_bytes;
     seg.rows = rows;
     seg.y = y;
-    return pk_mm_stage(x, n, cols, s, st) && pk_mm_run_staged(&seg, 1, cols, n, s, sms, st);
+    return pk_mm_stage(type, x, n, cols, s, st) && pk_mm_run_staged(&seg, 1, cols, n, s, sms, st);
 }
 
 extern "C" int gguf_cuda_matmul(const GGUFWeight *w, const float *x, int n, float *y, void *stream)
