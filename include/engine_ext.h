@@ -131,6 +131,22 @@ int engine_batch_open(LLMModel *model, int max_seqs, char *error, size_t error_c
 int engine_forward_batch(LLMModel *model, const int *tokens, const int *pos, const int *seq_ids, int n,
                          int *next_tokens, float *logits);
 
+/* A prompt of n tokens at positions pos0 .. pos0 + n - 1 of the cache
+ * engine_forward uses, in chunks of up to 64 rows through the batched step
+ * (the dense matmuls on the tensor cores), instead of n engine_forward calls
+ * (the reference feeds prompts one token at a time, src/pocket.c:294-301).
+ * Every position's K/V is appended before its chunk attends, so position i
+ * sees positions 0 .. i: afterwards engine_forward / engine_generate_greedy
+ * continue at pos0 + n exactly as after n engine_forward calls (within
+ * float rounding). Positions below pos0 hold what earlier calls wrote.
+ * last_logits (optional) receives the logits of position pos0 + n - 1.
+ * Returns that position's greedy token (lowest index on ties), -1 when a
+ * logit is not finite, -2 on invalid arguments or a device error (message
+ * in error). Single GPU; the first call allocates the batched step's
+ * working buffers (make it before any stream capture). */
+int engine_prefill(LLMModel *model, const int *tokens, int n, int pos0, float *last_logits, char *error,
+                   size_t error_capacity);
+
 /* Set the keys and values of positions [pos0, pos0 + npos) of layer `layer`
  * directly: seq -1 for the cache engine_forward uses, seq >= 0 for a
  * batched sequence (after engine_batch_open; pos0 must not leave a gap

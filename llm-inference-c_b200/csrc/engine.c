@@ -103,6 +103,7 @@ struct LLMModel {
     char description[256];
     PkdCtx *dev;
     PkbCtx *batch;     /* batched decode state (engine_batch_open), or NULL */
+    PkbCtx *prefill;   /* engine_prefill's state (its KV cache is the decode step's), made on first use */
     uint64_t weight_bytes;
     int tp_world;      /* tensor-parallel ranks (1: single GPU) */
     int connected;     /* the decode step exists (tensor parallel: after engine_tp_connect) */
@@ -620,6 +621,7 @@ void engine_close(LLMModel *m)
     if (m == NULL) return;
     tokenizer_free(&m->tokenizer);
     pkb_destroy(m->batch);
+    pkb_destroy(m->prefill);
     free(m->filled);
     pkd_destroy(m->dev);
     free(m);
@@ -1028,6 +1030,62 @@ int engine_forward_batch(LLMModel *m, const int *tokens, const int *pos, const i
     for (int i = 0; i < n; i++)
         if (pos[i] + 1 > m->filled[seq_ids[i]]) m->filled[seq_ids[i]] = pos[i] + 1;
     return 1;
+}
+
+int engine_prefill(LLMModel *m, const int *tokens, int n, int pos0, float *last_logits, char *err, size_t cap)
+{
+    if (m == NULL || m->dev == NULL || !m->connected || tokens == NULL || n < 1 || pos0 < 0 ||
+        pos0 > m->config.seq_len - n) {
+        seterr(err, cap, "Invalid arguments.");
+        return -2;
+    }
+    if (m->tp_world > 1) {
+        seterr(err, cap, "Prefill runs on one GPU (not on a tensor-parallel rank).");
+        return -2;
+    }
+    for (int i = 0; i < n; i++) {
+        if (tokens[i] < 0 || tokens[i] >= m->config.vocab_size) {
+            seterr(err, cap, "Token outside the vocabulary.");
+            return -2;
+        }
+    }
+    if (m->prefill == NULL) {
+        m->prefill = pkb_create_prefill(m->dev, err, cap);
+        if (m->prefill == NULL) return -2;
+    }
+    int pos[ENGINE_BATCH_MAX], seq[ENGINE_BATCH_MAX], next[ENGINE_BATCH_MAX];
+    float *lg = NULL;
+    int last = -2;
+    for (int i0 = 0; i0 < n; i0 += ENGINE_BATCH_MAX) {
+        const int k = n - i0 < ENGINE_BATCH_MAX ? n - i0 : ENGINE_BATCH_MAX;
+        const int final = i0 + k == n;
+        for (int j = 0; j < k; j++) {
+            pos[j] = pos0 + i0 + j;
+            seq[j] = 0;
+        }
+        if (final && last_logits != NULL) {
+            lg = (float *)malloc((size_t)k * (size_t)m->config.vocab_size * sizeof(float));
+            if (lg == NULL) {
+                seterr(err, cap, "Out of memory.");
+                return -2;
+            }
+        }
+        if (!pkb_step(m->prefill, tokens + i0, pos, seq, k, next, final ? lg : NULL)) {
+            snprintf(m->last_error, sizeof(m->last_error), "%s", pkb_error(m->prefill));
+            seterr(err, cap, m->last_error);
+            free(lg);
+            return -2;
+        }
+        if (final) {
+            last = next[k - 1];
+            if (lg != NULL)
+                memcpy(last_logits, lg + (size_t)(k - 1) * m->config.vocab_size,
+                       (size_t)m->config.vocab_size * sizeof(float));
+        }
+    }
+    free(lg);
+    if (err && cap) err[0] = '\0';
+    return last;
 }
 
 int engine_kv_write(LLMModel *m, int seq, int layer, int pos0, int npos, const float *k, const float *v,

@@ -636,6 +636,7 @@ struct PkbCtx {
     cudaGraph_t graph[bt::BMAX + 1];
     cudaGraphExec_t exec[bt::BMAX + 1];
     int gqa_smem;  // dynamic shared memory of attention_gqa_kernel (0: per-head attention instead)
+    int kv_alias;  // kc / vc belong to the decode step (pkb_create_prefill): not freed here
     cudaStream_t side;             // tile-kernel matrices that run beside a tensor-core launch
     cudaEvent_t ev_fork, ev_join;  //   (forked from and joined to st inside the captured step)
     char msg[256];
@@ -827,7 +828,19 @@ static int enqueue_step(PkbCtx *b, int n)
     return cudaGetLastError() == cudaSuccess;
 }
 
+static PkbCtx *pkb_create_ex(PkdCtx *ctx, int max_seqs, int alias, char *err, size_t cap);
+
 extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
+{
+    return pkb_create_ex(ctx, max_seqs, 0, err, cap);
+}
+
+extern "C" PkbCtx *pkb_create_prefill(PkdCtx *ctx, char *err, size_t cap)
+{
+    return pkb_create_ex(ctx, 1, 1, err, cap);
+}
+
+static PkbCtx *pkb_create_ex(PkdCtx *ctx, int max_seqs, int alias, char *err, size_t cap)
 {
     PkdView v;
     if (!pkd_view(ctx, &v)) {
@@ -901,8 +914,13 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
     b->mm.smem_max = pk_mm_smem_max(b->device);
     int ok = b->mm.smem_max > 0 || mx.xs == 0;
     if (!ok) snprintf(b->msg, sizeof(b->msg), "The tensor-core matmul cannot run on this device.");
-    ok = ok && !bfail(b, cudaMalloc(&b->kc, cache), "cudaMalloc(batched KV cache)") &&
-         !bfail(b, cudaMalloc(&b->vc, cache), "cudaMalloc(batched KV cache)") &&
+    if (alias) {
+        b->kc = v.kc;
+        b->vc = v.vc;
+        b->kv_alias = 1;
+    }
+    ok = ok && (alias || (!bfail(b, cudaMalloc(&b->kc, cache), "cudaMalloc(batched KV cache)") &&
+                          !bfail(b, cudaMalloc(&b->vc, cache), "cudaMalloc(batched KV cache)"))) &&
          !bfail(b, cudaMalloc(&b->x, (size_t)B * dim * 4), "cudaMalloc") &&
          !bfail(b, cudaMalloc(&b->xn, (size_t)B * dim * 4), "cudaMalloc") &&
          !bfail(b, cudaMalloc(&b->tmp, (size_t)B * dim * 4), "cudaMalloc") &&
@@ -924,8 +942,8 @@ extern "C" PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap)
          !bfail(b, cudaMalloc(&b->mm.err, 16), "cudaMalloc") &&
          !bfail(b, cudaMemsetAsync(b->mm.arrived, 0, mx.arrived + 16, b->st), "cudaMemset") &&
          !bfail(b, cudaMemsetAsync(b->mm.err, 0, 16, b->st), "cudaMemset") &&
-         !bfail(b, cudaMemsetAsync(b->kc, 0, cache, b->st), "cudaMemset") &&
-         !bfail(b, cudaMemsetAsync(b->vc, 0, cache, b->st), "cudaMemset");
+         (alias || (!bfail(b, cudaMemsetAsync(b->kc, 0, cache, b->st), "cudaMemset") &&
+                    !bfail(b, cudaMemsetAsync(b->vc, 0, cache, b->st), "cudaMemset")));
 #define PKB_ATTR(T)                                                                                           \
     ok = ok && !bfail(b, cudaFuncSetAttribute(bt::mv_tile_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                               bt::mv_smem<T>()),                                              \
@@ -1022,7 +1040,8 @@ extern "C" void pkb_destroy(PkbCtx *b)
         if (b->exec[i]) cudaGraphExecDestroy(b->exec[i]);
         if (b->graph[i]) cudaGraphDestroy(b->graph[i]);
     }
-    void *dev[] = {b->kc, b->vc, b->x, b->xn, b->tmp, b->q, b->att, b->k, b->v, b->g, b->u, b->logits, b->part, b->io_d,
+    void *dev[] = {b->kv_alias ? nullptr : b->kc, b->kv_alias ? nullptr : b->vc, b->x, b->xn, b->tmp, b->q, b->att,
+                   b->k, b->v, b->g, b->u, b->logits, b->part, b->io_d,
                    b->mm.xs, b->mm.x2s, b->mm.xinv, b->mm.ypart, b->mm.arrived, b->mm.err};
     for (void *p : dev)
         if (p) cudaFree(p);

@@ -120,6 +120,7 @@ typedef struct {
     const float *norms;
     const float *rope_cs;
     const PkdModel *model;
+    void *kc, *vc;  /* the decode step's KV cache ([layer][position][kv_dim]) */
 } PkdView;
 
 /* 0 for a tensor-parallel rank or an unbuilt context. */
@@ -132,6 +133,11 @@ typedef struct PkbCtx PkbCtx;
 /* Run state for max_seqs sequences (each a KV cache of the model's
  * seq_len) on ctx's device and stream. NULL + message on failure. */
 PkbCtx *pkb_create(PkdCtx *ctx, int max_seqs, char *err, size_t cap);
+
+/* A one-sequence batched state whose KV cache IS the decode step's (the
+ * layout of sequence 0 of a batched cache): prompt chunks run through the
+ * batched step and land where engine_forward reads them. */
+PkbCtx *pkb_create_prefill(PkdCtx *ctx, char *err, size_t cap);
 void pkb_destroy(PkbCtx *b);
 
 /* Sequence seq_ids[i] takes tokens[i] at position pos[i], i < n. next[i]

@@ -1678,6 +1678,8 @@ extern "C" int pkd_view(PkdCtx *c, PkdView *out)
     out->norms = c->norms;
     out->rope_cs = c->rope_cs;
     out->model = &c->model;
+    out->kc = c->kc;
+    out->vc = c->vc;
     return 1;
 }
 

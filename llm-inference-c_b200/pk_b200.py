@@ -28,7 +28,7 @@ EXPORTS = [
     "engine_is_stop_token", "engine_open_device", "engine_forward_greedy", "engine_last_error",
     "engine_weight_bytes", "engine_generate_greedy", "engine_trace", "engine_launches_per_step",
     "engine_tp_plan", "engine_open_tp", "engine_tp_handle", "engine_tp_connect",
-    "engine_batch_open", "engine_forward_batch", "engine_kv_write",
+    "engine_batch_open", "engine_forward_batch", "engine_kv_write", "engine_prefill",
     "gguf_cuda_matvec", "gguf_cuda_dequantize_rows", "gguf_cuda_fp16_table", "gguf_cuda_matvec_noalloc",
     "gguf_cuda_matvec_error", "gguf_cuda_matvec_noalloc_error",
     "gguf_cuda_matmul", "gguf_cuda_matmul_plan", "gguf_cuda_matmul_error",
@@ -140,6 +140,8 @@ def lib(path=LIB_PATH):
     L.engine_batch_open.argtypes = [_P, ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t]
     L.engine_forward_batch.restype = ctypes.c_int
     L.engine_forward_batch.argtypes = [_P, _P, _P, _P, ctypes.c_int, _P, _P]
+    L.engine_prefill.restype = ctypes.c_int
+    L.engine_prefill.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_char_p, ctypes.c_size_t]
     L.engine_kv_write.restype = ctypes.c_int
     L.engine_kv_write.argtypes = [_P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P,
                                   ctypes.c_char_p, ctypes.c_size_t]
@@ -237,6 +239,17 @@ class Engine:
         if ok != 1:
             return None
         return nxt[:n], lg
+
+    def prefill(self, tokens, pos0=0, logits=False):
+        """engine_prefill: (greedy token of the last position, its logits or
+        None); RuntimeError when the call returns -2."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        lg = np.zeros(self.vocab_size, dtype=np.float32) if logits else None
+        err = ctypes.create_string_buffer(256)
+        r = lib().engine_prefill(self.h, t.ctypes.data, t.size, pos0, lg.ctypes.data if logits else None, err, 256)
+        if r == -2:
+            raise RuntimeError("engine_prefill failed: " + err.value.decode())
+        return r, lg
 
     def kv_write(self, layer, pos0, k, v, seq=-1):
         """engine_kv_write: rows pos0 .. of layer `layer` (k, v: npos x kv_dim
