@@ -27,6 +27,10 @@ Extra objects of the default line:
           fraction of the measured HBM peak, beside the reference's own
           gguf_matvec on the same blocks (all host threads) and the relative
           L2 distance of the outputs.
+  llama2_7b_b16  (N = 1) Llama-2-7B shape, 16 sequences after a 1024-position
+          context, batched decode.
+  llama3_8b      (N = 1) Llama-3-8B shape: 2048-token prefill, 512 decode
+          steps, and decode at the end of an 8192 context.
   tp7b    the Llama-2-7B shape decoded tensor-parallel over the run's N GPUs
           (N = 1: one GPU): tok/s, e2e, roofline against N x the HBM peak,
           and whether the greedy tokens match a 1-GPU run of the same prompt.
@@ -452,6 +456,107 @@ def run_tp7b(args, world, rank, local, barrier, allmax):
             "gpu_launches_per_step": launches}
 
 
+def run_cfg4(args):
+    """Llama-3-8B shape, Q5_K/Q6_K/Q8_0 mix, one sequence at an 8192-token
+    context: a seeded 2048-token prompt through engine_prefill (chunks of 64
+    rows on the batched tensor-core step), then 512 greedy decode steps
+    (engine_generate_greedy, the persistent decode kernel) at positions
+    2048..2559; and 64 decode steps after position 8128, the first 8128
+    positions written with seeded keys and values (engine_kv_write)."""
+    import torch
+    import pk_b200
+    wl = WORKLOADS["llama3-8b"]
+    path = ensure_model(wl["preset"], 0, lambda: None)
+    note("8B model ready")
+    P, D, LONG, LSTEPS = 2048, 512, 8128, 64
+    e = pk_b200.Engine(path, 8192, device=0)
+    cfg = e.config
+    prompt = prompt_ids(P, cfg["vocab_size"], 0)
+    e.prefill(prompt[:64], 0)  # builds the 64-row step's graph
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    tok, _ = e.prefill(prompt, 0)
+    prefill_s = time.perf_counter() - t0
+    wt, _ = e.generate_greedy(tok, P, 4)
+    toks, ms = e.generate_greedy(tok, P, D)
+    kvd = cfg["dim"] // cfg["n_heads"] * cfg["n_kv_heads"]
+    for layer in range(cfg["n_layers"]):
+        k = pk_synth.gaussian(9000 + 2 * layer, LONG * kvd, std=0.5).reshape(LONG, kvd)
+        v = pk_synth.gaussian(9001 + 2 * layer, LONG * kvd, std=0.5).reshape(LONG, kvd)
+        e.kv_write(layer, 0, k, v)
+    e.generate_greedy(int(toks[-1]), LONG, 4)
+    ltoks, lms = e.generate_greedy(int(toks[-1]), LONG, LSTEPS)
+    e.close()
+    note("8B config done")
+    hbm, peak_kind = peaks()
+    wbytes = pk_synth.weight_bytes_per_token(wl["preset"])
+    dim, hid, L, V = cfg["dim"], cfg["hidden_dim"], cfg["n_layers"], cfg["vocab_size"]
+    mparams = L * (2 * dim * dim + 2 * dim * kvd + 3 * dim * hid) + V * dim
+    attn = 4 * cfg["n_heads"] * (dim // cfg["n_heads"]) * L * sum(range(1, P + 1))
+    flops = 2.0 * mparams * P + attn
+    step = ms / 1000.0 / D
+    kv_d = kv_bytes_per_step(cfg, list(range(P, P + D)), kv_entry_bytes())
+    step_l = lms / 1000.0 / LSTEPS
+    kv_l = kv_bytes_per_step(cfg, list(range(LONG, LONG + LSTEPS)), kv_entry_bytes())
+    return {"workload": "Llama-3-8B-arch Q5_K/Q6_K/Q8_0, one sequence, context 8192",
+            "model_file": os.path.basename(path),
+            "prefill": {"tokens": P, "seconds": prefill_s, "value": P / prefill_s, "unit": "tok/s",
+                        "path": "engine_prefill: 32 chunks of 64 rows; Q5_K and Q6_K matrices on the tcgen05 matmul, "
+                                "Q8_0 output on the CUDA-core tile kernel; host time around the synchronous call",
+                        "roofline": {"bound": "tensor", "flops": flops, "achieved_tflops": flops / prefill_s / 1e12,
+                                     "peak_tflops": 1655.5, "frac": flops / prefill_s / 1e12 / 1655.5,
+                                     "peak_source": "measured MEASURED_PEAKS.json bf16_tflops (burst)"}},
+            "decode": {"steps": D, "positions": [P, P + D - 1], "value": D / (ms / 1000.0), "unit": "tok/s",
+                       "ms_per_step": step * 1e3,
+                       "roofline": {"bound": "hbm", "achieved": (wbytes + kv_d) / step / 1e9, "peak": hbm,
+                                    "frac": (wbytes + kv_d) / step / 1e9 / hbm, "weight_bytes_per_step": wbytes}},
+            "decode_at_8k": {"steps": LSTEPS, "positions": [LONG, LONG + LSTEPS - 1],
+                             "value": LSTEPS / (lms / 1000.0), "unit": "tok/s", "ms_per_step": step_l * 1e3,
+                             "roofline": {"bound": "hbm", "achieved": (wbytes + kv_l) / step_l / 1e9, "peak": hbm,
+                                          "frac": (wbytes + kv_l) / step_l / 1e9 / hbm,
+                                          "kv_bytes_per_step": kv_l}},
+            "peak_source": f"{peak_kind} MEASURED_PEAKS.json"}
+
+
+def run_cfg3(args):
+    """Llama-2-7B shape, Q4_K_M mix, 16 independent sequences after a
+    1024-position context (written with seeded keys and values through
+    engine_kv_write), 32 greedy steps of engine_forward_batch, one GPU."""
+    import pk_b200
+    wl = WORKLOADS["llama2-7b"]
+    path = ensure_model(wl["preset"], 0, lambda: None)
+    B, C, K = 16, 1024, 32
+    e = pk_b200.Engine(path, C + K + 16, device=0)
+    e.batch_open(B)
+    cfg = e.config
+    kvd = cfg["dim"] // cfg["n_heads"] * cfg["n_kv_heads"]
+    for layer in range(cfg["n_layers"]):
+        k = pk_synth.gaussian(7000 + 2 * layer, C * kvd, std=0.5).reshape(C, kvd)
+        v = pk_synth.gaussian(7001 + 2 * layer, C * kvd, std=0.5).reshape(C, kvd)
+        for sq in range(B):
+            e.kv_write(layer, 0, k, v, seq=sq)
+    toks = prompt_ids(B, cfg["vocab_size"], 1)
+    seq = np.arange(B, dtype=np.int32)
+    for i in range(args.warmup):
+        toks, _ = e.forward_batch(toks, np.full(B, C + i), seq)
+    t0 = time.perf_counter()
+    for i in range(K):
+        toks, _ = e.forward_batch(toks, np.full(B, C + args.warmup + i), seq)
+    dt = time.perf_counter() - t0
+    e.close()
+    hbm, peak_kind = peaks()
+    wbytes = pk_synth.weight_bytes_per_token(wl["preset"])
+    kvb = kv_bytes_per_step(cfg, list(range(C + args.warmup, C + args.warmup + K)), kv_entry_bytes()) * B
+    step = dt / K
+    return {"workload": "Llama-2-7B-arch Q4_K_M, 16 sequences after a 1024-position context", "n_gpus": 1,
+            "steps": K, "value": B * K / dt, "unit": "tok/s", "ms_per_step": step * 1e3,
+            "path": "engine_forward_batch (tcgen05 matmuls), one graph per step, host time around synchronous "
+                    "steps; tensor parallelism is not built for the batched step",
+            "roofline": {"bound": "hbm", "achieved": (wbytes + kvb) / step / 1e9, "peak": hbm,
+                         "frac": (wbytes + kvb) / step / 1e9 / hbm, "weight_bytes_per_step": wbytes,
+                         "kv_bytes_per_step": kvb, "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs"}}
+
+
 def run_matmul_sweep(args):
     """The batched Q4_K matmul (gguf_cuda_matmul) alone: n activation
     vectors against one weight matrix, graph-replayed, inputs resident; one
@@ -628,6 +733,8 @@ def main():
                     help="N > 1 on the TinyLlama shape: one sequence tensor-parallel instead of one per GPU")
     ap.add_argument("--no-matvec", action="store_true", help="skip the matvec sweep object of the default line")
     ap.add_argument("--no-tp7b", action="store_true", help="skip the Llama-2-7B tensor-parallel object")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the Llama-2-7B B=16 and Llama-3-8B prefill/decode objects")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     os.environ["POCKET_CUDA_KV"] = args.kv
@@ -772,6 +879,11 @@ def main():
     if rank == 0 and world == 1 and not args.no_matvec and args.workload == "tinyllama":
         matvec = run_matvec_object(args)
         note("matvec sweep done")
+    cfg3 = cfg4 = None
+    if rank == 0 and world == 1 and not args.no_configs and args.workload == "tinyllama":
+        cfg3 = run_cfg3(args)
+        note("7B B=16 done")
+        cfg4 = run_cfg4(args)
     tp7b = None
     if not args.no_tp7b and args.workload == "tinyllama":
         tp7b = run_tp7b(args, world, rank, local, barrier, allmax)
@@ -809,6 +921,8 @@ def main():
             "b64": b64,
             "matvec": matvec,
             "tp7b": tp7b,
+            "llama2_7b_b16": cfg3,
+            "llama3_8b": cfg4,
             "clocks": clocks.summary(),
             "gpu_launches": launches_per_step * args.steps,
         }
