@@ -73,7 +73,7 @@ VS_BASELINE_NOTE = "published 8.03 tok/s: reference on 8 laptop cores, real Tiny
 # one ncu capture of that launch (the phase_kernel summary under profiles/:
 # dram__bytes_read.sum + dram__bytes_write.sum); None for workloads without
 # a capture.
-NCU_TRAFFIC = {"tinyllama-1.1b-q4km": 639899648 + 7175168}
+NCU_TRAFFIC = {"tinyllama-1.1b-q4km": 639016192 + 6886400}
 FALLBACK_HBM_GBS = 6650.0
 MODEL_SEED = 1234
 
