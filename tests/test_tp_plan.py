@@ -98,3 +98,34 @@ def test_handle_exchange_over_gloo_in_rank_order():
         assert p.exitcode == 0
     want = b"".join(bytes([r]) * 64 for r in range(world))
     assert got[0] == want and got[1] == want
+
+
+def _absent_peer_worker(rank, world, port, q):
+    import datetime
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world, init_method=f"tcp://127.0.0.1:{port}",
+                            timeout=datetime.timedelta(seconds=3))
+    if rank == 1:
+        q.put((rank, "left"))  # leaves between steps: never joins the exchange
+        return
+    try:
+        pk_b200.tp_exchange(bytes([rank]) * 64, world)
+        q.put((rank, "no error"))
+    except Exception as e:  # the process group's timeout ends the collective
+        q.put((rank, "error: " + type(e).__name__))
+
+
+def test_exchange_with_an_absent_rank_ends_in_an_error_not_a_hang():
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_absent_peer_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert got[1] == "left"
+    assert got[0].startswith("error"), got[0]
