@@ -21,21 +21,24 @@
 //       y[b] += (d * (D[2b] + D[2b+1]) - dmin * (D2[2b] + D2[2b+1])) / scale.
 //
 // One CTA per SM, warp-specialised, every hand-off an mbarrier:
-//   warps 0-7  dequantise into A and read the accumulators out: thread t
-//              owns weight row t % 128 of the tile (= TMEM lane t % 128);
-//              warps 0-3 take the low-nibble sub-block of each 64-column
-//              step and vectors 0-31, warps 4-7 the high-nibble sub-block
-//              and vectors 32-63;
-//   warp 8     loads the weight super-blocks of the tile (128 rows x 144
-//              bytes, one 2D TMA tensor copy each, plus the 64 scales of
-//              that x piece) into a 3-deep ring;
-//   warp 9     bulk-copies the staged x of each 64-column step into a ring
-//              as deep as shared memory allows (3 steps at n = 64, 24 at
-//              n <= 8);
-//   warp 10    allocates TMEM and issues the MMAs (one elected lane), committing
-//              to the barriers that free the A and B slots and publish the
-//              accumulators; two accumulator sets let the readout of one
-//              super-block overlap the MMAs of the next.
+//   warps 0-7   dequantise into A: thread t owns weight row t % 128 of the
+//               tile; warps 0-3 take the low-nibble sub-block of each
+//               64-column step, warps 4-7 the high-nibble one;
+//   warps 8-15  read the accumulators out: thread t owns tile row (= TMEM
+//               lane) t % 128, warps 8-11 vectors 0-31, warps 12-15 vectors
+//               32-63, and keep the running sums of the tile piece;
+//   warp 16     loads the weight super-blocks of the tile (128 rows x 144
+//               bytes, one 2D TMA tensor copy each, plus the 64 scales of
+//               that x piece) into a 3-deep ring;
+//   warp 17     bulk-copies the staged x of each 64-column step into a ring
+//               as deep as shared memory allows (3 steps at n = 64, 24 at
+//               n <= 8);
+//   warp 18     allocates TMEM and issues the MMAs from one lane, committing
+//               to the barriers that free the A and B slots and publish the
+//               accumulators; two accumulator sets let the readout of one
+//               super-block overlap the MMAs of the next.
+// Dequantisation and readout run on separate warps so that neither waits
+// for the other: the A ring keeps filling while a super-block is read out.
 // Work units are (row tile, super-block) pairs, split evenly over the CTAs
 // in row-tile-major order. A tile split over several CTAs leaves one partial
 // sum per CTA; for each block of 32 rows x 32 vectors the last CTA to
@@ -71,11 +74,12 @@ constexpr int TM = 128;    // weight rows per tile (MMA M)
 constexpr int NMAX = 128;  // MMA N at most: 2 parts x 64 vectors
 constexpr int VMAX = 64;   // activation vectors per call
 constexpr int QK = 256;    // columns per super-block
-constexpr int DQ_WARPS = 8, DQ_THREADS = 256;  // warps 0-7: two per row group of 32
-constexpr int W_PRODUCER = 8, B_PRODUCER = 9, ISSUER = 10;
-constexpr int THREADS = 352;
-constexpr int SA = 6, SW_MAX = 3, SB_MAX = 32;  // ring depths: A steps, weight super-blocks, x steps (at most)
-constexpr int SA2 = 3, SINV = 4;            // A2 slots, inverse-scale slots (see the dequantisers)
+constexpr int DQ_WARPS = 8, DQ_THREADS = 256;  // warps 0-7 dequantise: two per row group of 32
+constexpr int RO_WARP0 = 8, RO_THREADS = 256;   // warps 8-15 read the accumulators out
+constexpr int W_PRODUCER = 16, B_PRODUCER = 17, ISSUER = 18;
+constexpr int THREADS = 608;
+constexpr int SA = 5, SW_MAX = 3, SB_MAX = 32;  // ring depths: A steps, weight super-blocks, x steps (at most)
+constexpr int SA2 = 3, SINV = 4;            // A2 slots; inverse-scale and row-scale slots (see the readout)
 constexpr int A_BYTES = TM * 128;           // [8 chunks][128 rows][16 B]
 constexpr int A2_BYTES = TM * 32;           // [2 chunks][128 rows][16 B]
 // Barriers
@@ -93,12 +97,14 @@ enum {
 };
 // Shared-memory layout (offsets from a 128-byte aligned base)
 constexpr int OFF_BAR = 0;
-constexpr int OFF_INV = 1024;  // SINV x 64 inverse scales (readout)
-constexpr int OFF_A = 2048;
+constexpr int OFF_INV = 1024;  // SINV x 64 inverse scales of the x pieces (readout)
+constexpr int OFF_DD = 2048;   // SINV x 128 rows: (d, dmin) of each row's super-block as two fp16 (readout)
+constexpr int OFF_A = 4096;
 constexpr int OFF_A2 = OFF_A + SA * A_BYTES;
 constexpr int OFF_W = OFF_A2 + SA2 * A2_BYTES;  // 128-byte aligned (TMA tensor destination)
 constexpr int B_SLOT_MAX = NMAX * 128 + NMAX * 32;
-static_assert(NBARS * 8 <= OFF_INV && OFF_INV + SINV * VMAX * 4 <= OFF_A, "barriers, scales");
+static_assert(NBARS * 8 <= OFF_INV && OFF_INV + SINV * VMAX * 4 <= OFF_DD && OFF_DD + SINV * TM * 4 <= OFF_A,
+              "barriers, scales");
 
 // The super-block format: bytes, where its nibbles (qs) and fifth bits (qh)
 // start, and the depth of the weight ring that shared memory leaves room
@@ -215,23 +221,30 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
-// 32 consecutive fp32 columns of this thread's TMEM lane (warp w reads
-// lanes 32w .. 32w + 31; taddr carries the lane in bits 16-31).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v)
+// 16 consecutive fp32 columns of this thread's TMEM lane at taddr and 16 at
+// taddr2 (warp w reads lanes 32 (w % 4) .. + 31; an address carries the lane
+// in bits 16-31): both loads and their wait in one statement, so that no use
+// of the values can be scheduled before the wait.
+__device__ __forceinline__ void tmem_ld16x2(uint32_t taddr, uint32_t taddr2, float *v, float *v2)
 {
     uint32_t r[32];
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%32];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%33];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        : "r"(taddr), "r"(taddr2)
+        : "memory");
 #pragma unroll
-    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 16; i++) {
+        v[i] = __uint_as_float(r[i]);
+        v2[i] = __uint_as_float(r[16 + i]);
+    }
 }
 
 // Two quants of w (bits 0-3 and 16-19; Q5_K: 0-4 and 16-20) as the fp16
@@ -346,9 +359,10 @@ struct MmArgs {
 
 // Store the sums of one tile piece: acc[b] = vector b0 + b of tile row
 // row. A tile owned by one CTA goes straight to y. Otherwise the piece goes
-// to the CTA's partial slot; per warp (32 rows x 32 vectors) a counter of
-// the CTAs done with that block names the last one, which adds the pieces
-// in CTA order (no barrier between warps: an aborted warp blocks none).
+// to the CTA's partial slot; per read-out warp (32 rows x 32 vectors) a
+// counter of the CTAs done with that block names the last one, which adds
+// the pieces in CTA order (no barrier between warps: an aborted warp blocks
+// none).
 // Out of line and rare (once per tile piece): it keeps the kernel small.
 // T: the tile's index over all segments (partial slots, owners); lt: its
 // index inside its matrix, whose rows and output are rows / y.
@@ -356,7 +370,7 @@ __device__ __noinline__ void flush_piece(const float *acc, float *y, float *ypar
                                          int n, int nsb, int U, int G, int maxp, int T, int lt, int c, int row,
                                          int b0)
 {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = (threadIdx.x >> 5) - RO_WARP0, lane = threadIdx.x & 31;
     const int r = lt * TM + row;
     const int c0 = unit_owner((long long)T * nsb, U, G), c1 = unit_owner((long long)T * nsb + nsb - 1, U, G);
     const int nb = min(32, n - b0);
@@ -441,7 +455,7 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(bars + ACC_FULL + i, 1);
-            mbar_init(bars + ACC_EMPTY + i, DQ_THREADS);
+            mbar_init(bars + ACC_EMPTY + i, RO_THREADS);
         }
         mbar_init(bars + DRAIN, 1);
         for (int i = 0; i < SB; i++) {
@@ -507,128 +521,127 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
         // no copy may still be in flight when the CTA exits
         for (int j = max(0, issued - SW); j < issued; j++) mbar_wait_bounded(bars + FULL_W + j % SW, (j / SW) & 1);
     } else if (warp == B_PRODUCER) {
-        const bool leader = elect_one();
-        const uint32_t step_bytes = (uint32_t)N * 128, sum_bytes = (uint32_t)N * 32;
-        int issued = 0, slot = 0, s = s0;
-        uint32_t phase = 0;  // parity of the slot's next EMPTY_B completion
-        for (int i = 0; i < STEPS * nu; i++) {
-            if (i >= SB && !warp_wait(bars + EMPTY_B + slot, phase, abrt, a.err)) break;
-            const int t = i % STEPS;
-            const bool sums = !Q6 && t == STEPS - 1;  // the min term's x sums (Q4_K, Q5_K)
-            if (leader) {
+        // one lane copies the staged x of every step into the ring
+        if (elect_one()) {
+            const uint32_t step_bytes = (uint32_t)N * 128, sum_bytes = (uint32_t)N * 32;
+            int issued = 0, slot = 0, s = s0;
+            uint32_t phase = 0;  // parity of the slot's next EMPTY_B completion
+            for (int i = 0; i < STEPS * nu; i++) {
+                if (i >= SB && !wait_or_abort(bars + EMPTY_B + slot, phase, abrt, a.err)) break;
+                const int t = i % STEPS;
+                const bool sums = !Q6 && t == STEPS - 1;  // the min term's x sums (Q4_K, Q5_K)
                 uint8_t *dst = sm + OFF_B + slot * a.b_slot;
                 mbar_expect_tx(bars + FULL_B + slot, step_bytes + (sums ? sum_bytes : 0u));
                 bulk_g2s(dst, a.xs + ((size_t)s * STEPS + t) * step_bytes, step_bytes, bars + FULL_B + slot);
                 if (sums) bulk_g2s(dst + step_bytes, a.x2s + (size_t)s * sum_bytes, sum_bytes, bars + FULL_B + slot);
-            }
-            __syncwarp();
-            issued = i + 1;
-            if (t == STEPS - 1 && ++s == a.nsb) s = 0;
-            if (++slot == SB) {
-                slot = 0;
-                if (i >= SB) phase ^= 1u;
-            }
-        }
-        for (int i = max(0, issued - SB); i < issued; i++) mbar_wait_bounded(bars + FULL_B + i % SB, (i / SB) & 1);
-    } else if (warp == ISSUER) {
-        // the whole warp follows the loop; one elected lane issues
-        const bool leader = elect_one();
-        const uint32_t idesc = idesc_f16(TM, N);
-        // descriptors of slot 0 / chunk pair 0; later ones add (offset >> 4)
-        const uint64_t a_desc0 = sdesc(sbase + OFF_A, TM * 16, 128);
-        const uint64_t b_desc0 = sdesc(sbase + OFF_B, N * 16, 128);
-        const uint64_t a2_desc0 = sdesc(sbase + OFF_A2, TM * 16, 128);
-        const uint32_t b_kstep = (uint32_t)(2 * N * 16) >> 4, b_slot16 = (uint32_t)a.b_slot >> 4;
-        bool ok = true;
-        int issued = 0, as = 0, bs = 0;
-        uint32_t a_ph = 0, b_ph = 0;  // parity of the slots' next FULL completion
-        for (int j = 0; j < nu && ok; j++) {
-            const int acc = j & 1;
-            const uint32_t d_col = tmem + (uint32_t)(acc * 256);
-            if (j >= 2 && !warp_wait(bars + ACC_EMPTY + acc, ((j / 2) - 1) & 1, abrt, a.err)) break;
-            tc_fence_after();
-#pragma unroll 1
-            for (int t = 0; t < STEPS; t++) {
-                if (!warp_wait(bars + FULL_A + as, a_ph, abrt, a.err) ||
-                    !warp_wait(bars + FULL_B + bs, b_ph, abrt, a.err)) {
-                    ok = false;
-                    break;
+                issued = i + 1;
+                if (t == STEPS - 1 && ++s == a.nsb) s = 0;
+                if (++slot == SB) {
+                    slot = 0;
+                    if (i >= SB) phase ^= 1u;
                 }
+            }
+            for (int i = max(0, issued - SB); i < issued; i++) mbar_wait_bounded(bars + FULL_B + i % SB, (i / SB) & 1);
+        }
+        __syncwarp();
+    } else if (warp == ISSUER) {
+        // One lane issues: the loop between two MMA steps is a short chain
+        // of single-thread instructions (the tensor core takes an M = 128,
+        // N = 128, K = 16 MMA every 64 cycles; descriptor arithmetic between
+        // issues would leave it idle).
+        if (elect_one()) {
+            const uint32_t idesc = idesc_f16(TM, N);
+            // descriptors of slot 0 / chunk pair 0; later ones add (offset >> 4)
+            const uint64_t a_desc0 = sdesc(sbase + OFF_A, TM * 16, 128);
+            const uint64_t b_desc0 = sdesc(sbase + OFF_B, N * 16, 128);
+            const uint64_t a2_desc0 = sdesc(sbase + OFF_A2, TM * 16, 128);
+            const uint32_t a_kstep = (uint32_t)(2 * TM * 16) >> 4, b_kstep = (uint32_t)(2 * N * 16) >> 4;
+            const uint32_t a_slot16 = (uint32_t)A_BYTES >> 4, b_slot16 = (uint32_t)a.b_slot >> 4;
+            bool ok = true;
+            int issued = 0, as = 0, bs = 0;
+            uint32_t a_ph = 0, b_ph = 0;  // parity of the slots' next FULL completion
+            for (int j = 0; j < nu && ok; j++) {
+                const int acc = j & 1;
+                const uint32_t d_col = tmem + (uint32_t)(acc * 256);
+                if (j >= 2 && !wait_or_abort(bars + ACC_EMPTY + acc, ((j / 2) - 1) & 1, abrt, a.err)) break;
                 tc_fence_after();
-                if (leader) {
-                    const uint64_t ad = a_desc0 + (uint64_t)(as * (A_BYTES >> 4));
-                    const uint64_t bd = b_desc0 + (uint64_t)(bs * b_slot16);
-#pragma unroll
-                    for (int kk = 0; kk < 4; kk++) {
-                        mma_f16(d_col, ad + (uint64_t)(kk * ((2 * TM * 16) >> 4)), bd + (uint64_t)(kk * b_kstep), idesc,
-                                (t | kk) ? 1u : 0u);
+#pragma unroll 1
+                for (int t = 0; t < STEPS; t++) {
+                    if (!wait_or_abort(bars + FULL_A + as, a_ph, abrt, a.err) ||
+                        !wait_or_abort(bars + FULL_B + bs, b_ph, abrt, a.err)) {
+                        ok = false;
+                        break;
                     }
+                    tc_fence_after();
+                    const uint64_t ad = a_desc0 + (uint64_t)(as * a_slot16);
+                    const uint64_t bd = b_desc0 + (uint64_t)(bs * b_slot16);
+                    mma_f16(d_col, ad, bd, idesc, t != 0 ? 1u : 0u);
+                    mma_f16(d_col, ad + a_kstep, bd + b_kstep, idesc, 1u);
+                    mma_f16(d_col, ad + 2 * a_kstep, bd + 2 * b_kstep, idesc, 1u);
+                    mma_f16(d_col, ad + 3 * a_kstep, bd + 3 * b_kstep, idesc, 1u);
                     if (!Q6 && t == STEPS - 1) {
                         mma_f16(d_col + 128, a2_desc0 + (uint64_t)((j % SA2) * (A2_BYTES >> 4)),
                                 bd + (uint64_t)(4 * b_kstep), idesc, 0u);
                     }
                     mma_commit(bars + EMPTY_A + as);
                     mma_commit(bars + EMPTY_B + bs);
+                    issued++;
+                    if (++as == SA) {
+                        as = 0;
+                        a_ph ^= 1u;
+                    }
+                    if (++bs == SB) {
+                        bs = 0;
+                        b_ph ^= 1u;
+                    }
                 }
-                __syncwarp();
-                issued++;
-                if (++as == SA) {
-                    as = 0;
-                    a_ph ^= 1u;
-                }
-                if (++bs == SB) {
-                    bs = 0;
-                    b_ph ^= 1u;
-                }
+                if (ok) mma_commit(bars + ACC_FULL + acc);
             }
-            if (!ok) break;
-            if (leader) mma_commit(bars + ACC_FULL + acc);
-            __syncwarp();
+            // MMAs still running after an abort finish before TMEM is freed
+            if (issued > 0) {
+                mma_commit(bars + DRAIN);
+                mbar_wait_bounded(bars + DRAIN, 0);
+            }
         }
-        // MMAs still running after an abort finish before TMEM is freed
-        if (issued > 0) {
-            if (leader) mma_commit(bars + DRAIN);
-            __syncwarp();
-            mbar_wait_bounded(bars + DRAIN, 0);
-        }
-    } else {
-        // warps 0-7: dequantise and read out. Thread tid owns tile row
-        // row = tid % 128 (TMEM lane row); half = tid / 128 picks the
-        // sub-block of each step (low or high nibbles) and the vectors
-        // 32 half .. 32 half + 31 of the readout.
-        const int row = tid & (TM - 1), half = tid >> 7;
+        __syncwarp();
+    } else if (warp >= RO_WARP0) {
+        // warps 8-15: read the accumulators out. Thread rt owns tile row
+        // row = rt % 128 (TMEM lane row) and the vectors 32 half .. 32 half
+        // + 31, half = rt / 128. Per super-block jp (after its MMAs):
+        //   acc[b] += inv[b] * (d * (D[2b] + D[2b+1]) - dmin * (D2[2b] + D2[2b+1]))
+        // with the row's d, dmin and the x piece's inverse scales from slot
+        // jp % SINV. Slot lifetimes: the dequantisers write slot jp % SINV
+        // at the start of super-block jp and again at jp + SINV, i.e. at step
+        // STEPS (jp + 4); they start a step only after the MMAs of the step
+        // SA = 5 before it completed, here a step of super-block jp + 2 (or
+        // later), whose MMAs the issuer starts only after this readout has
+        // freed its accumulator set (ACC_EMPTY, arrived after the last read
+        // of the slot).
+        const int rt = tid - RO_WARP0 * 32;
+        const int row = rt & (TM - 1), half = rt >> 7;
         const int b0 = 32 * half;
+        const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        const uint32_t *dd = reinterpret_cast<const uint32_t *>(sm + OFF_DD);
         float acc[32];
 #pragma unroll
         for (int b = 0; b < 32; b++) acc[b] = 0.0f;
-        float d_prev = 0.0f, dmin_prev = 0.0f;
         int rT = T0, rs = s0;  // tile and super-block of the next readout
-        const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-        bool ok = true;
-        // Read out super-block jp and, at the end of a tile's piece, store it.
-        // Slot lifetimes, from the A ring (depth SA = 6): a thread starts step
-        // i only after the MMAs of step i - 6 completed, which needed every
-        // thread's A of that step. So the thread that rewrites inv_s slot
-        // jp % 4 (start of jp + 4: after step 4 jp + 15, i.e. after every
-        // thread wrote step 4 jp + 9, which follows readout jp) cannot run
-        // ahead of this readout; and A2 slot j % 3, written at step 4j after
-        // the MMAs of step 4j - 6, was last read by the MMA of step 4j - 9.
-        auto readout = [&](int jp, float d, float dmin) -> bool {
+        for (int jp = 0; jp < nu; jp++) {
             const int accs = jp & 1;
-            if (!warp_wait(bars + ACC_FULL + accs, (jp / 2) & 1, abrt, a.err)) return false;
+            if (!warp_wait(bars + ACC_FULL + accs, (jp / 2) & 1, abrt, a.err)) break;
             tc_fence_after();
-            __syncwarp();
-            const uint32_t col = lane_base + (uint32_t)(accs * 256 + 2 * b0);
+            const uint32_t hd = dd[(jp % SINV) * TM + row];
+            const float d = hf(hd & 0xFFFFu), dmin = hf(hd >> 16);
             const float *iv = inv_s + (jp % SINV) * VMAX + b0;
+            const uint32_t col = lane_base + (uint32_t)(accs * 256 + 2 * b0);
 #pragma unroll
-            for (int q = 0; q < 2; q++) {
-                if (2 * b0 + 32 * q < N) {
-                    float v[32], v2[32];
-                    tmem_ld32(col + 32 * q, v);
-                    if (!Q6) tmem_ld32(col + 128 + 32 * q, v2);
+            for (int q = 0; q < 4; q++) {
+                if (2 * b0 + 16 * q < N) {
+                    float v[16], v2[16];
+                    tmem_ld16x2(col + 16 * q, col + (Q6 ? 16 * q : 128 + 16 * q), v, v2);
 #pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        const int b = 16 * q + i;
+                    for (int i = 0; i < 8; i++) {
+                        const int b = 8 * q + i;
                         const float t1 = d * (v[2 * i] + v[2 * i + 1]);
                         acc[b] = Q6 ? fmaf(iv[b], t1, acc[b])
                                     : fmaf(iv[b], fmaf(-dmin, v2[2 * i] + v2[2 * i + 1], t1), acc[b]);
@@ -654,21 +667,27 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
 #pragma unroll
                 for (int b = 0; b < 32; b++) acc[b] = 0.0f;
             }
-            return true;
-        };
+        }
+    } else {
+        // warps 0-7: dequantise into A. Thread tid owns tile row
+        // row = tid % 128; half = tid / 128 picks the sub-block of each step
+        // (low or high nibbles). At the start of super-block j the row's
+        // (d, dmin) and the x piece's inverse scales go to slot j % SINV for
+        // the readout.
+        const int row = tid & (TM - 1), half = tid >> 7;
+        uint32_t *dd = reinterpret_cast<uint32_t *>(sm + OFF_DD);
+        bool ok = true;
         int as = 0;
         uint32_t ea_ph = 0;  // parity of the A slot's next EMPTY completion
         int dT = T0, ds = s0;  // tile and super-block being dequantised
-        // iteration j dequantises super-block j (j < nu), then reads out j - 1
-        for (int j = 0; j <= nu && ok; j++) {
-          if (j < nu) {
+        for (int j = 0; j < nu && ok; j++) {
             const int ws = j % SW;
             if (!warp_wait(bars + FULL_W + ws, (j / SW) & 1, abrt, a.err)) {
                 ok = false;
                 break;
             }
             const uint8_t *wslot = sm + OFF_W + ws * W_BYTES;
-            float d_cur = 0.0f, dmin_cur = 0.0f;
+            if (tid < VMAX) inv_s[(j % SINV) * VMAX + tid] = reinterpret_cast<const float *>(wslot + W_TILE)[tid];
             if constexpr (Q6) {
                 // this row's block sits in its window at the block's offset
                 // from a 16-byte boundary (an even number: rows and blocks
@@ -678,10 +697,9 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
                                         (uintptr_t)((dT - a.tile0[sg]) * TM + row) * a.seg_rb[sg] +
                                         (uintptr_t)ds * Fmt<T_Q6_K>::BLK;
                 const uint8_t *blk = wslot + row * SBB + (gaddr & 15u);
-                if (tid < VMAX) inv_s[(j % SINV) * VMAX + tid] = reinterpret_cast<const float *>(wslot + W_TILE)[tid];
                 uint32_t scw[4], ql[16], qh6[8];
                 ld_words_a2<4>(blk + 192, scw);  // the 16 signed 8-bit scales
-                d_cur = hf(ld_u16(blk + 208));
+                if (half == 0) dd[(j % SINV) * TM + row] = ld_u16(blk + 208);  // d; no mins
 #pragma unroll 1
                 for (int t = 0; t < STEPS; t++) {
                     const int i = STEPS * j + t;
@@ -719,7 +737,6 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
                         if (i >= SA) ea_ph ^= 1u;
                     }
                 }
-                if (!ok) break;
             } else {
                 const uint8_t *wrow = wslot + row * SBB;
                 const uint4 hdr = *reinterpret_cast<const uint4 *>(wrow);
@@ -730,7 +747,7 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
                     qh[0] = ha.x; qh[1] = ha.y; qh[2] = ha.z; qh[3] = ha.w;
                     qh[4] = hb.x; qh[5] = hb.y; qh[6] = hb.z; qh[7] = hb.w;
                 }
-                if (tid < VMAX) inv_s[(j % SINV) * VMAX + tid] = reinterpret_cast<const float *>(wslot + W_TILE)[tid];
+                if (half == 0) dd[(j % SINV) * TM + row] = hdr.x;  // d (low half), dmin (high half)
                 uint32_t scp[4], mnp[4];  // (scale, min) of sub-blocks 2t (low byte) and 2t + 1
 #pragma unroll
                 for (int t = 0; t < 4; t++) scale_min_pair(hdr.y, hdr.z, hdr.w, t, scp[t], mnp[t]);
@@ -785,23 +802,11 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
                         if (i >= SA) ea_ph ^= 1u;
                     }
                 }
-                if (!ok) break;
-                d_cur = hf(hdr.x & 0xFFFFu);
-                dmin_cur = hf(hdr.x >> 16);
             }
             if (++ds == a.nsb) {
                 ds = 0;
                 dT++;
             }
-            if (j > 0 && !readout(j - 1, d_prev, dmin_prev)) {
-                ok = false;
-                break;
-            }
-            d_prev = d_cur;
-            dmin_prev = dmin_cur;
-          } else if (!readout(j - 1, d_prev, dmin_prev)) {
-            ok = false;
-          }
         }
     }
     tc_fence_before();
