@@ -78,15 +78,14 @@ constexpr int DQ_WARPS = 8, DQ_THREADS = 256;  // warps 0-7 dequantise: two per 
 constexpr int RO_WARP0 = 8, RO_THREADS = 256;   // warps 8-15 read the accumulators out
 constexpr int W_PRODUCER = 16, B_PRODUCER = 17, ISSUER = 18;
 constexpr int THREADS = 608;
-constexpr int SA = 5, SW_MAX = 3, SB_MAX = 32;  // ring depths: A steps, weight super-blocks, x steps (at most)
-constexpr int SA2 = 3, SINV = 4;            // A2 slots; inverse-scale and row-scale slots (see the readout)
-constexpr int A_BYTES = TM * 128;           // [8 chunks][128 rows][16 B]
-constexpr int A2_BYTES = TM * 32;           // [2 chunks][128 rows][16 B]
+constexpr int SA_MAX = 8, SW_MAX = 4, SB_MAX = 32;  // ring depths at most: A steps, weight super-blocks, x steps
+constexpr int SA2 = 3, SINV = 4;  // A2 slots; inverse-scale and row-scale slots (see the readout)
+constexpr int A2_BYTES = TM * 32;  // [2 chunks][128 rows][16 B]
 // Barriers
 enum {
     FULL_A = 0,
-    EMPTY_A = FULL_A + SA,
-    FULL_W = EMPTY_A + SA,
+    EMPTY_A = FULL_A + SA_MAX,
+    FULL_W = EMPTY_A + SA_MAX,
     EMPTY_W = FULL_W + SW_MAX,
     ACC_FULL = EMPTY_W + SW_MAX,
     ACC_EMPTY = ACC_FULL + 2,
@@ -95,31 +94,43 @@ enum {
     EMPTY_B = FULL_B + SB_MAX,
     NBARS = EMPTY_B + SB_MAX
 };
-// Shared-memory layout (offsets from a 128-byte aligned base)
+// Shared-memory layout (offsets from a 128-byte aligned base). The A
+// operand lives in tensor memory, so shared memory holds the weight ring,
+// the x ring and the small per-super-block tables.
 constexpr int OFF_BAR = 0;
 constexpr int OFF_INV = 1024;  // SINV x 64 inverse scales of the x pieces (readout)
 constexpr int OFF_DD = 2048;   // SINV x 128 rows: (d, dmin) of each row's super-block as two fp16 (readout)
-constexpr int OFF_A = 4096;
-constexpr int OFF_A2 = OFF_A + SA * A_BYTES;
-constexpr int OFF_W = OFF_A2 + SA2 * A2_BYTES;  // 128-byte aligned (TMA tensor destination)
-constexpr int B_SLOT_MAX = NMAX * 128 + NMAX * 32;
-static_assert(NBARS * 8 <= OFF_INV && OFF_INV + SINV * VMAX * 4 <= OFF_DD && OFF_DD + SINV * TM * 4 <= OFF_A,
+constexpr int OFF_A2 = 4096;   // SA2 A2 slots (the mins; Q4_K and Q5_K)
+constexpr int B_SLOT_MAX = NMAX * 128 + VMAX * 32;
+static_assert(NBARS * 8 <= OFF_INV && OFF_INV + SINV * VMAX * 4 <= OFF_DD && OFF_DD + SINV * TM * 4 <= OFF_A2,
               "barriers, scales");
 
+// Tensor memory (512 columns of 128 lanes x 32 bits):
+//   D set s (s = 0, 1):   columns 128 s .. 128 s + 127, fp32, MMA N <= 128
+//   D2 set s (Q4_K/Q5_K): columns 256 + 64 s .., one column per vector
+//   A ring:               32 columns per 64-k step (row = lane, two fp16 per
+//                         column in k order), from column ACOL
+constexpr int TMEM_COLS = 512;
+constexpr int D2_COL = 256;
+
 // The super-block format: bytes, where its nibbles (qs) and fifth bits (qh)
-// start, and the depth of the weight ring that shared memory leaves room
-// for (src/gguf_quant.c:107-161 Q4_K, :307-345 Q5_K).
+// start, the depth of the weight ring that shared memory leaves room for,
+// and the A ring in tensor memory (src/gguf_quant.c:107-161 Q4_K, :307-345
+// Q5_K).
 template <int T>
 struct Fmt;
 // SBB: shared-memory bytes per row and super-block; STEPS: MMA steps of 64
-// k per super-block; OFFW: the weight ring's offset.
+// k per super-block; OFFW: the weight ring's offset; SA, ACOL: A ring slots
+// and first column.
 template <>
 struct Fmt<T_Q4_K> {
-    static constexpr int SBB = 144, QS = 16, QH = 0, SW = 3, STEPS = 4, OFFW = OFF_W;
+    static constexpr int SBB = 144, QS = 16, QH = 0, SW = 4, STEPS = 4, OFFW = OFF_A2 + SA2 * A2_BYTES;
+    static constexpr int SA = 4, ACOL = 384;
 };
 template <>
 struct Fmt<T_Q5_K> {
-    static constexpr int SBB = 176, QS = 48, QH = 16, SW = 2, STEPS = 4, OFFW = OFF_W;
+    static constexpr int SBB = 176, QS = 48, QH = 16, SW = 4, STEPS = 4, OFFW = OFF_A2 + SA2 * A2_BYTES;
+    static constexpr int SA = 4, ACOL = 384;
 };
 // Q6_K (src/gguf_quant.c:185-252): 210-byte super-blocks, which no tensor
 // map can address (neither the blocks nor, in general, the rows start on 16
@@ -128,11 +139,11 @@ struct Fmt<T_Q5_K> {
 // fp16 products with q - 32, so each 64-k step holds 32 columns twice: k
 // 0-31 as 16 a (q - 32), k 32-63 as b (q - 32) with sc = 16 a + b,
 // a in [-8, 7], b in [0, 15] (both exact in fp16), against x staged twice;
-// the sum over the step is sum sc (q - 32) x. No mins, so the A2 slots hold
-// the weight ring.
+// the sum over the step is sum sc (q - 32) x. No mins: no A2, no D2.
 template <>
 struct Fmt<T_Q6_K> {
-    static constexpr int SBB = 224, BLK = 210, SW = 2, STEPS = 8, OFFW = OFF_A2;
+    static constexpr int SBB = 224, BLK = 210, SW = 4, STEPS = 8, OFFW = OFF_A2;
+    static constexpr int SA = 8, ACOL = 256;
 };
 template <int T>
 struct Lay {
@@ -143,10 +154,13 @@ struct Lay {
     static constexpr int OFF_B = OFF_W + SW * W_BYTES;
     static_assert(OFF_W % 128 == 0 && W_BYTES % 128 == 0, "TMA destinations");
     static_assert(OFF_B + 3 * B_SLOT_MAX + 128 <= 227 * 1024 - 1024, "at least 3 x steps of N = 128");
-    static_assert(OFF_B > 227 * 1024 / 2, "one CTA per SM (it allocates all of TMEM)");
-    static_assert(SW <= SW_MAX, "weight ring barriers");
+    static_assert(SW <= SW_MAX && Fmt<T>::SA <= SA_MAX, "ring barriers");
+    static_assert(Fmt<T>::ACOL + 32 * Fmt<T>::SA <= TMEM_COLS, "A ring inside tensor memory");
+    // a readout slot (SINV deep) is rewritten at the start of super-block
+    // j + SINV; the dequantisers then have waited for the MMAs of a step of
+    // super-block j + 2 or later (see the readout) only if SA < 2 STEPS
+    static_assert(Fmt<T>::SA < 2 * Fmt<T>::STEPS && SINV >= 4, "readout slot lifetimes");
 };
-constexpr int TMEM_COLS = 512;  // 2 accumulator sets x (D: 128 columns, D2: 128 columns)
 
 // Position of column k (mod 8) inside its 16-byte run: 1 <-> 2, 5 <-> 6.
 __host__ __device__ constexpr int perm8(int i)
@@ -187,6 +201,19 @@ __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b,
         : "memory");
 }
 
+// The same with A in tensor memory: 128 lanes (rows) x 8 columns (16 fp16
+// in k order) from column address a_tmem.
+__device__ __forceinline__ void mma_f16_ta(uint32_t tmem_d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                           uint32_t accum)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
 // Arrive on bar once every tcgen05 operation issued so far by this thread
 // has completed.
 __device__ __forceinline__ void mma_commit(uint64_t *bar)
@@ -221,30 +248,56 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
-// 16 consecutive fp32 columns of this thread's TMEM lane at taddr and 16 at
+// 16 consecutive fp32 columns of this thread's TMEM lane at taddr and 8 at
 // taddr2 (warp w reads lanes 32 (w % 4) .. + 31; an address carries the lane
 // in bits 16-31): both loads and their wait in one statement, so that no use
 // of the values can be scheduled before the wait.
-__device__ __forceinline__ void tmem_ld16x2(uint32_t taddr, uint32_t taddr2, float *v, float *v2)
+__device__ __forceinline__ void tmem_ld16x8(uint32_t taddr, uint32_t taddr2, float *v, float *v2)
 {
-    uint32_t r[32];
+    uint32_t r[24];
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%32];\n\t"
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%33];\n\t"
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%24];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%16, %17, %18, %19, %20, %21, %22, %23}, [%25];\n\t"
         "tcgen05.wait::ld.sync.aligned;"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23])
         : "r"(taddr), "r"(taddr2)
         : "memory");
 #pragma unroll
-    for (int i = 0; i < 16; i++) {
-        v[i] = __uint_as_float(r[i]);
-        v2[i] = __uint_as_float(r[16 + i]);
-    }
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+#pragma unroll
+    for (int i = 0; i < 8; i++) v2[i] = __uint_as_float(r[16 + i]);
+}
+
+// 16 consecutive fp32 columns at taddr, loaded and waited for in one statement.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v)
+{
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Store 16 32-bit words to consecutive columns of this thread's TMEM lane,
+// then wait until the stores are done (the tensor core reads them next).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *r)
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};\n\t"
+        "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
 }
 
 // Two quants of w (bits 0-3 and 16-19; Q5_K: 0-4 and 16-20) as the fp16
@@ -345,9 +398,9 @@ struct MmArgs {
     uint64_t seg_rb[MSEG];
     int nsb;                // super-blocks per row
     const uint8_t *xs;      // staged x: [nsb][STEPS][8 chunks][N rows][16 B]
-    const uint8_t *x2s;     // staged x sums: [nsb][2 chunks][N rows][16 B]
+    const uint8_t *x2s;     // staged x sums: [nsb][2 chunks (hi, lo)][N2 rows][16 B]
     const float *xinv;      // [nsb][64] inverse scales of the staged pieces
-    int n, N;               // vectors, MMA N
+    int n, N, N2;           // vectors, MMA N of D (hi and lo column per vector) and of D2 (one per vector)
     int sb, b_slot;         // x ring depth and slot bytes
     int U;                  // work units (row tiles x super-blocks)
     int G;                  // CTAs
@@ -422,7 +475,7 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
 {
     constexpr int SBB = Fmt<FT>::SBB, SW = Fmt<FT>::SW, STEPS = Fmt<FT>::STEPS;
     constexpr int W_TILE = Lay<FT>::W_TILE, W_BYTES = Lay<FT>::W_BYTES, OFF_B = Lay<FT>::OFF_B;
-    constexpr int OFF_W = Lay<FT>::OFF_W;
+    constexpr int OFF_W = Lay<FT>::OFF_W, SA = Fmt<FT>::SA, ACOL = Fmt<FT>::ACOL;
     constexpr bool Q6 = FT == T_Q6_K;
     extern __shared__ __align__(128) uint8_t sm_raw[];
     uint8_t *sm = sm_raw + ((128u - (smem_u32(sm_raw) & 127u)) & 127u);
@@ -464,11 +517,6 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
         }
         fence_mbar_init();
         abort_flag = 0;
-    }
-    // A2 column chunk 1 (k 8..15) stays zero in every slot
-    for (int i = tid; !Q6 && i < SA2 * TM; i += THREADS) {
-        const int slot = i / TM, row = i % TM;
-        *reinterpret_cast<uint4 *>(sm + OFF_A2 + slot * A2_BYTES + TM * 16 + row * 16) = make_uint4(0, 0, 0, 0);
     }
     tc_fence_before();
     __syncthreads();
@@ -523,7 +571,7 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
     } else if (warp == B_PRODUCER) {
         // one lane copies the staged x of every step into the ring
         if (elect_one()) {
-            const uint32_t step_bytes = (uint32_t)N * 128, sum_bytes = (uint32_t)N * 32;
+            const uint32_t step_bytes = (uint32_t)N * 128, sum_bytes = (uint32_t)a.N2 * 32;
             int issued = 0, slot = 0, s = s0;
             uint32_t phase = 0;  // parity of the slot's next EMPTY_B completion
             for (int i = 0; i < STEPS * nu; i++) {
@@ -550,19 +598,20 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
         // N = 128, K = 16 MMA every 64 cycles; descriptor arithmetic between
         // issues would leave it idle).
         if (elect_one()) {
-            const uint32_t idesc = idesc_f16(TM, N);
-            // descriptors of slot 0 / chunk pair 0; later ones add (offset >> 4)
-            const uint64_t a_desc0 = sdesc(sbase + OFF_A, TM * 16, 128);
+            const uint32_t idesc = idesc_f16(TM, N), idesc2 = idesc_f16(TM, a.N2);
+            // descriptors of slot 0 / chunk pair 0; later ones add (offset >> 4).
+            // A of step slot as: tensor-memory columns ACOL + 32 as + 8 kk.
             const uint64_t b_desc0 = sdesc(sbase + OFF_B, N * 16, 128);
+            const uint64_t b2_desc0 = sdesc(sbase + OFF_B + N * 128, a.N2 * 16, 128);
             const uint64_t a2_desc0 = sdesc(sbase + OFF_A2, TM * 16, 128);
-            const uint32_t a_kstep = (uint32_t)(2 * TM * 16) >> 4, b_kstep = (uint32_t)(2 * N * 16) >> 4;
-            const uint32_t a_slot16 = (uint32_t)A_BYTES >> 4, b_slot16 = (uint32_t)a.b_slot >> 4;
+            const uint32_t b_kstep = (uint32_t)(2 * N * 16) >> 4, b_slot16 = (uint32_t)a.b_slot >> 4;
+            const uint32_t a_col0 = tmem + (uint32_t)ACOL;
             bool ok = true;
             int issued = 0, as = 0, bs = 0;
             uint32_t a_ph = 0, b_ph = 0;  // parity of the slots' next FULL completion
             for (int j = 0; j < nu && ok; j++) {
                 const int acc = j & 1;
-                const uint32_t d_col = tmem + (uint32_t)(acc * 256);
+                const uint32_t d_col = tmem + (uint32_t)(acc * 128);
                 if (j >= 2 && !wait_or_abort(bars + ACC_EMPTY + acc, ((j / 2) - 1) & 1, abrt, a.err)) break;
                 tc_fence_after();
 #pragma unroll 1
@@ -573,15 +622,18 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t ad = a_desc0 + (uint64_t)(as * a_slot16);
+                    const uint32_t ta = a_col0 + (uint32_t)(32 * as);
                     const uint64_t bd = b_desc0 + (uint64_t)(bs * b_slot16);
-                    mma_f16(d_col, ad, bd, idesc, t != 0 ? 1u : 0u);
-                    mma_f16(d_col, ad + a_kstep, bd + b_kstep, idesc, 1u);
-                    mma_f16(d_col, ad + 2 * a_kstep, bd + 2 * b_kstep, idesc, 1u);
-                    mma_f16(d_col, ad + 3 * a_kstep, bd + 3 * b_kstep, idesc, 1u);
+                    mma_f16_ta(d_col, ta, bd, idesc, t != 0 ? 1u : 0u);
+                    mma_f16_ta(d_col, ta + 8, bd + b_kstep, idesc, 1u);
+                    mma_f16_ta(d_col, ta + 16, bd + 2 * b_kstep, idesc, 1u);
+                    mma_f16_ta(d_col, ta + 24, bd + 3 * b_kstep, idesc, 1u);
                     if (!Q6 && t == STEPS - 1) {
-                        mma_f16(d_col + 128, a2_desc0 + (uint64_t)((j % SA2) * (A2_BYTES >> 4)),
-                                bd + (uint64_t)(4 * b_kstep), idesc, 0u);
+                        // the min term: D2[b] = sum_j m_j (hi_j + lo_j) of the x piece's
+                        // 32-column sums (k 0-7 against the hi parts, 8-15 the lo parts)
+                        mma_f16(tmem + (uint32_t)(D2_COL + 64 * acc),
+                                a2_desc0 + (uint64_t)((j % SA2) * (A2_BYTES >> 4)),
+                                b2_desc0 + (uint64_t)(bs * b_slot16), idesc2, 0u);
                     }
                     mma_commit(bars + EMPTY_A + as);
                     mma_commit(bars + EMPTY_B + bs);
@@ -608,15 +660,16 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
         // warps 8-15: read the accumulators out. Thread rt owns tile row
         // row = rt % 128 (TMEM lane row) and the vectors 32 half .. 32 half
         // + 31, half = rt / 128. Per super-block jp (after its MMAs):
-        //   acc[b] += inv[b] * (d * (D[2b] + D[2b+1]) - dmin * (D2[2b] + D2[2b+1]))
+        //   acc[b] += inv[b] * (d * (D[2b] + D[2b+1]) - dmin * D2[b])
         // with the row's d, dmin and the x piece's inverse scales from slot
         // jp % SINV. Slot lifetimes: the dequantisers write slot jp % SINV
-        // at the start of super-block jp and again at jp + SINV, i.e. at step
-        // STEPS (jp + 4); they start a step only after the MMAs of the step
-        // SA = 5 before it completed, here a step of super-block jp + 2 (or
-        // later), whose MMAs the issuer starts only after this readout has
-        // freed its accumulator set (ACC_EMPTY, arrived after the last read
-        // of the slot).
+        // at the start of super-block jp and again at the start of jp +
+        // SINV, after the last step of jp + SINV - 1, for which they waited
+        // until the MMAs of the step SA before it completed: a step of
+        // super-block jp + 2 or later (SA < 2 STEPS, SINV >= 4), whose MMAs
+        // the issuer starts only after this readout has freed its
+        // accumulator set (ACC_EMPTY, arrived after the last read of the
+        // slot).
         const int rt = tid - RO_WARP0 * 32;
         const int row = rt & (TM - 1), half = rt >> 7;
         const int b0 = 32 * half;
@@ -633,18 +686,22 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
             const uint32_t hd = dd[(jp % SINV) * TM + row];
             const float d = hf(hd & 0xFFFFu), dmin = hf(hd >> 16);
             const float *iv = inv_s + (jp % SINV) * VMAX + b0;
-            const uint32_t col = lane_base + (uint32_t)(accs * 256 + 2 * b0);
+            const uint32_t col = lane_base + (uint32_t)(accs * 128 + 2 * b0);
+            const uint32_t col2 = lane_base + (uint32_t)(D2_COL + 64 * accs + b0);
 #pragma unroll
             for (int q = 0; q < 4; q++) {
                 if (2 * b0 + 16 * q < N) {
-                    float v[16], v2[16];
-                    tmem_ld16x2(col + 16 * q, col + (Q6 ? 16 * q : 128 + 16 * q), v, v2);
+                    float v[16], v2[8];
+                    if (Q6) {
+                        tmem_ld16(col + 16 * q, v);
+                    } else {
+                        tmem_ld16x8(col + 16 * q, col2 + 8 * q, v, v2);
+                    }
 #pragma unroll
                     for (int i = 0; i < 8; i++) {
                         const int b = 8 * q + i;
                         const float t1 = d * (v[2 * i] + v[2 * i + 1]);
-                        acc[b] = Q6 ? fmaf(iv[b], t1, acc[b])
-                                    : fmaf(iv[b], fmaf(-dmin, v2[2 * i] + v2[2 * i + 1], t1), acc[b]);
+                        acc[b] = Q6 ? fmaf(iv[b], t1, acc[b]) : fmaf(iv[b], fmaf(-dmin, v2[i], t1), acc[b]);
                     }
                 }
             }
@@ -659,7 +716,7 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
                 flush_piece(out, a.seg_y[sg], a.ypart, a.arrived, a.seg_rows[sg], a.n, a.nsb, a.U, a.G, a.maxp, rT,
                             rT - a.tile0[sg], c, row, b0);
             }
-            if (++rs == a.nsb) {
+        if (++rs == a.nsb) {
                 rs = 0;
                 rT++;
             }
@@ -676,6 +733,8 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
         // the readout.
         const int row = tid & (TM - 1), half = tid >> 7;
         uint32_t *dd = reinterpret_cast<uint32_t *>(sm + OFF_DD);
+        // this warp's TMEM lanes (32 (warp % 4) ..) at the A ring's first column
+        const uint32_t a_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)ACOL;
         bool ok = true;
         int as = 0;
         uint32_t ea_ph = 0;  // parity of the A slot's next EMPTY completion
@@ -697,44 +756,52 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
                                         (uintptr_t)((dT - a.tile0[sg]) * TM + row) * a.seg_rb[sg] +
                                         (uintptr_t)ds * Fmt<T_Q6_K>::BLK;
                 const uint8_t *blk = wslot + row * SBB + (gaddr & 15u);
-                uint32_t scw[4], ql[16], qh6[8];
-                ld_words_a2<4>(blk + 192, scw);  // the 16 signed 8-bit scales
+                uint32_t ql[16], qh6[8], scw[2];
                 if (half == 0) dd[(j % SINV) * TM + row] = ld_u16(blk + 208);  // d; no mins
+                // the two halves of the block (h: columns 128h ..) in a runtime
+                // loop, the four steps of a half unrolled: every array index
+                // below is a constant, so the words stay in registers
 #pragma unroll 1
-                for (int t = 0; t < STEPS; t++) {
-                    const int i = STEPS * j + t;
-                    if (i >= SA && !warp_wait(bars + EMPTY_A + as, ea_ph, abrt, a.err)) {
-                        ok = false;
-                        break;
-                    }
-                    // step t: columns 32t .. 32t + 31 = 128h + 32m + l of the block
-                    const int h = t >> 2, m = t & 3;
-                    if (m == 0) {
-                        ld_words_a2<16>(blk + 64 * h, ql);        // ql bytes 64h .. 64h + 63
-                        ld_words_a2<8>(blk + 128 + 32 * h, qh6);  // qh bytes 32h .. 32h + 31
-                        if (h == 1) mbar_arrive(bars + EMPTY_W + ws);  // the slot's last read
-                    }
-                    const int nsh = m >= 2 ? 4 : 0, hsh = 2 * m, wb = 8 * (m & 1);
-                    uint8_t *arow = sm + OFF_A + as * A_BYTES + row * 16 + half * 4 * (TM * 16);
+                for (int h = 0; h < 2 && ok; h++) {
+                    ld_words_a2<16>(blk + 64 * h, ql);        // ql bytes 64h .. 64h + 63
+                    ld_words_a2<8>(blk + 128 + 32 * h, qh6);  // qh bytes 32h .. 32h + 31
+                    ld_words_a2<2>(blk + 192 + 8 * h, scw);   // the signed scales 8h .. 8h + 7
+                    if (h == 1) mbar_arrive(bars + EMPTY_W + ws);  // the slot's last read
 #pragma unroll
-                    for (int cc = 0; cc < 4; cc++) {
-                        // columns l = 8cc .. 8cc + 7; scale group 2t + l / 16; this
-                        // half's part of sc = 16 a + b: 16 a (k 0-31) or b (k 32-63)
-                        const int g = 2 * t + (cc >> 1);
-                        const int sc = (int)(int8_t)((scw[g >> 2] >> (8 * (g & 3))) & 255u);
-                        const __half2 s2 = __float2half2_rn(half == 0 ? (float)(16 * (sc >> 4)) : (float)(sc & 15));
-                        const uint32_t q0 = ((ql[wb + 2 * cc] >> nsh) & 0x0F0F0F0Fu) |
-                                            (((qh6[2 * cc] >> hsh) & 0x03030303u) << 4);
-                        const uint32_t q1 = ((ql[wb + 2 * cc + 1] >> nsh) & 0x0F0F0F0Fu) |
-                                            (((qh6[2 * cc + 1] >> hsh) & 0x03030303u) << 4);
-                        *reinterpret_cast<uint4 *>(arow + cc * (TM * 16)) =
-                            make_uint4(q6pair(q0, s2), q6pair(q0 >> 8, s2), q6pair(q1, s2), q6pair(q1 >> 8, s2));
-                    }
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    mbar_arrive(bars + FULL_A + as);
-                    if (++as == SA) {
-                        as = 0;
-                        if (i >= SA) ea_ph ^= 1u;
+                    for (int m = 0; m < 4; m++) {
+                        const int i = STEPS * j + 4 * h + m;
+                        if (i >= SA && !warp_wait(bars + EMPTY_A + as, ea_ph, abrt, a.err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();  // the MMAs that read this A slot have completed
+                        // step 4h + m: columns 128h + 32m + l of the block
+                        const int nsh = m >= 2 ? 4 : 0, hsh = 2 * m, wb = 8 * (m & 1);
+                        uint32_t aw[16];  // this half of the step: tensor-memory columns 16 half .. + 15
+#pragma unroll
+                        for (int cc = 0; cc < 4; cc++) {
+                            // columns l = 8cc .. 8cc + 7; scale 8h + 2m + l / 16; this
+                            // half's part of sc = 16 a + b: 16 a (k 0-31) or b (k 32-63)
+                            const int g = 2 * m + (cc >> 1);
+                            const int sc = (int)(int8_t)((scw[g >> 2] >> (8 * (g & 3))) & 255u);
+                            const __half2 s2 =
+                                __float2half2_rn(half == 0 ? (float)(16 * (sc >> 4)) : (float)(sc & 15));
+                            const uint32_t q0 = ((ql[wb + 2 * cc] >> nsh) & 0x0F0F0F0Fu) |
+                                                (((qh6[2 * cc] >> hsh) & 0x03030303u) << 4);
+                            const uint32_t q1 = ((ql[wb + 2 * cc + 1] >> nsh) & 0x0F0F0F0Fu) |
+                                                (((qh6[2 * cc + 1] >> hsh) & 0x03030303u) << 4);
+                            aw[4 * cc] = q6pair(q0, s2);
+                            aw[4 * cc + 1] = q6pair(q0 >> 8, s2);
+                            aw[4 * cc + 2] = q6pair(q1, s2);
+                            aw[4 * cc + 3] = q6pair(q1 >> 8, s2);
+                        }
+                        tmem_st16(a_lane + (uint32_t)(32 * as + 16 * half), aw);
+                        tc_fence_before();
+                        mbar_arrive(bars + FULL_A + as);
+                        if (++as == SA) {
+                            as = 0;
+                            if (i >= SA) ea_ph ^= 1u;
+                        }
                     }
                 }
             } else {
@@ -751,13 +818,14 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
                 uint32_t scp[4], mnp[4];  // (scale, min) of sub-blocks 2t (low byte) and 2t + 1
 #pragma unroll
                 for (int t = 0; t < 4; t++) scale_min_pair(hdr.y, hdr.z, hdr.w, t, scp[t], mnp[t]);
-#pragma unroll 1
-                for (int t = 0; t < 4; t++) {
+#pragma unroll
+                for (int t = 0; t < 4; t++) {  // unrolled: scp[t] stays in registers
                     const int i = 4 * j + t;
                     if (i >= SA && !warp_wait(bars + EMPTY_A + as, ea_ph, abrt, a.err)) {
                         ok = false;
                         break;
                     }
+                    tc_fence_after();  // the MMAs that read this A slot have completed
                     const uint4 qa = *reinterpret_cast<const uint4 *>(wrow + Fmt<FT>::QS + 32 * t);
                     const uint4 qb = *reinterpret_cast<const uint4 *>(wrow + Fmt<FT>::QS + 16 + 32 * t);
                     if (t == 3) mbar_arrive(bars + EMPTY_W + ws);
@@ -767,7 +835,7 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
                     const __half2 sc2 = __halves2half2(sc, sc);
                     const __half2 nsc2 = __hmul2(sc2, __float2half2_rn(-1024.0f));
                     const int sh = 4 * half;
-                    uint8_t *arow = sm + OFF_A + as * A_BYTES + row * 16 + half * 4 * (TM * 16);
+                    uint32_t aw[16];  // this half of the step: tensor-memory columns 16 half .. + 15
 #pragma unroll
                     for (int cc = 0; cc < 4; cc++) {
                         // columns 8cc .. 8cc+7 of the sub-block: nibbles of bytes 8cc .. 8cc+7
@@ -778,12 +846,15 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
                             w0 = (w0 & 0x0F0F0F0Fu) | (((qh[2 * cc] >> hs) & 0x01010101u) << 4);
                             w1 = (w1 & 0x0F0F0F0Fu) | (((qh[2 * cc + 1] >> hs) & 0x01010101u) << 4);
                         }
-                        *reinterpret_cast<uint4 *>(arow + cc * (TM * 16)) =
-                            make_uint4(nib2<FT>(w0, sc2, nsc2), nib2<FT>(w0 >> 8, sc2, nsc2), nib2<FT>(w1, sc2, nsc2),
-                                       nib2<FT>(w1 >> 8, sc2, nsc2));
+                        aw[4 * cc] = nib2<FT>(w0, sc2, nsc2);
+                        aw[4 * cc + 1] = nib2<FT>(w0 >> 8, sc2, nsc2);
+                        aw[4 * cc + 2] = nib2<FT>(w1, sc2, nsc2);
+                        aw[4 * cc + 3] = nib2<FT>(w1 >> 8, sc2, nsc2);
                     }
+                    tmem_st16(a_lane + (uint32_t)(32 * as + 16 * half), aw);
                     if (t == 0 && half == 0) {
-                        // A2 row: the 8 mins of this super-block (chunk 0, natural order)
+                        // A2 row: the 8 mins of this super-block in natural order, in
+                        // chunk 0 (against the hi parts of the sums) and chunk 1 (lo)
                         uint32_t m2[4];
 #pragma unroll
                         for (int p = 0; p < 4; p++) {
@@ -791,11 +862,13 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
                                                              __ushort2half_rn((unsigned short)(mnp[p] >> 8)));
                             m2[p] = *reinterpret_cast<const uint32_t *>(&h);
                         }
-                        *reinterpret_cast<uint4 *>(sm + OFF_A2 + (j % SA2) * A2_BYTES + row * 16) =
-                            make_uint4(m2[0], m2[1], m2[2], m2[3]);
+                        uint8_t *a2row = sm + OFF_A2 + (j % SA2) * A2_BYTES + row * 16;
+                        *reinterpret_cast<uint4 *>(a2row) = make_uint4(m2[0], m2[1], m2[2], m2[3]);
+                        *reinterpret_cast<uint4 *>(a2row + TM * 16) = make_uint4(m2[0], m2[1], m2[2], m2[3]);
+                        // the generic-proxy writes, seen by the tensor core's async proxy
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     }
-                    // the generic-proxy writes above, seen by the tensor core's async proxy
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    tc_fence_before();
                     mbar_arrive(bars + FULL_A + as);
                     if (++as == SA) {
                         as = 0;
@@ -822,14 +895,14 @@ __global__ void __launch_bounds__(THREADS, 1) qk_mm_kernel(const __grid_constant
 // x into the B operands. Block (s, b) stages super-block s of vector b:
 // scale = a power of two with max |x piece| * scale < 2^10 (1 for a zero or
 // non-finite piece), rows nn = 2b (hi) and 2b + 1 (lo) of the four step
-// tiles, the 32-column sums in B2, and 1 / scale in xinv. Blocks with
-// b >= n write the zero rows up to N. 256 threads, thread t = column
-// 256 s + t.
-__global__ void __launch_bounds__(256) mm_stage_kernel(const float *x, int n, int K, int N, uint8_t *xs, uint8_t *x2s,
-                                                       float *xinv)
+// tiles (b < N / 2), row b of B2 (b < N2: the 32-column sums, hi parts at
+// k 0-7, lo parts at k 8-15), and 1 / scale in xinv. Blocks with b >= n
+// write the zero rows. 256 threads, thread t = column 256 s + t.
+__global__ void __launch_bounds__(256) mm_stage_kernel(const float *x, int n, int K, int N, int N2, uint8_t *xs,
+                                                       uint8_t *x2s, float *xinv)
 {
     __shared__ float red[8];
-    const int s = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
+    const int s = blockIdx.x, b = blockIdx.y, t = threadIdx.x;  // b < max(N / 2, N2)
     const float xv = b < n ? x[(size_t)b * K + (size_t)s * QK + t] : 0.0f;
     float m = fabsf(xv);
 #pragma unroll
@@ -849,24 +922,26 @@ __global__ void __launch_bounds__(256) mm_stage_kernel(const float *x, int n, in
     const __half hi = __float2half_rn(v);
     const __half lo = __float2half_rn(v - __half2float(hi));
     const int step = t >> 6, chunk = (t >> 3) & 7, e = t & 7;
-    uint8_t *run = xs + ((size_t)s * 4 + step) * N * 128 + (size_t)chunk * N * 16 + (size_t)(2 * b) * 16 + perm8(e) * 2;
-    *reinterpret_cast<__half *>(run) = hi;
-    *reinterpret_cast<__half *>(run + 16) = lo;
+    if (2 * b < N) {
+        uint8_t *run =
+            xs + ((size_t)s * 4 + step) * N * 128 + (size_t)chunk * N * 16 + (size_t)(2 * b) * 16 + perm8(e) * 2;
+        *reinterpret_cast<__half *>(run) = hi;
+        *reinterpret_cast<__half *>(run + 16) = lo;
+    }
     // warp w holds sub-block w: its sum, then split
     float sum = v;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
-    if ((t & 31) == 0) {
+    if ((t & 31) == 0 && b < N2) {
+        // B2 row b: k 0-7 the hi parts of the 8 sums (chunk 0), k 8-15 the lo parts
         const int j = t >> 5;
         const __half shi = __float2half_rn(sum);
         const __half slo = __float2half_rn(sum - __half2float(shi));
-        uint8_t *row = x2s + (size_t)s * N * 32 + (size_t)(2 * b) * 16 + j * 2;
+        uint8_t *row = x2s + (size_t)s * N2 * 32 + (size_t)b * 16 + j * 2;
         *reinterpret_cast<__half *>(row) = shi;
-        *reinterpret_cast<__half *>(row + 16) = slo;
-        *reinterpret_cast<__half *>(row + (size_t)N * 16) = __half();  // chunk 1: k 8..15
-        *reinterpret_cast<__half *>(row + (size_t)N * 16 + 16) = __half();
+        *reinterpret_cast<__half *>(row + (size_t)N2 * 16) = slo;
     }
-    if (t == 0) xinv[(size_t)s * VMAX + b] = b < n ? 1.0f / scale : 0.0f;
+    if (t == 0 && b < VMAX) xinv[(size_t)s * VMAX + b] = b < n ? 1.0f / scale : 0.0f;
 }
 
 // x into the B operands of the Q6_K launch: each 32-column piece of a
@@ -997,6 +1072,12 @@ extern "C" void gguf_cuda_matmul_plan(int rows, int nsb, int sms, int *ctas, int
     plan_tiles((rows + mm::TM - 1) / mm::TM, nsb, sms, ctas, maxp);
 }
 
+// MMA N of the min term: one column per vector, a multiple of 16.
+static int mm_n2(int n)
+{
+    return n <= 16 ? 16 : (n + 15) / 16 * 16;
+}
+
 static int mm_sbb(uint32_t type)
 {
     return type == T_Q4_K ? mm::Fmt<T_Q4_K>::SBB : type == T_Q5_K ? mm::Fmt<T_Q5_K>::SBB
@@ -1078,7 +1159,9 @@ int pk_mm_stage(uint32_t type, const float *x, int n, int cols, const PkMmScratc
     if (type == T_Q6_K) {
         mm::mm_stage6_kernel<<<dim3(cols / mm::QK, N / 2), 256, 0, st>>>(x, n, cols, N, s->xs, s->xinv);
     } else {
-        mm::mm_stage_kernel<<<dim3(cols / mm::QK, N / 2), 256, 0, st>>>(x, n, cols, N, s->xs, s->x2s, s->xinv);
+        const int N2 = mm_n2(n);
+        mm::mm_stage_kernel<<<dim3(cols / mm::QK, N / 2 > N2 ? N / 2 : N2), 256, 0, st>>>(x, n, cols, N, N2, s->xs,
+                                                                                         s->x2s, s->xinv);
     }
     return cudaGetLastError() == cudaSuccess;
 }
@@ -1127,7 +1210,8 @@ int pk_mm_run_staged(const PkMmSeg *seg, int nseg, int cols, int n, const PkMmSc
     a.xinv = s->xinv;
     a.n = n;
     a.N = N;
-    a.b_slot = N * 160;
+    a.N2 = mm_n2(n);
+    a.b_slot = N * 128 + (type == T_Q6_K ? 0 : a.N2 * 32);
     a.sb = (s->smem_max - off_b - 128) / a.b_slot;
     if (a.sb > mm::SB_MAX) a.sb = mm::SB_MAX;
     a.U = tiles * nsb;
@@ -1136,7 +1220,9 @@ int pk_mm_run_staged(const PkMmSeg *seg, int nseg, int cols, int n, const PkMmSc
     a.ypart = s->ypart;
     a.arrived = s->arrived;
     a.err = s->err;
-    const int smem = off_b + a.sb * a.b_slot + 128;
+    // one CTA per SM: each allocates all 512 tensor-memory columns
+    int smem = off_b + a.sb * a.b_slot + 128;
+    if (smem <= s->smem_max / 2) smem = s->smem_max / 2 + 128;
     if (type == T_Q5_K) {
         mm::qk_mm_kernel<T_Q5_K><<<G, mm::THREADS, smem, st>>>(maps, a);
     } else if (type == T_Q6_K) {
