@@ -1,37 +1,41 @@
 // pk_mma.cu - the batched fused dequant-matmul on the sm_100a tensor cores:
 // Y[b][r] = sum_k W[r][k] * x_b[k] for up to 64 activation vectors x_b that
-// share one pass over the packed Q4_K or Q5_K weights (the matmul form of
-// the matvec, src/gguf_model.c:693-771, for several sequences at once).
+// share one pass over the packed Q4_K, Q5_K or Q6_K weights (the matmul
+// form of the matvec, src/gguf_model.c:693-771, for several sequences at
+// once).
 //
 // Operands (fp16 products are exact in the fp32 accumulator):
 //   A (weights): per super-block of 256 columns, the integers sc_j * q
 //       (at most 63 * 15 for Q4_K, 63 * 31 for Q5_K: below 2048, exact in
 //       fp16), one LOP3 (two for Q5_K, whose fifth bit comes from qh) and
-//       one HFMA2 per two weights; the super-block scales d and dmin stay out of the product
+//       one HFMA2 per two weights, written by the dequantising threads
+//       straight into tensor memory (tcgen05.st: row = lane, two fp16 per
+//       column); the super-block scales d and dmin stay out of the product
 //       and are applied in fp32 when the accumulator is read out. A second
-//       operand A2 holds the 6-bit mins m_j.
-//   B (activations): each 256-column piece of every x_b, scaled by a power
-//       of two so that its largest magnitude is below 2^10, split into two
-//       fp16 parts hi = fp16(x) and lo = fp16(x - hi) (22 significant bits
-//       together), at MMA columns 2b and 2b + 1. B2 holds the 32-column
-//       sums of the scaled piece (the Q4_K min term sum_j m_j * xsum_j) the
-//       same way.
-//   D = A x B and D2 = A2 x B2 in TMEM (fp32, M = 128 rows, N = 2n rounded
-//       up to 16), read out once per super-block:
-//       y[b] += (d * (D[2b] + D[2b+1]) - dmin * (D2[2b] + D2[2b+1])) / scale.
+//       operand A2 (shared memory) holds the 6-bit mins m_j, twice.
+//   B (activations, shared memory): each 256-column piece of every x_b,
+//       scaled by a power of two so that its largest magnitude is below
+//       2^10, split into two fp16 parts hi = fp16(x) and lo = fp16(x - hi)
+//       (22 significant bits together), at MMA columns 2b and 2b + 1. B2
+//       holds the 32-column sums of the scaled piece (the min term
+//       sum_j m_j * xsum_j): row b, the hi parts at k 0-7 and the lo parts
+//       at k 8-15, so that one MMA adds both.
+//   D = A x B (N = 2n rounded up to 16) and D2 = A2 x B2 (N2 = n rounded up
+//       to 16) in TMEM, fp32, M = 128 rows, read out once per super-block:
+//       y[b] += (d * (D[2b] + D[2b+1]) - dmin * D2[b]) / scale.
 //
 // One CTA per SM, warp-specialised, every hand-off an mbarrier:
 //   warps 0-7   dequantise into A: thread t owns weight row t % 128 of the
-//               tile; warps 0-3 take the low-nibble sub-block of each
-//               64-column step, warps 4-7 the high-nibble one;
+//               tile (= TMEM lane); warps 0-3 take the low-nibble sub-block
+//               of each 64-column step, warps 4-7 the high-nibble one;
 //   warps 8-15  read the accumulators out: thread t owns tile row (= TMEM
 //               lane) t % 128, warps 8-11 vectors 0-31, warps 12-15 vectors
 //               32-63, and keep the running sums of the tile piece;
 //   warp 16     loads the weight super-blocks of the tile (128 rows x 144
 //               bytes, one 2D TMA tensor copy each, plus the 64 scales of
-//               that x piece) into a 3-deep ring;
+//               that x piece) into a 4-deep ring;
 //   warp 17     bulk-copies the staged x of each 64-column step into a ring
-//               as deep as shared memory allows (3 steps at n = 64, 24 at
+//               as deep as shared memory allows (7 steps at n = 64, 32 at
 //               n <= 8);
 //   warp 18     allocates TMEM and issues the MMAs from one lane, committing
 //               to the barriers that free the A and B slots and publish the
@@ -42,18 +46,20 @@
 // Work units are (row tile, super-block) pairs, split evenly over the CTAs
 // in row-tile-major order. A tile split over several CTAs leaves one partial
 // sum per CTA; for each block of 32 rows x 32 vectors the last CTA to
-// finish it adds the partials up in CTA order (a fixed order: the result does not depend on
-// timing). Two launches per call: the x staging kernel, then this one.
+// finish it adds the partials up in CTA order (a fixed order: the result
+// does not depend on timing). Two launches per call: the x staging kernel,
+// then this one.
 //
-// Shared-memory operands are fp16, K-major, without swizzle: core matrices
-// of 8 rows x 16 bytes, rows 16 bytes apart. A step tile of 64 columns is
-// [8 column chunks][rows][16 bytes]; element (row, k) sits at
+// Shared-memory operands (B, B2, A2) are fp16, K-major, without swizzle:
+// core matrices of 8 rows x 16 bytes, rows 16 bytes apart. A step tile of
+// 64 columns is [8 column chunks][rows][16 bytes]; element (row, k) sits at
 //     (k / 8) * chunk_bytes + row * 16 + pos(k % 8) * 2,
-// chunk_bytes = 128 * 16 for A, N * 16 for B (the descriptors' leading
-// offset; their stride offset is 128 bytes, the next 8 rows). pos()
-// permutes each run of 8 columns as {0, 2, 1, 3, 4, 6, 5, 7}: the order in
-// which one LOP3 takes the nibbles out of a 32-bit word of packed weights
-// (the sum over k does not depend on the order).
+// chunk_bytes = N * 16 (the descriptors' leading offset; their stride offset
+// is 128 bytes, the next 8 rows). pos() permutes each run of 8 columns as
+// {0, 2, 1, 3, 4, 6, 5, 7}: the order in which one LOP3 takes the nibbles
+// out of a 32-bit word of packed weights. A in tensor memory holds the same
+// 16-byte runs, in the same order, in four consecutive columns (the sum over
+// k does not depend on the order as long as A and B agree).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
