@@ -1051,16 +1051,18 @@ MmScratch *mm_scratch(int dev, size_t xs_b, size_t x2s_b, size_t xinv_b, size_t 
 
 }  // namespace
 
-// The work split of gguf_cuda_matmul for a matrix of `rows` rows and `nsb`
-// super-blocks per row on `sms` SMs: CTAs, and partial slots per row tile.
-// At most one CTA per SM, and no more CTAs than split each row tile in
-// about two pieces: the last CTA of a tile adds the pieces up after all
-// others, so many pieces per tile leave one straggler per tile.
+// The work split of the batched matmul for a matrix of `tiles` row tiles
+// and `nsb` super-blocks per row on `sms` SMs: CTAs, and partial slots per
+// row tile. At most one CTA per SM, and no more CTAs than split each row
+// tile in about four pieces: every CTA pays a fixed cost (tensor memory,
+// barriers, the first copies) and the last CTA of a split tile adds the
+// pieces up after the others, so short pieces cost more than they save
+// (measured on the TinyLlama and Llama shapes: two pieces per tile leave
+// SMs idle, eight or one per SM are slower than four).
 static void plan_tiles(int tiles, int nsb, int sms, int *ctas, int *maxp)
 {
     const long long U = (long long)tiles * nsb;
-    long long G = (2 * U + nsb - 1) / nsb;  // about two pieces per tile
-    if (G < tiles) G = tiles;
+    long long G = 4LL * tiles;  // about four pieces per tile
     if (G > sms) G = sms;
     if (G > U) G = U;
     int mp = 1;

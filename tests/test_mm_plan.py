@@ -1,6 +1,6 @@
 """Host-side work split of the batched matmul (gguf_cuda_matmul_plan): the
 (row tile, super-block) units are split evenly over at most one CTA per SM
-and about two CTAs per row tile, and the partial-sum slots per tile cover
+and about four CTAs per row tile, and the partial-sum slots per tile cover
 every CTA that shares the tile.
 Runs without a GPU."""
 import pytest
@@ -11,7 +11,7 @@ import pk_b200
 def brute(rows, nsb, sms):
     tiles = (rows + 127) // 128
     U = tiles * nsb
-    G = min(U, sms, max(tiles, -(-2 * U // nsb)))
+    G = min(U, sms, 4 * tiles)
     owner = []
     for c in range(G):
         owner += [c] * ((c + 1) * U // G - c * U // G)
