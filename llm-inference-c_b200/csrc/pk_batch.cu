@@ -463,9 +463,10 @@ __global__ void __launch_bounds__(128) attention_kernel(const float *q, const KV
 // w, w + 16, ...; weighted sum: thread (tg, d4) reads float4 d4 of the
 // value rows t = tg mod G (G = 512 / (hs / 4)) once and adds p_h[t] times
 // it for every head h, and the G partials are added in order.
-// 512 threads; H <= 8, H * hs / 4 <= 128.
+// 512 threads, two CTAs per SM (the loads in flight of two CTAs keep HBM
+// busier than longer unrolls in one); H <= 8, H * hs / 4 <= 128.
 template <typename KV>
-__global__ void __launch_bounds__(512) attention_gqa_kernel(const float *q, const KV *kc, const KV *vc,
+__global__ void __launch_bounds__(512, 2) attention_gqa_kernel(const float *q, const KV *kc, const KV *vc,
                                                             const int *io, int bmax, int layer, int L, int seq_len,
                                                             int hs, int qd, int kvd, int H, float scale, float *out)
 {
@@ -483,6 +484,7 @@ __global__ void __launch_bounds__(512) attention_gqa_kernel(const float *q, cons
         float dot[8];
 #pragma unroll
         for (int h = 0; h < 8; h++) dot[h] = 0.0f;
+#pragma unroll 4  // several key loads in flight per thread
         for (int i = 0; i < F4; i++) {
             const float4 kv = kv_load4(kt, 4 * (size_t)i);
 #pragma unroll
@@ -529,7 +531,7 @@ __global__ void __launch_bounds__(512) attention_gqa_kernel(const float *q, cons
         float4 o[8];
 #pragma unroll
         for (int h = 0; h < 8; h++) o[h] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll 2
+#pragma unroll 4  // several value loads in flight per thread
         for (int t = tg; t < P; t += G) {
             const float4 vv = kv_load4(vb, (size_t)t * kvd);
 #pragma unroll
