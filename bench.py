@@ -735,6 +735,8 @@ def main():
     ap.add_argument("--no-tp7b", action="store_true", help="skip the Llama-2-7B tensor-parallel object")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the Llama-2-7B B=16 and Llama-3-8B prefill/decode objects")
+    ap.add_argument("--configs", default="both", choices=["both", "llama2_7b_b16", "llama3_8b"],
+                    help="which of those two objects to run")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     os.environ["POCKET_CUDA_KV"] = args.kv
@@ -881,9 +883,11 @@ def main():
         note("matvec sweep done")
     cfg3 = cfg4 = None
     if rank == 0 and world == 1 and not args.no_configs and args.workload == "tinyllama":
-        cfg3 = run_cfg3(args)
-        note("7B B=16 done")
-        cfg4 = run_cfg4(args)
+        if args.configs in ("both", "llama2_7b_b16"):
+            cfg3 = run_cfg3(args)
+            note("7B B=16 done")
+        if args.configs in ("both", "llama3_8b"):
+            cfg4 = run_cfg4(args)
     tp7b = None
     if not args.no_tp7b and args.workload == "tinyllama":
         tp7b = run_tp7b(args, world, rank, local, barrier, allmax)
