@@ -144,6 +144,12 @@ class ClockSampler:
                  "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # nvidia-smi takes a moment to start: wait for its first sample so
+            # that a short timed region still has samples around it
+            t0 = time.perf_counter()
+            while not self.rows and time.perf_counter() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.02)
+            self.first = len(self.rows)
         except OSError:
             self.proc = None
         return self
@@ -156,6 +162,10 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            # one sample taken after the region ends (at least 100 ms apart)
+            n, t0 = len(self.rows), time.perf_counter()
+            while len(self.rows) <= n and time.perf_counter() - t0 < 1.0 and self.proc.poll() is None:
+                time.sleep(0.02)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
