@@ -112,7 +112,10 @@ int engine_launches_per_step(const LLMModel *model);
 #define ENGINE_BATCH_MAX 64
 
 /* Allocate the batched state for max_seqs sequences (1..64), dropping any
- * previous one. Returns 1, or 0 with a message in error. */
+ * previous one. On a tensor-parallel rank (after engine_tp_connect) every
+ * rank of the group opens the same state: each rank keeps the KV heads of
+ * its own query heads for every sequence. Returns 1, or 0 with a message in
+ * error. */
 int engine_batch_open(LLMModel *model, int max_seqs, char *error, size_t error_capacity);
 
 /* One step over n <= 64 rows: sequence seq_ids[i] consumes tokens[i] at
@@ -126,8 +129,12 @@ int engine_batch_open(LLMModel *model, int max_seqs, char *error, size_t error_c
  * any row attends, so row i sees the sequence's positions 0 .. pos[i].
  * next_tokens[i] receives the greedy token of row i (device argmax, lowest
  * index on ties; -1 when a logit is not finite); logits, when not NULL, the
- * n x vocab_size logits. Returns 1, or 0 on bad arguments or a device error
- * (engine_last_error). */
+ * n x vocab_size logits. Tensor parallel: every rank of the group makes the
+ * same call (the same rows, and logits given on all ranks or on none); the
+ * ranks add their heads' and hidden slices' partial sums after Wo and
+ * ffn_down over NVLink, pick the greedy tokens over their vocabulary slices,
+ * and each rank returns the same tokens (and full logits). Returns 1, or 0
+ * on bad arguments or a device error (engine_last_error). */
 int engine_forward_batch(LLMModel *model, const int *tokens, const int *pos, const int *seq_ids, int n,
                          int *next_tokens, float *logits);
 

@@ -971,10 +971,6 @@ int engine_batch_open(LLMModel *m, int max_seqs, char *err, size_t cap)
         seterr(err, cap, "No model.");
         return 0;
     }
-    if (m->tp_world > 1) {
-        seterr(err, cap, "Batched decode runs on one GPU (not on a tensor-parallel rank).");
-        return 0;
-    }
     if (max_seqs < 1 || max_seqs > ENGINE_BATCH_MAX) {
         seterr(err, cap, "Batched decode takes 1 to 64 sequences.");
         return 0;

@@ -564,6 +564,158 @@ __global__ void __launch_bounds__(512, 2) attention_gqa_kernel(const float *q, c
     }
 }
 
+// ------------------------------------------------------------------ //
+// Tensor parallel exchanges of the batched step                      //
+// ------------------------------------------------------------------ //
+//
+// Every rank's exchange region holds [2 slots][world][len] 64-bit words
+// (tag << 32 | payload). Exchange t (tags are consecutive over all of a
+// handle's exchanges; 0 never appears) uses slot t & 1: each rank writes
+// its part into part `rank` of that slot on every rank (NVLink stores) and
+// then polls its own copy of the other parts until they carry tag t. A
+// rank writes slot s again two exchanges later, only after it has read the
+// exchange between them, which its peers published after finishing their
+// reads of slot s: no word is overwritten before it is read. Every poll is
+// bounded and records a timeout in the error word.
+
+constexpr long long TP_WAIT_LIMIT_CYCLES = 20000000000LL;  // ~10 s: a peer may start its step later
+constexpr int TP_ERR_TIMEOUT = 2;
+
+struct TpX {
+    uint64_t *peer[PKD_TP_MAX];  // each rank's exchange region (slot 0, part 0)
+    uint64_t len;                // words per part
+    int rank, world;
+};
+
+__device__ __forceinline__ void tp_st(uint64_t *p, uint32_t payload, uint32_t tag)
+{
+    const uint64_t w = ((uint64_t)tag << 32) | payload;
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+// The payload of the word at p once it carries `tag` (0 after a timeout).
+__device__ __forceinline__ uint32_t tp_ld(const uint64_t *p, uint32_t tag, int *err)
+{
+    uint64_t w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    if ((uint32_t)(w >> 32) == tag) return (uint32_t)w;
+    const long long t0 = clock64();
+    for (;;) {
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+        if ((uint32_t)(w >> 32) == tag) return (uint32_t)w;
+        if ((*(volatile int *)err & TP_ERR_TIMEOUT) || clock64() - t0 > TP_WAIT_LIMIT_CYCLES) {
+            atomicOr(err, TP_ERR_TIMEOUT);
+            return 0u;
+        }
+    }
+}
+
+// Publish len floats of src as this rank's part of exchange tag0 + idx.
+__global__ void tp_push_kernel(TpX x, const float *src, int len, const int *tag0, int idx)
+{
+    const uint32_t tag = 1u + (uint32_t)tag0[0] + (uint32_t)idx;
+    const size_t off = ((size_t)(tag & 1u) * x.world + x.rank) * x.len;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < len; i += gridDim.x * blockDim.x) {
+        const uint32_t v = __float_as_uint(src[i]);
+        for (int q = 0; q < x.world; q++) tp_st(x.peer[q] + off + i, v, tag);
+    }
+}
+
+// out[i] = the sum of the ranks' parts in rank order (the all-reduce).
+__global__ void tp_sum_kernel(TpX x, float *out, int len, const int *tag0, int idx, int *err)
+{
+    const uint32_t tag = 1u + (uint32_t)tag0[0] + (uint32_t)idx;
+    const uint64_t *mine = x.peer[x.rank] + (size_t)(tag & 1u) * x.world * x.len;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < len; i += gridDim.x * blockDim.x) {
+        float s = __uint_as_float(tp_ld(mine + i, tag, err));
+        for (int q = 1; q < x.world; q++) s = __fadd_rn(s, __uint_as_float(tp_ld(mine + (size_t)q * x.len + i, tag, err)));
+        out[i] = s;
+    }
+}
+
+// The ranks' logits slices (rank q: n rows of voc[q] floats from column
+// voc0[q]) assembled into out[n][vocab].
+__global__ void tp_gather_kernel(TpX x, float *out, int n, int vocab, const int *tag0, int idx, int *err)
+{
+    const uint32_t tag = 1u + (uint32_t)tag0[0] + (uint32_t)idx;
+    const uint64_t *mine = x.peer[x.rank] + (size_t)(tag & 1u) * x.world * x.len;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n * vocab; i += gridDim.x * blockDim.x) {
+        const int b = i / vocab, c = i - b * vocab;
+        int q = 0;
+        while (q + 1 < x.world && c >= (int)((long long)vocab * (q + 1) / x.world)) q++;
+        const int v0 = (int)((long long)vocab * q / x.world), vq = (int)((long long)vocab * (q + 1) / x.world) - v0;
+        out[i] = __uint_as_float(tp_ld(mine + (size_t)q * x.len + (size_t)b * vq + (c - v0), tag, err));
+    }
+}
+
+// Sequence b's greedy token over the ranks' vocabulary slices: the rank's
+// largest logit and its lowest index on ties (src/sampler.c:39-52), as an
+// ordered key, published to every rank; -1 from any rank that saw a
+// non-finite logit.
+__global__ void __launch_bounds__(1024) tp_argmax_push_kernel(TpX x, const float *logits, int voc, int voc0,
+                                                              const int *tag0, int idx)
+{
+    __shared__ unsigned long long best_w[32];
+    __shared__ int bad_w[32];
+    const int b = blockIdx.x, tid = threadIdx.x;
+    unsigned long long best = 0ull;
+    int bad = 0;
+    for (int j = tid; j < voc; j += blockDim.x) {
+        const float v = logits[(size_t)b * voc + j];
+        if (!isfinite(v)) bad = 1;
+        const uint32_t u = __float_as_uint(v);
+        const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+        const unsigned long long k = ((unsigned long long)ord << 32) | (0xFFFFFFFFu - (uint32_t)(voc0 + j));
+        if (k > best) best = k;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long ob = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+        if (ob > best) best = ob;
+        bad |= __shfl_xor_sync(0xFFFFFFFFu, bad, o);
+    }
+    if ((tid & 31) == 0) {
+        best_w[tid >> 5] = best;
+        bad_w[tid >> 5] = bad;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) {
+            if (best_w[w] > best) best = best_w[w];
+            bad |= bad_w[w];
+        }
+        const uint32_t tag = 1u + (uint32_t)tag0[0] + (uint32_t)idx;
+        const size_t off = ((size_t)(tag & 1u) * x.world + x.rank) * x.len + (size_t)b * 3;
+        for (int q = 0; q < x.world; q++) {
+            tp_st(x.peer[q] + off, (uint32_t)(best >> 32), tag);
+            tp_st(x.peer[q] + off + 1, (uint32_t)best, tag);
+            tp_st(x.peer[q] + off + 2, (uint32_t)bad, tag);
+        }
+    }
+}
+
+__global__ void tp_argmax_kernel(TpX x, int n, int *next, const int *tag0, int idx, int *err)
+{
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n) return;
+    const uint32_t tag = 1u + (uint32_t)tag0[0] + (uint32_t)idx;
+    const uint64_t *mine = x.peer[x.rank] + (size_t)(tag & 1u) * x.world * x.len;
+    unsigned long long best = 0ull;
+    bool bad = false;
+    for (int q = 0; q < x.world; q++) {
+        const uint64_t *w = mine + (size_t)q * x.len + (size_t)b * 3;
+        const unsigned long long k = ((unsigned long long)tp_ld(w, tag, err) << 32) | tp_ld(w + 1, tag, err);
+        if (k > best) best = k;
+        if (tp_ld(w + 2, tag, err) != 0u) bad = true;
+    }
+    next[b] = (bad || best == 0ull) ? -1 : (int)(0xFFFFFFFFu - (uint32_t)best);
+}
+
+// The next step's tags start after this step's `count` exchanges.
+__global__ void tp_advance_kernel(int *tag0, int count)
+{
+    tag0[0] += count;
+}
+
 // g = silu(g) * u, the reference's rounding steps (src/gguf_forward.c).
 __global__ void swiglu_kernel(float *g, const float *u, int count)
 {
@@ -635,8 +787,14 @@ struct PkbCtx {
     float *part;                                              // split-K partial sums of mv_tile_kernel
     int *io_d, *io_h;  // [tokens 64][pos 64][seq 64][next 64][error word]
     PkMmScratch mm;
-    cudaGraph_t graph[bt::BMAX + 1];
-    cudaGraphExec_t exec[bt::BMAX + 1];
+    cudaGraph_t graph[2][bt::BMAX + 1];  // per batch size; [1]: with the logits gathered (tensor parallel)
+    cudaGraphExec_t exec[2][bt::BMAX + 1];
+    // tensor parallel (world > 1): the exchanges of the step, the device
+    // counter their tags start from, and the assembled logits
+    int world;
+    bt::TpX tpx;
+    int *tag0;
+    float *logits_full;
     int gqa_smem;  // dynamic shared memory of attention_gqa_kernel (0: per-head attention instead)
     int kv_alias;  // kc / vc belong to the decode step (pkb_create_prefill): not freed here
     cudaStream_t side;             // tile-kernel matrices that run beside a tensor-core launch
@@ -789,7 +947,16 @@ static void attend(PkbCtx *b, int l, int n, size_t att_smem, KV *kc, KV *vc)
 }
 
 // The launches of one step for n sequences (inputs already in io_d).
-static int enqueue_step(PkbCtx *b, int n)
+// This rank's part of an all-reduce (sum) of len floats at y, in place.
+static void tp_allreduce(PkbCtx *b, float *y, int len, int &idx)
+{
+    const int grid = (len + 255) / 256 < 2 * b->sms ? (len + 255) / 256 : 2 * b->sms;
+    bt::tp_push_kernel<<<grid, 256, 0, b->st>>>(b->tpx, y, len, b->tag0, idx);
+    bt::tp_sum_kernel<<<grid, 256, 0, b->st>>>(b->tpx, y, len, b->tag0, idx, b->mm.err);
+    idx++;
+}
+
+static int enqueue_step(PkbCtx *b, int n, int with_logits)
 {
     const PkdModel &m = b->m;
     const int dim = m.dim, hs = m.head_size, hid = m.hidden_dim;
@@ -799,6 +966,7 @@ static int enqueue_step(PkbCtx *b, int n)
     bt::embed_kernel<<<n, 256, 0, st>>>(b->arena + m.embd.offset, m.embd.row_bytes, (int)m.embd.type, b->io_d, dim,
                                         b->x);
     const size_t att_smem = (((size_t)m.seq_len + 3) / 4 * 4 + hs + 128 * 4) * 4;
+    int tix = 0;  // this step's tensor-parallel exchanges so far
     for (int l = 0; l < L; l++) {
         if (l == 0)  // later layers: the residual add and this norm at the end of the previous layer
             bt::rmsnorm_kernel<<<n, 1024, 0, st>>>(b->x, nullptr, b->norms, dim, m.rms_eps, b->xn);
@@ -811,6 +979,7 @@ static int enqueue_step(PkbCtx *b, int n)
             attend(b, l, n, att_smem, static_cast<float *>(b->kc), static_cast<float *>(b->vc));
         }
         if (!bmatmul(b, m.wo[l], b->att, n, b->tmp)) return 0;
+        if (b->world > 1) tp_allreduce(b, b->tmp, n * dim, tix);  // the heads' partial sums
         bt::rmsnorm_kernel<<<n, 1024, 0, st>>>(b->x, b->tmp, b->norms + (size_t)(2 * l + 1) * dim, dim, m.rms_eps,
                                                b->xn);
         const PkdTensor *gu[2] = {&m.gate[l], &m.up[l]};
@@ -818,12 +987,30 @@ static int enqueue_step(PkbCtx *b, int n)
         if (!bmatmul_group(b, gu, gu_y, 2, b->xn, n)) return 0;
         bt::swiglu_kernel<<<ew, 256, 0, st>>>(b->g, b->u, n * hid);
         if (!bmatmul(b, m.down[l], b->g, n, b->tmp)) return 0;
+        if (b->world > 1) tp_allreduce(b, b->tmp, n * dim, tix);  // the hidden slices' partial sums
         // x += down, then the next layer's attention norm (the output norm after the last)
         bt::rmsnorm_kernel<<<n, 1024, 0, st>>>(b->x, b->tmp, b->norms + (size_t)(2 * (l + 1)) * dim, dim,
                                                m.rms_eps, b->xn);
     }
     if (!bmatmul(b, m.output, b->xn, n, b->logits)) return 0;
-    bt::argmax_kernel<<<n, 1024, 0, st>>>(b->logits, m.vocab_size, b->io_d + 3 * B);
+    if (b->world > 1) {
+        // the vocabulary rows of this rank: local keys, the best over ranks
+        const int voc = (int)m.output.rows, voc0 = m.tp.voc0;
+        bt::tp_argmax_push_kernel<<<n, 1024, 0, st>>>(b->tpx, b->logits, voc, voc0, b->tag0, tix);
+        bt::tp_argmax_kernel<<<1, 64, 0, st>>>(b->tpx, n, b->io_d + 3 * B, b->tag0, tix, b->mm.err);
+        tix++;
+        if (with_logits) {
+            const int len = n * voc, grid = (len + 255) / 256 < 2 * b->sms ? (len + 255) / 256 : 2 * b->sms;
+            bt::tp_push_kernel<<<grid, 256, 0, st>>>(b->tpx, b->logits, len, b->tag0, tix);
+            const int all = n * m.vocab_size;
+            bt::tp_gather_kernel<<<(all + 255) / 256 < 4 * b->sms ? (all + 255) / 256 : 4 * b->sms, 256, 0, st>>>(
+                b->tpx, b->logits_full, n, m.vocab_size, b->tag0, tix, b->mm.err);
+            tix++;
+        }
+        bt::tp_advance_kernel<<<1, 1, 0, st>>>(b->tag0, tix);
+    } else {
+        bt::argmax_kernel<<<n, 1024, 0, st>>>(b->logits, m.vocab_size, b->io_d + 3 * B);
+    }
     // the greedy tokens and the matmul error word come back with the step
     cudaMemcpyAsync(b->io_d + 4 * B, b->mm.err, sizeof(int), cudaMemcpyDeviceToDevice, st);
     cudaMemcpyAsync(b->io_h + 3 * B, b->io_d + 3 * B, (B + 1) * sizeof(int), cudaMemcpyDeviceToHost, st);
@@ -846,7 +1033,11 @@ static PkbCtx *pkb_create_ex(PkdCtx *ctx, int max_seqs, int alias, char *err, si
 {
     PkdView v;
     if (!pkd_view(ctx, &v)) {
-        if (err && cap) snprintf(err, cap, "Batched decode needs a built single-GPU model.");
+        if (err && cap) snprintf(err, cap, "Batched decode needs a built model (tensor parallel: after the connect).");
+        return NULL;
+    }
+    if (alias && v.world > 1) {
+        if (err && cap) snprintf(err, cap, "Prefill runs on one GPU (not on a tensor-parallel rank).");
         return NULL;
     }
     if (max_seqs < 1 || max_seqs > bt::BMAX) {
@@ -878,6 +1069,19 @@ static PkbCtx *pkb_create_ex(PkdCtx *ctx, int max_seqs, int alias, char *err, si
     b->norms = v.norms;
     b->rope_cs = v.rope_cs;
     b->max_seqs = max_seqs;
+    b->world = v.world;
+    if (v.world > 1) {
+        b->tpx.rank = v.rank;
+        b->tpx.world = v.world;
+        b->tpx.len = v.bx_len;
+        for (int q = 0; q < v.world; q++) b->tpx.peer[q] = v.peers[q] + v.bx;
+        if (bfail(b, cudaMalloc(&b->tag0, 16), "cudaMalloc") || bfail(b, cudaMemset(b->tag0, 0, 16), "cudaMemset") ||
+            bfail(b, cudaMalloc(&b->logits_full, (size_t)bt::BMAX * m.vocab_size * 4), "cudaMalloc")) {
+            if (err && cap) snprintf(err, cap, "%s", b->msg);
+            pkb_destroy(b);
+            return NULL;
+        }
+    }
     cudaSetDevice(b->device);
     cudaDeviceGetAttribute(&b->sms, cudaDevAttrMultiProcessorCount, b->device);
     const int B = bt::BMAX, dim = m.dim, hs = m.head_size, qd = m.n_heads * hs, kvd = m.n_kv_heads * hs;
@@ -998,32 +1202,38 @@ extern "C" int pkb_step(PkbCtx *b, const int *tokens, const int *pos, const int 
     memcpy(b->io_h, tokens, (size_t)n * 4);
     memcpy(b->io_h + B, pos, (size_t)n * 4);
     memcpy(b->io_h + 2 * B, seq_ids, (size_t)n * 4);
-    if (b->exec[n] == NULL) {
+    // a tensor-parallel rank assembles the full logits only when asked
+    // (every rank of the group must ask alike: the exchanges are collective)
+    const int wl = b->world > 1 && logits != NULL ? 1 : 0;
+    if (b->exec[wl][n] == NULL) {
         // capture the step for this batch size: input copy, kernels, outputs
         cudaGetLastError();
         if (bfail(b, cudaStreamBeginCapture(b->st, cudaStreamCaptureModeThreadLocal), "capture")) return 0;
         cudaMemcpyAsync(b->io_d, b->io_h, (size_t)(3 * B) * 4, cudaMemcpyHostToDevice, b->st);
-        const int ok = enqueue_step(b, n);
+        const int ok = enqueue_step(b, n, wl);
         cudaGraph_t g = NULL;
         const cudaError_t e = cudaStreamEndCapture(b->st, &g);
-        if (!ok || bfail(b, e, "capture") || bfail(b, cudaGraphInstantiate(&b->exec[n], g, 0), "graph instantiate")) {
+        if (!ok || bfail(b, e, "capture") ||
+            bfail(b, cudaGraphInstantiate(&b->exec[wl][n], g, 0), "graph instantiate")) {
             if (!b->msg[0]) snprintf(b->msg, sizeof(b->msg), "Could not build the batched step.");
             if (g) cudaGraphDestroy(g);
-            b->exec[n] = NULL;
+            b->exec[wl][n] = NULL;
             return 0;
         }
-        b->graph[n] = g;
+        b->graph[wl][n] = g;
     }
-    if (bfail(b, cudaGraphLaunch(b->exec[n], b->st), "graph launch") ||
+    if (bfail(b, cudaGraphLaunch(b->exec[wl][n], b->st), "graph launch") ||
         bfail(b, cudaStreamSynchronize(b->st), "batched step"))
         return 0;
     if (b->io_h[4 * B] != 0) {
-        snprintf(b->msg, sizeof(b->msg), "A tensor-core matmul wait ran out of time (error word %d).", b->io_h[4 * B]);
+        snprintf(b->msg, sizeof(b->msg), "A device wait of the batched step ran out of time (error word %d).",
+                 b->io_h[4 * B]);
         return 0;
     }
     memcpy(next, b->io_h + 3 * B, (size_t)n * 4);
     if (logits != NULL &&
-        bfail(b, cudaMemcpy(logits, b->logits, (size_t)n * b->m.vocab_size * 4, cudaMemcpyDeviceToHost),
+        bfail(b, cudaMemcpy(logits, wl ? b->logits_full : b->logits, (size_t)n * b->m.vocab_size * 4,
+                            cudaMemcpyDeviceToHost),
               "logits copy"))
         return 0;
     return 1;
@@ -1038,12 +1248,14 @@ extern "C" void pkb_destroy(PkbCtx *b)
 {
     if (b == NULL) return;
     cudaSetDevice(b->device);
-    for (int i = 0; i <= bt::BMAX; i++) {
-        if (b->exec[i]) cudaGraphExecDestroy(b->exec[i]);
-        if (b->graph[i]) cudaGraphDestroy(b->graph[i]);
+    for (int w = 0; w < 2; w++) {
+        for (int i = 0; i <= bt::BMAX; i++) {
+            if (b->exec[w][i]) cudaGraphExecDestroy(b->exec[w][i]);
+            if (b->graph[w][i]) cudaGraphDestroy(b->graph[w][i]);
+        }
     }
     void *dev[] = {b->kv_alias ? nullptr : b->kc, b->kv_alias ? nullptr : b->vc, b->x, b->xn, b->tmp, b->q, b->att,
-                   b->k, b->v, b->g, b->u, b->logits, b->part, b->io_d,
+                   b->k, b->v, b->g, b->u, b->logits, b->part, b->io_d, b->tag0, b->logits_full,
                    b->mm.xs, b->mm.x2s, b->mm.xinv, b->mm.ypart, b->mm.arrived, b->mm.err};
     for (void *p : dev)
         if (p) cudaFree(p);

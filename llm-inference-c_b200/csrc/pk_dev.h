@@ -121,9 +121,16 @@ typedef struct {
     const float *rope_cs;
     const PkdModel *model;
     void *kc, *vc;  /* the decode step's KV cache ([layer][position][kv_dim]) */
+    /* tensor parallel (world > 1, after pkd_tp_connect): every rank's
+     * exchange buffer (64-bit tagged words, mapped here), where the batched
+     * step's exchange region starts in it (bx, in words) and how many words
+     * one rank's part of a slot holds (bx_len); [2 slots][world][bx_len] */
+    int rank, world;
+    uint64_t *peers[PKD_TP_MAX];
+    uint64_t bx, bx_len;
 } PkdView;
 
-/* 0 for a tensor-parallel rank or an unbuilt context. */
+/* 0 for an unbuilt context or a tensor-parallel rank before pkd_tp_connect. */
 int pkd_view(PkdCtx *ctx, PkdView *out);
 
 /* Batched decode: one step for up to 64 independent sequences that share

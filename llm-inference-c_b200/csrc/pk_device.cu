@@ -1012,7 +1012,7 @@ static void seg_of(MvSeg &s, const PkdCtx *c, const PkdTensor &t, int kind)
 // it at the same offsets).
 struct LLPlan {
     size_t q, k, v, att, rwo, xmid, hb, rdn, xout, per_layer;
-    size_t keys, logits, total;
+    size_t keys, logits, bx, bx_len, total;
 };
 
 static LLPlan ll_plan(const PkdModel *m)
@@ -1035,7 +1035,12 @@ static LLPlan ll_plan(const PkdModel *m)
     p.per_layer = p.xout + r32(dim);
     p.keys = p.per_layer * (size_t)m->n_layers;
     p.logits = p.keys + r32(4 * (size_t)t.world);
-    p.total = p.logits + r32(((size_t)m->vocab_size + 1) / 2);
+    p.bx = p.logits + r32(((size_t)m->vocab_size + 1) / 2);
+    // the batched step's exchanges (tensor parallel): per slot and rank up
+    // to 64 rows of the residual stream or of the rank's vocabulary slice
+    const size_t voc_max = ((size_t)m->vocab_size + (size_t)t.world - 1) / (size_t)t.world;
+    p.bx_len = t.world > 1 ? r32(64 * (dim > voc_max ? dim : voc_max)) : 0;
+    p.total = p.bx + 2 * (size_t)t.world * p.bx_len;
     return p;
 }
 
@@ -1671,7 +1676,19 @@ extern "C" const char *pkd_error(const PkdCtx *c)
 
 extern "C" int pkd_view(PkdCtx *c, PkdView *out)
 {
-    if (c == NULL || out == NULL || c->tensors == NULL || c->tp.world > 1 || c->norms == NULL) return 0;
+    if (c == NULL || out == NULL || c->tensors == NULL || c->norms == NULL) return 0;
+    memset(out, 0, sizeof(*out));
+    out->rank = c->tp.world > 1 ? c->tp.rank : 0;
+    out->world = c->tp.world > 1 ? c->tp.world : 1;
+    if (out->world > 1) {
+        for (int q = 0; q < out->world; q++) {
+            if (c->peers[q] == NULL) return 0;  // not connected yet
+            out->peers[q] = c->peers[q];
+        }
+        const LLPlan lp = ll_plan(&c->model);
+        out->bx = lp.bx;
+        out->bx_len = lp.bx_len;
+    }
     out->device = c->device;
     out->stream = (void *)c->stream;
     out->arena = c->arena;
