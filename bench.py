@@ -528,15 +528,22 @@ def run_cfg4(args):
             "peak_source": f"{peak_kind} MEASURED_PEAKS.json"}
 
 
-def run_cfg3(args):
+def run_cfg3(args, world=1, rank=0, local=0, barrier=lambda: None, allmax=lambda v: v):
     """Llama-2-7B shape, Q4_K_M mix, 16 independent sequences after a
     1024-position context (written with seeded keys and values through
-    engine_kv_write), 32 greedy steps of engine_forward_batch, one GPU."""
+    engine_kv_write), 32 greedy steps of engine_forward_batch; at N > 1 the
+    N ranks run the batched step tensor-parallel (every rank the same
+    calls), timed on each rank's host around its synchronous steps, the
+    slowest rank's time."""
     import pk_b200
     wl = WORKLOADS["llama2-7b"]
-    path = ensure_model(wl["preset"], 0, lambda: None)
+    path = ensure_model(wl["preset"], rank, barrier)
     B, C, K = 16, 1024, 32
-    e = pk_b200.Engine(path, C + K + 16, device=0)
+    if world > 1:
+        e = pk_b200.Engine(path, C + K + 16, device=local, rank=rank, world=world)
+        e.tp_connect(pk_b200.tp_exchange(e.tp_handle(), world))
+    else:
+        e = pk_b200.Engine(path, C + K + 16, device=local)
     e.batch_open(B)
     cfg = e.config
     kvd = cfg["dim"] // cfg["n_heads"] * cfg["n_kv_heads"]
@@ -549,22 +556,32 @@ def run_cfg3(args):
     seq = np.arange(B, dtype=np.int32)
     for i in range(args.warmup):
         toks, _ = e.forward_batch(toks, np.full(B, C + i), seq)
+    barrier()
     t0 = time.perf_counter()
     for i in range(K):
         toks, _ = e.forward_batch(toks, np.full(B, C + args.warmup + i), seq)
     dt = time.perf_counter() - t0
+    barrier()
     e.close()
+    dt = allmax([dt])[0]
+    if rank != 0:
+        return None
     hbm, peak_kind = peaks()
+    hbm_all = hbm * world
     wbytes = pk_synth.weight_bytes_per_token(wl["preset"])
     kvb = kv_bytes_per_step(cfg, list(range(C + args.warmup, C + args.warmup + K)), kv_entry_bytes()) * B
     step = dt / K
-    return {"workload": "Llama-2-7B-arch Q4_K_M, 16 sequences after a 1024-position context", "n_gpus": 1,
+    return {"workload": "Llama-2-7B-arch Q4_K_M, 16 sequences after a 1024-position context", "n_gpus": world,
             "steps": K, "value": B * K / dt, "unit": "tok/s", "ms_per_step": step * 1e3,
+            "parallelism": f"tensor parallel over {world} GPUs" if world > 1 else "1 GPU",
             "path": "engine_forward_batch (tcgen05 matmuls), one graph per step, host time around synchronous "
-                    "steps; tensor parallelism is not built for the batched step",
-            "roofline": {"bound": "hbm", "achieved": (wbytes + kvb) / step / 1e9, "peak": hbm,
-                         "frac": (wbytes + kvb) / step / 1e9 / hbm, "weight_bytes_per_step": wbytes,
-                         "kv_bytes_per_step": kvb, "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs"}}
+                    "steps" + ("; the ranks all-reduce the Wo and ffn_down partial sums over NVLink" if world > 1
+                               else ""),
+            "roofline": {"bound": "hbm", "achieved": (wbytes + kvb) / step / 1e9, "peak": hbm_all,
+                         "frac": (wbytes + kvb) / step / 1e9 / hbm_all, "weight_bytes_per_step": wbytes,
+                         "kv_bytes_per_step": kvb,
+                         "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs" +
+                                        (f" x {world} GPUs" if world > 1 else "")}}
 
 
 def run_matmul_sweep(args):
@@ -892,10 +909,10 @@ def main():
         matvec = run_matvec_object(args)
         note("matvec sweep done")
     cfg3 = cfg4 = None
+    if not args.no_configs and args.workload == "tinyllama" and args.configs in ("both", "llama2_7b_b16"):
+        cfg3 = run_cfg3(args, world, rank, local, barrier, allmax)  # all ranks: tensor parallel at N > 1
+        note("7B B=16 done")
     if rank == 0 and world == 1 and not args.no_configs and args.workload == "tinyllama":
-        if args.configs in ("both", "llama2_7b_b16"):
-            cfg3 = run_cfg3(args)
-            note("7B B=16 done")
         if args.configs in ("both", "llama3_8b"):
             cfg4 = run_cfg4(args)
     tp7b = None
