@@ -699,36 +699,62 @@ def run_b64(path, args, cfg, device=0, barrier=lambda: None):
 
 def run_step_trace(args, positions=130):
     """Per-phase critical path of one B=1 decode step on the TinyLlama
-    shape, from the step trace (POCKET_CUDA_TRACE=1: every CTA's
-    %globaltimer stamps after staging its input and after its work, per
-    phase). Decodes `positions` greedy steps, then reports per phase kind,
-    averaged over layers 1..20: the phase's length on the critical path
-    (last CTA end minus the previous phase's last CTA end), the median time
-    from that previous end until a CTA has staged its input, and the median
-    and maximum work time of the CTAs with work. A diagnostic, not a bench
-    line: the tracing itself adds a barrier per phase."""
+    shape (under torchrun with N > 1: the Llama-2-7B shape tensor-parallel
+    over the N GPUs, rank 0's trace), from the step trace
+    (POCKET_CUDA_TRACE=1: every CTA's %globaltimer stamps after staging its
+    input and after its work, per phase). Decodes `positions` greedy steps,
+    then reports per phase kind, averaged over the inner layers: the phase's
+    length on the critical path (last CTA end minus the previous phase's
+    last CTA end), the median time from that previous end until a CTA has
+    staged its input, and the median and maximum work time of the CTAs with
+    work. A diagnostic, not a bench line: the tracing itself adds a barrier
+    per phase."""
     os.environ["POCKET_CUDA_TRACE"] = "1"
     import pk_b200
-    path = ensure_model(WORKLOADS["tinyllama"]["preset"], 0, lambda: None)
-    e = pk_b200.Engine(path, positions + 8, device=0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+        path = ensure_model(WORKLOADS["llama2-7b"]["preset"], rank, dist.barrier)
+        e = pk_b200.Engine(path, positions + 8, device=local, rank=rank, world=world)
+        e.tp_connect(pk_b200.tp_exchange(e.tp_handle(), world))
+    else:
+        path = ensure_model(WORKLOADS["tinyllama"]["preset"], 0, lambda: None)
+        e = pk_b200.Engine(path, positions + 8, device=0)
     tok = 1
     for pos in range(positions):
         tok = int(np.argmax(e.forward(tok, pos)))
     a = e.trace(all_ctas=True)  # [cta][phase][after staging, after work], us from CTA 0's start
     e.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+        if rank != 0:
+            return 0
     stg, end = a[:, :, 0], a[:, :, 1]
-    kinds = ["qkv", "attention", "wo", "gate_up", "down"]
+    kinds = (["qkv", "attention", "wo", "wo_allreduce", "gate_up", "down", "down_allreduce"] if world > 1
+             else ["qkv", "attention", "wo", "gate_up", "down"])
+    per = len(kinds)
     out = {k: [] for k in kinds}
-    nl = (a.shape[1] - 1) // 5
+    nl = (a.shape[1] - 1) // per
     for layer in range(1, nl - 1):
         for i, k in enumerate(kinds):
-            ph = 5 * layer + i
+            ph = per * layer + i
             prev = end[:, ph - 1].max()
             work = end[:, ph] - stg[:, ph]
             busy = work > 0.3
+            if not busy.any():
+                busy = work >= work.max()
             out[k].append((end[:, ph].max() - prev, np.median(stg[busy, ph] - prev), np.median(work[busy]),
                            work.max()))
-    res = {"metric": "decode step trace (B=1)", "unit": "us", "position": positions,
+    res = {"metric": "decode step trace (B=1)", "unit": "us", "position": positions, "n_gpus": world,
+           "workload": "Llama-2-7B-arch Q4_K_M, tensor parallel" if world > 1 else "TinyLlama-1.1B-arch Q4_K_M",
            "step_us": float(end[:, -1].max()), "phases": {}}
     for k, v in out.items():
         v = np.array(v)

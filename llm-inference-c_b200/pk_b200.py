@@ -187,6 +187,7 @@ class Engine:
             self.h = L.engine_open_device(ctypes.byref(opts), device, err, 512)
         if not self.h:
             raise RuntimeError("engine_open failed: " + err.value.decode())
+        self.world = world
         c = L.engine_config(self.h).contents
         self.config = {n: getattr(c, n) for n, _ in Config._fields_}
         self.vocab_size = c.vocab_size
@@ -273,8 +274,10 @@ class Engine:
         """Per-phase device times (us) of the last step, or None when tracing
         is off. CTA 0's rows (stage x, work, 0); with all_ctas, an array
         [cta][phase][2] of (after staging, after work) in us from CTA 0's
-        start instead."""
-        nph = 5 * self.config["n_layers"] + 1
+        start instead. A tensor-parallel step has seven phases per layer
+        (QKV, attention, Wo, its all-reduce, gate/up, down, its all-reduce),
+        one GPU five."""
+        nph = (7 if self.world > 1 else 5) * self.config["n_layers"] + 1
         out = np.zeros(3 * nph + 1 + 2 * 1024 * nph, dtype=np.uint64)
         n = lib().engine_trace(self.h, out.ctypes.data, out.size)
         if n <= 1:
