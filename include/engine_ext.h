@@ -149,8 +149,10 @@ int engine_forward_batch(LLMModel *model, const int *tokens, const int *pos, con
  * last_logits (optional) receives the logits of position pos0 + n - 1.
  * Returns that position's greedy token (lowest index on ties), -1 when a
  * logit is not finite, -2 on invalid arguments or a device error (message
- * in error). Single GPU; the first call allocates the batched step's
- * working buffers (make it before any stream capture). */
+ * in error). On a tensor-parallel group every rank makes the same call
+ * (the chunks run through the tensor-parallel batched step). The first
+ * call allocates the batched step's working buffers (make it before any
+ * stream capture). */
 int engine_prefill(LLMModel *model, const int *tokens, int n, int pos0, float *last_logits, char *error,
                    size_t error_capacity);
 

@@ -1035,10 +1035,6 @@ int engine_prefill(LLMModel *m, const int *tokens, int n, int pos0, float *last_
         seterr(err, cap, "Invalid arguments.");
         return -2;
     }
-    if (m->tp_world > 1) {
-        seterr(err, cap, "Prefill runs on one GPU (not on a tensor-parallel rank).");
-        return -2;
-    }
     for (int i = 0; i < n; i++) {
         if (tokens[i] < 0 || tokens[i] >= m->config.vocab_size) {
             seterr(err, cap, "Token outside the vocabulary.");

@@ -1036,10 +1036,6 @@ static PkbCtx *pkb_create_ex(PkdCtx *ctx, int max_seqs, int alias, char *err, si
         if (err && cap) snprintf(err, cap, "Batched decode needs a built model (tensor parallel: after the connect).");
         return NULL;
     }
-    if (alias && v.world > 1) {
-        if (err && cap) snprintf(err, cap, "Prefill runs on one GPU (not on a tensor-parallel rank).");
-        return NULL;
-    }
     if (max_seqs < 1 || max_seqs > bt::BMAX) {
         if (err && cap) snprintf(err, cap, "Batched decode takes 1 to %d sequences.", bt::BMAX);
         return NULL;

@@ -176,3 +176,64 @@ def test_tensor_parallel_batched_decode_matches_oracle(orc, synth_model, tmp_pat
             if not np.isnan(got["logits"][i][0]):
                 err = float(np.max(np.abs(got["logits"][i] - w)))
                 assert err <= LOGIT_TOL, (r, i, err)
+
+
+def _prefill_rank(rank, world, port, path, out_dir):
+    import datetime
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world, init_method=f"tcp://127.0.0.1:{port}",
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        e = pk_b200.Engine(path, 128, device=rank, rank=rank, world=world)
+        e.tp_connect(pk_b200.tp_exchange(e.tp_handle(), world))
+        prompt = [(37 * i + 11) % e.vocab_size for i in range(70)]  # two chunks: 64 + 6
+        tok, last = e.prefill(prompt, 0, logits=True)
+        after = []
+        for i in range(4):
+            lg = e.forward(tok, len(prompt) + i)
+            assert lg is not None, e.last_error()
+            after.append(np.asarray(lg).copy())
+            tok = int(np.argmax(lg))
+        np.savez(os.path.join(out_dir, f"prank{rank}.npz"), prompt=np.asarray(prompt), final=tok, last=last,
+                 after=np.stack(after))
+        e.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tensor_parallel_prefill_matches_oracle(orc, synth_model, tmp_path, world):
+    """engine_prefill on a tensor-parallel group (70 tokens: a 64-row chunk
+    and a 6-row chunk through the tensor-parallel batched step into the
+    decode step's cache), then engine_forward continuing after it: the last
+    prompt position's logits and four decode steps against the oracle."""
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    path = synth_model("tp8-q4km" if world == 8 else "tp-q4km")
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_prefill_rank, args=(r, world, port, path, str(tmp_path))) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    got0 = np.load(os.path.join(str(tmp_path), "prank0.npz"))
+    prompt = [int(t) for t in got0["prompt"]]
+    m = orc.open(path, 128)
+    lg = None
+    for pos, t in enumerate(prompt):
+        lg = np.asarray(m.forward(t, pos)).copy()
+    want_last, tok, want_after = lg, int(np.argmax(lg)), []
+    for i in range(4):
+        lg = np.asarray(m.forward(tok, len(prompt) + i)).copy()
+        want_after.append(lg)
+        tok = int(np.argmax(lg))
+    m.close()
+    for r in range(world):
+        got = np.load(os.path.join(str(tmp_path), f"prank{r}.npz"))
+        assert float(np.max(np.abs(got["last"] - want_last))) <= LOGIT_TOL, r
+        assert float(np.max(np.abs(got["after"] - np.stack(want_after)))) <= LOGIT_TOL, r
+        assert int(got["final"]) == tok, r
