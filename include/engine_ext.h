@@ -105,10 +105,11 @@ int engine_launches_per_step(const LLMModel *model);
 
 /* ---- Batched decode (additive; the reference decodes one sequence) --
  * Up to ENGINE_BATCH_MAX independent sequences decode together, sharing
- * one pass over the weights per step: Q4_K matrices on the tensor cores,
- * the other formats on CUDA cores. Each sequence has its own KV cache of
- * the model's context length, separate from the one engine_forward uses.
- * Single GPU only (refused on a tensor-parallel rank). */
+ * one pass over the weights per step: Q4_K, Q5_K and Q6_K matrices on the
+ * tensor cores, the other formats on CUDA cores. Each sequence has its own
+ * KV cache of the model's context length, separate from the one
+ * engine_forward uses. Runs on one GPU or on a tensor-parallel group (all
+ * ranks making the same calls). */
 #define ENGINE_BATCH_MAX 64
 
 /* Allocate the batched state for max_seqs sequences (1..64), dropping any
