@@ -6,7 +6,10 @@ One spawned process per GPU; the ranks exchange their 64-byte handles over
 gloo on the host, then decode the same token sequence. Every rank's
 engine_forward must return the full logits within 1e-3 max-abs of the
 oracle, and the greedy tokens (device argmax across the ranks) must be the
-oracle's. Skipped when the machine has fewer GPUs than ranks.
+oracle's. The same holds for the batched step on the group
+(engine_forward_batch: a prompt chunk, single rows, a late-joining
+sequence, with and without logits) and for engine_prefill followed by
+engine_forward. Skipped when the machine has fewer GPUs than ranks.
 """
 import multiprocessing as mp
 import os
